@@ -1,0 +1,318 @@
+"""Benchmark of the Fry int8 forward on B200: positions/s of the 28-block network at batch 256 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
+
+A step is one forward of 256 synthetic positions (seeded legal-looking boards, independent seeds per GPU) through the
+full 28-block int8 network with random-init weights (no checkpoint ships here), replayed as a CUDA graph. Each GPU runs
+its own replica (no collective on the data path; NCCL only for the barrier and the max of the timings). L2 is flushed
+between timed steps by writing a 256 MiB buffer outside the timed events. Rank 0 prints one JSON line.
+
+--impl reference times the reference's own CPU implementation of the path, the fp32 ChessTransformer forward run through
+cpu_batches (engine/inference.py:274-278), as restated by the CPU oracle (oracle/model.py), on all host cores, one bounded
+sample of boards a step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH = 256
+LATENCY_BATCH = 64
+FLUSH_BYTES = 256 << 20
+PROFILE_SUMMARY = ROOT / "profiles" / "int8_gemm_traffic.json"
+
+
+def arguments():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-sweep", action="store_true", help="skip the batch sweep and the latency run")
+    return parser.parse_args()
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        measured = json.loads(path.read_text())
+        return {"hbm_gbs": measured["hbm_gbs"], "bf16_tflops": measured["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.process = None
+
+    def __enter__(self):
+        try:
+            self.process = subprocess.Popen(["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                             "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.process = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.process is not None:
+            self.process.terminate()
+            self.process.wait(timeout=10)
+
+    def summary(self) -> dict:
+        self.file.flush()
+        self.file.seek(0)
+        rows = [line.split(",") for line in self.file.read().splitlines() if line.strip()]
+        Path(self.file.name).unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, value in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def reference_arm(args, rank: int) -> None:
+    """The reference's CPU path on the host cores: fp32 forward of a bounded sample of boards a step."""
+    if rank != 0:
+        return
+    import torch
+    from oracle.model import fp32_forward
+    from chess_transformer_b200.boards import random_boards
+    from chess_transformer_b200.network import FRY_SETTINGS, synthetic_state_dict
+    torch.set_num_threads(os.cpu_count() or 1)
+    state = synthetic_state_dict(FRY_SETTINGS, 0)
+    sample = 16
+    boards = torch.from_numpy(random_boards(sample, 0)).long()
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            fp32_forward(state, FRY_SETTINGS, boards)
+        start = time.perf_counter()
+        for _ in range(args.steps):
+            fp32_forward(state, FRY_SETTINGS, boards)
+        elapsed = time.perf_counter() - start
+    value = sample * args.steps / elapsed
+    cores = torch.get_num_threads()
+    line = {"metric": "positions/sec (28L int8 fwd, batch 256)", "value": value, "unit": "positions/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "fry-28L-forward-b256", "sample": f"{sample} boards a step (bounded CPU sample of the batch of 256)",
+                       "seq_len": 70, "parallelism": "host cores"},
+            "cpu_baseline": {"value": value, "unit": "positions/s", "cores": cores, "kind": "port",
+                             "sample": f"{sample} boards x {args.steps} steps, fp32 ChessTransformer forward (oracle/model.py) "
+                                       f"on {cores} threads, {os.cpu_count()} host cores"},
+            "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline() -> dict:
+    """The oracle port of the reference's CPU path on this host's cores, a ~10-20 s sample."""
+    import torch
+    from oracle.model import fp32_forward
+    from chess_transformer_b200.boards import random_boards
+    from chess_transformer_b200.network import FRY_SETTINGS, synthetic_state_dict
+    threads = torch.get_num_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    state = synthetic_state_dict(FRY_SETTINGS, 0)
+    sample = 8
+    boards = torch.from_numpy(random_boards(sample, 1)).long()
+    with torch.no_grad():
+        fp32_forward(state, FRY_SETTINGS, boards)
+        start, repeats = time.perf_counter(), 0
+        while time.perf_counter() - start < 10 or repeats < 2:
+            fp32_forward(state, FRY_SETTINGS, boards)
+            repeats += 1
+        elapsed = time.perf_counter() - start
+    cores = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    return {"value": sample * repeats / elapsed, "unit": "positions/s", "cores": cores, "kind": "port",
+            "sample": f"{sample} boards x {repeats} forwards, fp32 ChessTransformer forward (oracle/model.py, the reference's "
+                      f"cpu_batches path) on {cores} threads of {os.cpu_count()} host cores"}
+
+
+def gemm_roofline(torch, stream) -> dict:
+    """The dominant kernel, the int8 tensor-core GEMM, timed alone at the step's shapes (M = 256 x 70 tokens) with CUDA
+    events on its stream: algorithmic int8 ops per launch / mean launch time, against the int8 dense peak."""
+    from chess_transformer_b200 import ops
+    M = BATCH * 70
+    # per forward: projection at dq 8/16/24 (10, 9, 9 of the 28 blocks), gate_up and down in every block
+    shapes = [("projection", 864, 768, False, 10), ("projection", 1152, 768, False, 9), ("projection", 1440, 768, False, 9),
+              ("gate_up", 992, 768, True, 28), ("down", 768, 1024, False, 28)]
+    generator = torch.Generator().manual_seed(0)
+    total_ops = total_seconds = 0.0
+    per_shape = {}
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    with torch.cuda.stream(stream):
+        for name, N, K, gated, count in shapes:
+            x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
+            w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
+            xs = torch.rand(M, generator=generator).cuda() / 100
+            ws = torch.rand(len(w), generator=generator).cuda() / 100
+            bias = torch.randn(N, generator=generator).half().cuda() if name == "projection" else None
+            residual = torch.randn(M, N, generator=generator).half().cuda() if name == "down" else None
+            run = lambda: ops.int8_linear(x, xs, w, ws, bias, residual, gated, name)
+            for _ in range(3):
+                run()
+            times = []
+            for _ in range(10):
+                flush.fill_(1)
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                run()
+                end.record(stream)
+                end.synchronize()
+                times.append(start.elapsed_time(end) / 1000)
+            seconds = statistics.mean(times)
+            ops_per_launch = 2.0 * M * K * N * (2 if gated else 1)
+            per_shape[f"{name}_{N}x{K}"] = round(ops_per_launch / seconds / 1e12, 1)
+            total_ops += ops_per_launch * count
+            total_seconds += seconds * count
+    return {"ops_per_forward": total_ops, "seconds_per_forward": total_seconds, "tops_by_shape": per_shape}
+
+
+def main() -> None:
+    args = arguments()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from chess_transformer_b200.boards import random_boards
+    from chess_transformer_b200.network import FRY_SETTINGS, Int8Network, quantize, synthetic_state_dict
+    from chess_transformer_b200.runtime import GraphedBatches
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    state = synthetic_state_dict(FRY_SETTINGS, 1000 + rank)
+    network = Int8Network(state, FRY_SETTINGS, quantize(state, FRY_SETTINGS), device)
+    del state
+    boards = torch.from_numpy(random_boards(BATCH, 77 + rank)).long().to(device)
+    stream = torch.cuda.Stream(device)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    # the step as a CUDA graph (the reference records its forwards the same way, engine/inference.py:117-125)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream), torch.no_grad():
+        for _ in range(2):
+            network(boards)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream), torch.no_grad():
+        rows = network(boards)
+    torch.cuda.synchronize()
+    if not torch.isfinite(rows).all():
+        raise RuntimeError("the forward gave non-finite answers")
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clocks, torch.cuda.stream(stream):
+        for start, end in events:
+            flush.fill_(1)
+            start.record(stream)
+            graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    seconds = sum(start.elapsed_time(end) for start, end in events) / 1000
+    if world > 1:
+        slowest = torch.tensor([seconds], device=device)
+        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+        seconds = slowest.item()
+
+    # end to end through the runtime: pinned host boards in, graph replay, answer rows out, every step
+    host_boards = random_boards(BATCH, 99 + rank)
+    batches = GraphedBatches(network, [LATENCY_BATCH, BATCH], in_flight=1)
+    for _ in range(max(3, args.warmup)):
+        batches.collect(batches.launch(host_boards))
+    if world > 1:
+        dist.barrier()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        batches.collect(batches.launch(host_boards))
+    e2e_seconds = time.perf_counter() - start
+    if world > 1:
+        slowest = torch.tensor([e2e_seconds], device=device)
+        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+        e2e_seconds = slowest.item()
+
+    extra = {}
+    if rank == 0 and not args.no_sweep:
+        latencies = []
+        for _ in range(60):
+            t0 = time.perf_counter()
+            batches.collect(batches.launch(host_boards[:LATENCY_BATCH]))
+            latencies.append(time.perf_counter() - t0)
+        extra["latency_p50_ms_batch64"] = round(1000 * statistics.median(latencies[10:]), 3)
+    del batches
+
+    if rank == 0:
+        gemm = gemm_roofline(torch, stream)
+        peak = peaks()
+        int8_peak = 2 * peak["bf16_tflops"]
+        achieved = gemm["ops_per_forward"] / gemm["seconds_per_forward"] / 1e12
+        traffic = None
+        if PROFILE_SUMMARY.exists():
+            traffic = json.loads(PROFILE_SUMMARY.read_text()).get("dram_bytes_per_launch")
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
+                    "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                    "kernel": "gemm_kernel<kind::i8> (projection, gate_up, down at M=17920)",
+                    "peak_source": f"int8 dense = 2 x {peak['source']} cuBLAS bf16 burst ({peak['bf16_tflops']} TFLOP/s), of {peak['source']}",
+                    "tops_by_shape": gemm["tops_by_shape"]}
+        forward_tops = 12.40e9 * BATCH / (seconds / args.steps) / 1e12
+        line = {"metric": "positions/sec (28L int8 fwd, batch 256)", "value": BATCH * args.steps * world / seconds, "unit": "positions/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * seconds / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": {"workload": "fry-28L-int8-forward-b256", "model": "fry d768, 28 int8 blocks, 24q/12kv heads, dq 8/16/24, SwiGLU 992",
+                           "global_batch": BATCH * world, "seq_len": 70, "parallelism": f"replicas x{world}",
+                           "l2": "flushed between steps (256 MiB write outside the timed events)", "weights": "random-init N(0,0.02), round-to-nearest int8"},
+                "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
+                        "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4},
+                "gpu_launches": 231 * args.steps,
+                "forward_int8_tops": round(forward_tops, 1),
+                "roofline": roofline, "clocks": clocks.summary(), **extra}
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,271 @@
+// The C ABI (include/fry_b200.h): argument checks on the host, then the kernels of gemm.cu, rows.cu, attention.cu and
+// heads.cu on the caller's stream. fry_forward runs the whole int8 network: the block sequence of `Int8Block.forward`
+// (model/int8_blocks.py:274-288) with `link_input_mixes` (model/fused_blocks.py:358-363), then the heads.
+#include <cstdio>
+#include <string>
+
+#include "../../include/fry_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& message) {
+    g_last_error = message;
+    return code;
+}
+
+int check(cudaError_t status, const std::string& what, const std::string& detail = "") {
+    if (status == cudaSuccess) {
+        g_last_error.clear();
+        return FRY_OK;
+    }
+    std::string message = what + ": " + cudaGetErrorString(status);
+    if (!detail.empty()) message += " (" + detail + ")";
+    return fail(status == cudaErrorInvalidValue && !detail.empty() ? FRY_ERROR_SHAPE : FRY_ERROR_CUDA, message);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+size_t round_up(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+int projection_rows(const FryNetwork* n, int dq) {
+    return (n->heads + n->kv_heads) * dq + n->kv_heads * n->dv + n->heads * n->templates_count;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fry_last_error(void) { return g_last_error.c_str(); }
+
+const char* fry_version(void) { return "fry_b200 0.1 sm_100a"; }
+
+int fry_device_status(int* code, int* where, int clear) {
+    int host[2] = {0, 0};
+    cudaError_t status = cudaMemcpyFromSymbol(host, fry::g_status, sizeof(host));
+    if (status == cudaSuccess && clear) {
+        const int zero[2] = {0, 0};
+        status = cudaMemcpyToSymbol(fry::g_status, zero, sizeof(zero));
+    }
+    if (code) *code = host[0];
+    if (where) *where = host[1];
+    return check(status, "fry_device_status");
+}
+
+int fry_int8_linear(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
+                    const uint16_t* residual, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                    uint16_t* out, int M, int N, int K, int gated, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear takes N a multiple of 8 and K a multiple of 16, got N " + std::to_string(N) +
+                                         ", K " + std::to_string(K));
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || (residual && !aligned16(residual)) || (original && !aligned16(original)))
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear reads and writes 16-byte vectors: x, weight, out, residual and original must be 16-byte aligned");
+    if (original && (!residual || !residual_scale || !input_scale))
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear mixes the next input only with a residual and both scales");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.x_scale = x_scale;
+    args.w_scale = weight_scale;
+    args.bias = bias;
+    args.residual = residual;
+    args.original = original;
+    args.residual_scale = residual_scale;
+    args.input_scale = input_scale;
+    args.out = out;
+    const int epilogue = gated ? fry::kEpiGated : residual == nullptr ? fry::kEpiBias : original == nullptr ? fry::kEpiResidual : fry::kEpiMix;
+    std::string detail;
+    return check(fry::gemm(0, epilogue, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_linear", detail);
+}
+
+int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int M, int N, int K, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_i32 takes N a multiple of 8 and K a multiple of 16");
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out)) return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_i32 needs 16-byte aligned tensors");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.out = out;
+    std::string detail;
+    return check(fry::gemm(0, fry::kEpiInt32, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_matmul_i32", detail);
+}
+
+int fry_norm_quant(const uint16_t* x, const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int D, void* stream) {
+    if (M < 0 || D <= 0 || D % 8 != 0 || D > 1024) return fail(FRY_ERROR_SHAPE, "fry_norm_quant takes D a multiple of 8 up to 1024");
+    if (!aligned16(x) || !aligned16(gain) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(FRY_ERROR_SHAPE, "fry_norm_quant needs aligned rows");
+    return check(fry::norm_quant(x, nullptr, nullptr, nullptr, gain, eps, nullptr, q, scale, M, D, as_stream(stream)), "fry_norm_quant");
+}
+
+int fry_mix_norm_quant(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                       const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, void* stream) {
+    if (M < 0 || D <= 0 || D % 8 != 0 || D > 1024) return fail(FRY_ERROR_SHAPE, "fry_mix_norm_quant takes D a multiple of 8 up to 1024");
+    if (!aligned16(x) || !aligned16(original) || !aligned16(mixed) || !aligned16(gain) || (reinterpret_cast<uintptr_t>(q) & 7u))
+        return fail(FRY_ERROR_SHAPE, "fry_mix_norm_quant needs aligned rows");
+    return check(fry::norm_quant(x, original, residual_scale, input_scale, gain, eps, mixed, q, scale, M, D, as_stream(stream)),
+                 "fry_mix_norm_quant");
+}
+
+int fry_rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, void* stream) {
+    if (M < 0 || hidden <= 0 || hidden % 8 != 0 || width % 32 != 0 || width > 1024 || hidden > width)
+        return fail(FRY_ERROR_SHAPE, "fry_rotate_quant takes hidden a multiple of 8 and width a multiple of 32 up to 1024, width >= hidden");
+    if (!aligned16(h) || !aligned16(q)) return fail(FRY_ERROR_SHAPE, "fry_rotate_quant needs 16-byte aligned rows");
+    return check(fry::rotate_quant(h, q, scale, M, hidden, width, as_stream(stream)), "fry_rotate_quant");
+}
+
+int fry_template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+                           uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps, void* stream) {
+    if (B < 0) return fail(FRY_ERROR_SHAPE, "fry_template_attention takes B >= 0");
+    if (!aligned16(projected) || !aligned16(out) || (reinterpret_cast<uintptr_t>(templates) & 3u))
+        return fail(FRY_ERROR_SHAPE, "fry_template_attention needs 16-byte aligned projections and outputs");
+    std::string detail;
+    return check(fry::template_attention(projected, templates, q_gain, k_gain, out, B, heads, kv_heads, dq, dv, templates_count, eps,
+                                         as_stream(stream), &detail),
+                 "fry_template_attention", detail);
+}
+
+int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, const uint16_t* residual, void* out, int M, int N, int K,
+               int out_fp32, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 8 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_linear takes N and K multiples of 8");
+    if (out_fp32 && residual) return fail(FRY_ERROR_SHAPE, "fry_linear adds no residual to an fp32 output");
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || (residual && !aligned16(residual)))
+        return fail(FRY_ERROR_SHAPE, "fry_linear needs 16-byte aligned tensors");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    if (out_fp32)
+        args.bias_f32 = static_cast<const float*>(bias);
+    else
+        args.bias = static_cast<const uint16_t*>(bias);
+    args.residual = residual;
+    args.out = out;
+    std::string detail;
+    return check(fry::gemm(1, out_fp32 ? fry::kEpiLinearF32 : fry::kEpiLinearF16, x, weight, args, M, N, K, as_stream(stream), &detail),
+                 "fry_linear", detail);
+}
+
+int fry_board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table, uint16_t* out,
+                        int B, int D, void* stream) {
+    if (B < 0 || D <= 0 || D % 8 != 0) return fail(FRY_ERROR_SHAPE, "fry_board_embedding takes D a multiple of 8");
+    if (!aligned16(embed) || !aligned16(position) || !aligned16(table) || !aligned16(out))
+        return fail(FRY_ERROR_SHAPE, "fry_board_embedding needs 16-byte aligned tables and output");
+    return check(fry::board_embedding(boards, embed, position, table, out, B, D, as_stream(stream)), "fry_board_embedding");
+}
+
+size_t fry_heads_workspace_bytes(int B, int D) { return fry::heads_workspace_bytes(B, D); }
+
+int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
+              int D, void* stream) {
+    if (!heads || B < 0) return fail(FRY_ERROR_SHAPE, "fry_heads needs its weights and B >= 0");
+    if (!aligned16(stream_x) || !aligned16(workspace) || !aligned16(heads->a_weight) || !aligned16(heads->ln_gain))
+        return fail(FRY_ERROR_SHAPE, "fry_heads needs 16-byte aligned tensors");
+    fry::HeadWeights w{heads->ln_gain,     heads->a_weight,    heads->a_bias,     heads->narrow_weight, heads->narrow_bias,
+                       heads->hidden_weight, heads->hidden_bias, heads->out_weight, heads->out_bias,      heads->bins};
+    std::string detail;
+    return check(fry::heads(stream_x, w, eps, rows, workspace, workspace_bytes, B, D, as_stream(stream), &detail), "fry_heads", detail);
+}
+
+size_t fry_forward_workspace_bytes(const FryNetwork* n, int B) {
+    if (!n || B <= 0) return 0;
+    const size_t M = static_cast<size_t>(B) * 70, D = n->d_model;
+    int widest = 0;
+    for (int i = 0; i < n->layers; ++i) {
+        const int rows = projection_rows(n, n->blocks[i].dq);
+        widest = rows > widest ? rows : widest;
+    }
+    const size_t q_width = D > static_cast<size_t>(n->down_width) ? D : static_cast<size_t>(n->down_width);
+    return round_up(M * D * 2) * 3 + round_up(M * q_width) + round_up(M * 4) + round_up(M * widest * 2) + round_up(M * n->hidden * 2) +
+           round_up(fry::heads_workspace_bytes(B, n->d_model));
+}
+
+int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!n || B < 0) return fail(FRY_ERROR_SHAPE, "fry_forward needs a network and B >= 0");
+    if (B == 0) return check(cudaSuccess, "");
+    if (workspace_bytes < fry_forward_workspace_bytes(n, B))
+        return fail(FRY_ERROR_SHAPE, "fry_forward's workspace is smaller than fry_forward_workspace_bytes");
+    if (!aligned16(workspace)) return fail(FRY_ERROR_SHAPE, "fry_forward needs a 16-byte aligned workspace");
+    const cudaStream_t s = as_stream(stream);
+    const int D = n->d_model, M = B * 70;
+    uint8_t* cursor = static_cast<uint8_t*>(workspace);
+    auto take = [&](size_t bytes) {
+        uint8_t* p = cursor;
+        cursor += round_up(bytes);
+        return p;
+    };
+    int widest = 0;
+    for (int i = 0; i < n->layers; ++i) {
+        const int r = projection_rows(n, n->blocks[i].dq);
+        widest = r > widest ? r : widest;
+    }
+    const int q_width = D > n->down_width ? D : n->down_width;
+    uint16_t* original = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    uint16_t* x = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    uint16_t* attended = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    int8_t* q = reinterpret_cast<int8_t*>(take(static_cast<size_t>(M) * q_width));
+    float* scale = reinterpret_cast<float*>(take(static_cast<size_t>(M) * 4));
+    uint16_t* projected = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * widest * 2));
+    uint16_t* hidden = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * n->hidden * 2));
+    const size_t heads_bytes = fry::heads_workspace_bytes(B, D);
+    void* heads_workspace = take(heads_bytes);
+
+    std::string detail;
+    cudaError_t status = fry::board_embedding(boards, n->embed, n->position, n->table, original, B, D, s);
+    if (status != cudaSuccess) return check(status, "fry_forward: embedding");
+    for (int i = 0; i < n->layers; ++i) {
+        const FryBlock& b = n->blocks[i];
+        const std::string where = "fry_forward: block " + std::to_string(i);
+        // ln1 (the first block mixes its own input; later ones get it mixed by the previous down)
+        status = i == 0 ? fry::norm_quant(original, original, b.residual_scale, b.input_scale, b.ln1, n->eps, x, q, scale, M, D, s)
+                        : fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln1, n->eps, nullptr, q, scale, M, D, s);
+        if (status != cudaSuccess) return check(status, where + " ln1");
+        const int rows_p = projection_rows(n, b.dq);
+        fry::GemmArgs projection;
+        projection.x_scale = scale;
+        projection.w_scale = b.projection_scale;
+        projection.bias = b.projection_bias;
+        projection.out = projected;
+        status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " projection", detail);
+        status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
+                                         n->templates_count, n->eps, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " attention", detail);
+        fry::GemmArgs combine;
+        combine.bias = b.combine_heads_bias;
+        combine.residual = x;
+        combine.out = x;
+        status = fry::gemm(1, fry::kEpiLinearF16, attended, b.combine_heads, combine, M, D, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " combine_heads", detail);
+        status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
+        if (status != cudaSuccess) return check(status, where + " ln2");
+        fry::GemmArgs gate_up;
+        gate_up.x_scale = scale;
+        gate_up.w_scale = b.gate_up_scale;
+        gate_up.out = hidden;
+        status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " gate_up", detail);
+        status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
+        if (status != cudaSuccess) return check(status, where + " rotate_quant");
+        fry::GemmArgs down;
+        down.x_scale = scale;
+        down.w_scale = b.down_scale;
+        down.residual = x;
+        down.out = x;
+        const bool mixes = i + 1 < n->layers;
+        if (mixes) {
+            down.original = original;
+            down.residual_scale = n->blocks[i + 1].residual_scale;
+            down.input_scale = n->blocks[i + 1].input_scale;
+        }
+        status = fry::gemm(0, mixes ? fry::kEpiMix : fry::kEpiResidual, q, b.down, down, M, D, n->down_width, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " down", detail);
+    }
+    const FryHeads& h = n->head_weights;
+    fry::HeadWeights w{h.ln_gain, h.a_weight, h.a_bias, h.narrow_weight, h.narrow_bias, h.hidden_weight, h.hidden_bias, h.out_weight,
+                       h.out_bias, h.bins};
+    status = fry::heads(x, w, n->eps, rows, heads_workspace, heads_bytes, B, D, s, &detail);
+    return check(status, "fry_forward: heads", detail);
+}
+
+}  // extern "C"

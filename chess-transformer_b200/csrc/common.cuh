@@ -1,0 +1,228 @@
+// Device helpers shared by the Fry kernels: mbarriers with bounded waits, TMA tile loads,
+// tcgen05 (TMEM allocation, MMA issue, commit, loads), and the library's error flag.
+// sm_100a only. No TMA load here uses cluster multicast: the same code runs on every GPU of a box.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <set>
+#include <tuple>
+
+#define FRY_DEVICE __device__ __forceinline__
+
+namespace fry {
+
+// Error codes a kernel records in the device-side status word (first failure wins).
+enum DeviceError : int {
+    kOk = 0,
+    kWaitTimeout = 1,      // a bounded mbarrier wait gave up
+    kBadToken = 2,         // a board token outside the vocabulary
+    kBadShape = 3,         // a launch got a shape its kernel does not take
+};
+
+// Set by kernels on a failure they can detect; read and cleared by fry_device_status(). The library is one
+// translation unit (fry_b200.cu includes every kernel file), so this is its only definition.
+__device__ int g_status[2];  // [code, where]
+
+FRY_DEVICE void record_error(int code, int where) {
+    if (atomicCAS(&g_status[0], 0, code) == 0) g_status[1] = where;
+}
+
+// Time bound for every wait on an mbarrier: 2 s of the global timer, far beyond any real wait (microseconds).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+FRY_DEVICE uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+FRY_DEVICE uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+FRY_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+FRY_DEVICE void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+FRY_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+FRY_DEVICE void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+FRY_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase of the given parity to complete; false (and the error flag set) if it never does.
+FRY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) break;
+    }
+    record_error(kWaitTimeout, where);
+    return false;
+}
+
+// 2-D tiled TMA load of box {x, y} (x the contiguous coordinate) into shared memory, completing on bar.
+FRY_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+FRY_DEVICE void prefetch_tensor_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+FRY_DEVICE bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// ---- tcgen05 -------------------------------------------------------------------------------------------
+
+FRY_DEVICE void tmem_alloc(uint32_t* dst_smem, uint32_t columns) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)), "r"(columns)
+                 : "memory");
+}
+FRY_DEVICE void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+FRY_DEVICE void tmem_dealloc(uint32_t addr, uint32_t columns) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(addr), "r"(columns) : "memory");
+}
+FRY_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FRY_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T for one MMA instruction; kind::i8 or kind::f16 by template.
+template <int KIND>
+FRY_DEVICE void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    if constexpr (KIND == 0) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    }
+}
+
+// Arrives on bar once every MMA this thread issued before it has completed.
+FRY_DEVICE void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape: lane i of the warp reads TMEM lane base+i).
+FRY_DEVICE void tmem_load32(uint32_t addr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(addr));
+}
+FRY_DEVICE void tmem_load16(uint32_t addr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(addr));
+}
+FRY_DEVICE void tmem_load_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand tile in the 128-byte swizzle layout TMA writes:
+// rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked along M/N. Fields: start address >> 4 [0,14),
+// leading byte offset >> 4 [16,30) (unused for swizzled K-major, set to 1), stride byte offset >> 4 [32,46)
+// (1024 bytes between 8-row groups), descriptor version 1 [46,48), swizzle mode 2 = 128B [61,64).
+FRY_DEVICE uint64_t smem_desc_sw128(uint32_t smem_byte_addr) {
+    uint64_t desc = 0;
+    desc |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFF);
+    desc |= static_cast<uint64_t>(1) << 16;
+    desc |= static_cast<uint64_t>(1024 >> 4) << 32;
+    desc |= static_cast<uint64_t>(1) << 46;
+    desc |= static_cast<uint64_t>(2) << 61;
+    return desc;
+}
+
+// Instruction descriptor for a dense MMA with both operands K-major, M = 128 rows:
+// D format [4,6) (1 f32, 2 s32), A format [7,10) and B format [10,13) (kind::i8: 1 signed; kind::f16: 0 f16),
+// N >> 3 at [17,23), M >> 4 at [24,29).
+template <int KIND>
+__host__ __device__ constexpr uint32_t instr_desc(int n) {
+    return (KIND == 0 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4)) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+// ---- small numeric helpers -----------------------------------------------------------------------------
+
+FRY_DEVICE float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+FRY_DEVICE float div_full(float a, float b) {
+    float y;
+    asm("div.full.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+    return y;
+}
+FRY_DEVICE float warp_sum(float v) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+    return v;
+}
+FRY_DEVICE float warp_max(float v) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+    return v;
+}
+FRY_DEVICE float h2f(__half h) { return __half2float(h); }
+FRY_DEVICE float h2f_bits(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
+FRY_DEVICE uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// Raises a kernel's dynamic shared memory limit once per (kernel, device, size); safe from several host threads.
+inline cudaError_t ensure_smem(const void* kernel, int bytes) {
+    static std::mutex mutex;
+    static std::set<std::tuple<const void*, int, int>> done;
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (done.count({kernel, device, bytes})) return cudaSuccess;
+    status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (status == cudaSuccess) done.insert({kernel, device, bytes});
+    return status;
+}
+
+}  // namespace fry

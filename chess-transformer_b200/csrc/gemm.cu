@@ -1,0 +1,295 @@
+// Tensor-core GEMMs for the Fry forward: out[M, N] = epilogue(A[M, K] . B[N, K]^T) with both operands K-major.
+//
+//  kind::i8  (int8 x int8 -> int32 in TMEM): the int8 linears of a block (projection, gate_up, down), replacing
+//            `int8_linear` (model/int8_blocks.py:66-139) and `small_int8` (model/int8_cuda.py:34-183) of the reference.
+//  kind::f16 (fp16 x fp16 -> fp32 in TMEM): `linear` (model/fused_blocks.py:229-318): attention-out (combine_heads,
+//            + bias + residual, fp16 out) and the policy head's `a` matmul (+ bias, fp32 out).
+//
+// One CTA computes one 128 x BN output tile. Warp 4 streams 128-byte-wide K slices of A and B into a ring of shared
+// memory stages with TMA (128-byte swizzle); warp 5 issues tcgen05.mma from one elected thread and frees each stage with
+// tcgen05.commit; warps 0-3 wait for the accumulator, read it with tcgen05.ld (one TMEM lane = one output row per
+// thread) and apply the epilogue in the reference's op order (model/int8_cuda.py:163-178). No TMA load multicasts.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fry {
+
+constexpr int kBlockM = 128;
+constexpr int kTileKBytes = 128;  // one swizzle row: the K bytes a stage holds
+constexpr int kGemmThreads = 192;
+constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
+
+template <int KIND, int BN, bool GATED>
+struct GemmShape {
+    static constexpr int kElem = KIND == 0 ? 1 : 2;
+    static constexpr int kBoxK = kTileKBytes / kElem;
+    static constexpr int kABytes = kBlockM * kTileKBytes;
+    static constexpr int kBBytes = BN * kTileKBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes * (GATED ? 2 : 1);
+    static constexpr int kStagesFit = (200 * 1024) / kStageBytes;
+    static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+    static constexpr int kAccCols = BN * (GATED ? 2 : 1);
+    static constexpr int kTmemCols = kAccCols <= 32 ? 32 : kAccCols <= 64 ? 64 : kAccCols <= 128 ? 128 : kAccCols <= 256 ? 256 : 512;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
+    static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
+};
+
+// Applies the epilogue to 16 consecutive columns [n, n + 16) of one row m; acc holds the raw TMEM words.
+template <int EPI>
+FRY_DEVICE void epilogue16(const GemmArgs& p, int m, int n, int N, const uint32_t (&acc)[16], const uint32_t (&up)[16]) {
+    const size_t row = static_cast<size_t>(m) * N + n;
+    const int valid = N - n >= 16 ? 16 : N - n;  // 8 or 16: N is a multiple of 8
+    if constexpr (EPI == kEpiInt32) {
+        int32_t* out = static_cast<int32_t*>(p.out) + row;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+            if (v * 4 < valid)
+                reinterpret_cast<int4*>(out)[v] = make_int4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+        return;
+    } else if constexpr (EPI == kEpiLinearF32) {
+        float* out = static_cast<float*>(p.out) + row;
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(acc[e]) + (p.bias_f32 ? p.bias_f32[n + e < N ? n + e : N - 1] : 0.0f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (q * 4 < valid) reinterpret_cast<float4*>(out)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        return;
+    } else {
+        uint16_t res[16], orig[16];
+        if constexpr (EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16) {
+            if (EPI != kEpiLinearF16 || p.residual != nullptr) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    if (h * 8 < valid) *reinterpret_cast<uint4*>(res + 8 * h) = *reinterpret_cast<const uint4*>(p.residual + row + 8 * h);
+            }
+        }
+        if constexpr (EPI == kEpiMix) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (h * 8 < valid) *reinterpret_cast<uint4*>(orig + 8 * h) = *reinterpret_cast<const uint4*>(p.original + row + 8 * h);
+        }
+        float xs = 0.0f;
+        if constexpr (EPI <= kEpiMix) xs = p.x_scale[m];
+        float rs = 0.0f, is = 0.0f;
+        if constexpr (EPI == kEpiMix) {
+            rs = h2f_bits(*p.residual_scale);
+            is = h2f_bits(*p.input_scale);
+        }
+        uint16_t result[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int col = n + e < N ? n + e : N - 1;
+            float value;
+            if constexpr (EPI == kEpiBias) {
+                value = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs);
+                value = __fmaf_rn(value, p.w_scale[col], p.bias ? h2f_bits(p.bias[col]) : 0.0f);
+            } else if constexpr (EPI == kEpiGated) {
+                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), p.w_scale[col]);
+                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), p.w_scale[N + col]);
+                // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
+                const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
+                value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
+            } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
+                value = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs);
+                value = __fmaf_rn(value, p.w_scale[col], h2f_bits(res[e]));
+                if constexpr (EPI == kEpiMix) {
+                    const float stream = __half2float(__float2half_rn(value));
+                    value = __fmaf_rn(stream, rs, __fmul_rn(h2f_bits(orig[e]), is));
+                }
+            } else {  // kEpiLinearF16: (acc + bias) + residual
+                value = __uint_as_float(acc[e]);
+                if (p.bias) value = __fadd_rn(value, h2f_bits(p.bias[col]));
+                if (p.residual) value = __fadd_rn(value, h2f_bits(res[e]));
+            }
+            result[e] = f2h_bits(value);
+        }
+        uint16_t* out = static_cast<uint16_t*>(p.out) + row;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (h * 8 < valid) reinterpret_cast<uint4*>(out)[h] = *reinterpret_cast<const uint4*>(result + 8 * h);
+    }
+}
+
+template <int KIND, int BN, bool GATED, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmArgs args, int M, int N,
+                int K) {
+    using S = GemmShape<KIND, BN, GATED>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+    uint64_t* empty = full + S::kStages;
+    uint64_t* acc_full = empty + S::kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kBlockM, n0 = blockIdx.x * BN;
+    const int k_tiles = (K * S::kElem + kTileKBytes - 1) / kTileKBytes;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, S::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 4 && lane == 0) {
+        prefetch_tensor_map(&map_a);
+        prefetch_tensor_map(&map_b);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (elect_one()) {
+            for (int kt = 0; kt < k_tiles; ++kt) {
+                const int s = kt % S::kStages;
+                const uint32_t phase = (kt / S::kStages) & 1;
+                if (!mbar_wait(&empty[s], phase ^ 1, 10)) break;
+                uint8_t* a = smem + s * S::kStageBytes;
+                uint8_t* b = a + S::kABytes;
+                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+                tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
+                tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
+                if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
+            }
+        }
+    } else if (warp == 5) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = instr_desc<KIND>(BN);
+            for (int kt = 0; kt < k_tiles; ++kt) {
+                const int s = kt % S::kStages;
+                const uint32_t phase = (kt / S::kStages) & 1;
+                if (!mbar_wait(&full[s], phase, 11)) break;
+                tc_fence_after();
+                const uint32_t a = smem_addr(smem + s * S::kStageBytes);
+                const uint32_t b = a + S::kABytes;
+#pragma unroll
+                for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
+                    const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
+                    const uint32_t accumulate = (kt > 0 || k > 0) ? 1u : 0u;
+                    mma_ss<KIND>(tmem, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
+                    if constexpr (GATED) mma_ss<KIND>(tmem + BN, da, smem_desc_sw128(b + S::kBBytes + k * kMmaKBytes), idesc, accumulate);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(acc_full);
+        }
+    } else {
+        // warps 0-3: TMEM lanes 32w..32w+31 are rows m0 + 32w + lane
+        if (mbar_wait(acc_full, 0, 12)) {
+            tc_fence_after();
+            const int m = m0 + warp * 32 + lane;
+            const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+            for (int c = 0; c < BN; c += 16) {
+                if (n0 + c >= N) break;  // uniform across the warp
+                uint32_t acc[16], up[16];
+                tmem_load16(lane_base + c, acc);
+                if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
+                tmem_load_wait();
+                if (m < M) epilogue16<EPI>(args, m, n0 + c, N, acc, up);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmemCols);
+    }
+}
+
+// ---- host side ---------------------------------------------------------------------------------------------
+
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                 const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder(std::string* error) {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* symbol = nullptr;
+        cudaDriverEntryPointQueryResult found;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &symbol, cudaEnableDefault, &found) == cudaSuccess &&
+            found == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(symbol);
+    });
+    if (!fn && error) *error = "the CUDA driver has no cuTensorMapEncodeTiled";
+    return fn;
+}
+
+// A [rows, k] K-major operand as a TMA map with a box of 128 bytes of K by box_rows rows, 128-byte swizzle, zero fill.
+bool make_map(CUtensorMap* map, const void* base, int elem_bytes, int k, int rows, int box_rows, std::string* error) {
+    EncodeTiled encode = encoder(error);
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * elem_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileKBytes / elem_bytes), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult result = encode(map, elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                   const_cast<void*>(base), dims, strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (result != CUDA_SUCCESS) {
+        if (error) *error = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(result));
+        return false;
+    }
+    return true;
+}
+
+template <int KIND, int BN, bool GATED, int EPI>
+cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
+    using S = GemmShape<KIND, BN, GATED>;
+    auto kernel = gemm_kernel<KIND, BN, GATED, EPI>;
+    const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
+    if (attribute != cudaSuccess) return attribute;
+    CUtensorMap map_a, map_b;
+    if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error) || !make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error))
+        return cudaErrorInvalidValue;
+    const dim3 grid((N + BN - 1) / BN, (M + kBlockM - 1) / kBlockM);
+    kernel<<<grid, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, args, M, N, K);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 128 everywhere else.
+cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
+                 std::string* error) {
+    if (kind == 0) {
+        switch (epilogue) {
+            case kEpiBias:
+                return N % 144 == 0 ? launch<0, 144, false, kEpiBias>(a, b, args, M, N, K, stream, error)
+                                    : launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
+            case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
+            case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
+            case kEpiMix: return launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
+            case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
+            default: break;
+        }
+    } else {
+        switch (epilogue) {
+            case kEpiLinearF16: return launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
+            default: break;
+        }
+    }
+    if (error) *error = "no GEMM for this kind and epilogue";
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace fry

@@ -1,0 +1,69 @@
+// Internal launch API of the Fry kernels (C++). The C ABI in abi.cu wraps these; include/fry_b200.h declares it.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace fry {
+
+// GEMM epilogues. The int8 ones follow model/int8_cuda.py:163-178 (EPI 0-3 there); the fp16 ones
+// model/fused_blocks.py:208-225 without the gate.
+enum GemmEpilogue : int {
+    kEpiBias = 0,       // int8: fp16(fma(acc * xs, ws, bias))
+    kEpiGated = 1,      // int8: fp16((g * sigmoid(g)) * u), weight rows = gate rows then up rows
+    kEpiResidual = 2,   // int8: fp16(fma(acc * xs, ws, residual))
+    kEpiMix = 3,        // int8: the residual sum rounded to fp16, then fp16(fma(stream, rs, original * is))
+    kEpiInt32 = 4,      // int8: the raw int32 sums
+    kEpiLinearF16 = 5,  // fp16: fp16((acc + bias) + residual), bias and residual optional
+    kEpiLinearF32 = 6,  // fp16: fp32 acc + fp32 bias (optional)
+};
+
+struct GemmArgs {
+    const float* x_scale = nullptr;          // [M]
+    const float* w_scale = nullptr;          // [N] ([2N] gated)
+    const uint16_t* bias = nullptr;          // fp16 [N]
+    const float* bias_f32 = nullptr;         // fp32 [N]
+    const uint16_t* residual = nullptr;      // fp16 [M, N]
+    const uint16_t* original = nullptr;      // fp16 [M, N]
+    const uint16_t* residual_scale = nullptr;  // fp16 scalar
+    const uint16_t* input_scale = nullptr;     // fp16 scalar
+    void* out = nullptr;                     // [M, N]
+};
+
+// kind 0: int8 A [M, K], B [N, K] (gated: [2N, K]); kind 1: fp16 A [M, K], B [N, K].
+cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
+                 std::string* error);
+
+// Row kernels (rows.cu).
+cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                       const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream);
+cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream);
+cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream);
+cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
+                            uint16_t* out, int B, int D, cudaStream_t stream);
+
+// Template attention (attention.cu).
+cudaError_t template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+                               uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
+                               cudaStream_t stream, std::string* error);
+
+// Heads (heads.cu).
+struct HeadWeights {
+    const uint16_t* ln_gain;         // fp16 [d]
+    const uint16_t* a_weight;        // fp16 [d, d]: row n of (W_f^T W_t / sqrt d)^T, K-major for the GEMM
+    const float* a_bias;             // fp32 [d]
+    const float* narrow_weight;      // fp32 [21, d]: s, 4 promotions, 16 board-down rows
+    const float* narrow_bias;        // fp32 [21]
+    const float* hidden_weight;      // fp32 [d, 1120]
+    const float* hidden_bias;        // fp32 [d]
+    const float* out_weight;         // fp32 [bins, d]
+    const float* out_bias;           // fp32 [bins]
+    int bins;
+};
+size_t heads_workspace_bytes(int B, int D);
+cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
+                  int D, cudaStream_t stream, std::string* error);
+
+}  // namespace fry

@@ -1,0 +1,344 @@
+// Row kernels of the Fry forward: HBM/L2-bound, one warp per activation row, 16-byte vector loads.
+//
+//  norm_quant_kernel    `norm_quant` / `mix_norm_quant` (model/int8_blocks.py:156-212): optional input mix, RMSNorm with
+//                       gain in fp32, per-row absmax, int8 by round-half-even, scale absmax / 127.
+//  rms_norm_kernel      the final nn.RMSNorm in fp16 (model/fused_blocks.py:863) ahead of the heads.
+//  rotate_quant_kernel  `rotate_quant` (model/int8_blocks.py:216-251): the SwiGLU output zero-padded to the down width,
+//                       times the block-diagonal 32x32 Sylvester Hadamard matrix (a 5-stage butterfly in registers, one
+//                       32-block per lane), per-row absmax, int8.
+//  embedding_kernel     `board_embedding` (model/fused_blocks.py:449-507): embed[token] + position[t] + the 23 square
+//                       feature rows of `SquareFeatures.indices` (model/model.py:147-169), found in-kernel from the board.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fry {
+
+constexpr int kRowWarps = 8;
+
+FRY_DEVICE void unpack8(const uint4& u, float (&v)[8]) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = h2f_bits(h[i]);
+}
+
+// x [M, D] fp16 -> q [M, D] int8, scale [M]; with MIX, x is first mixed with original and the mix stored to mixed.
+template <int CHUNKS, bool MIX>
+__global__ void __launch_bounds__(kRowWarps * 32) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
+                                                                    const uint16_t* residual_scale, const uint16_t* input_scale,
+                                                                    const uint16_t* __restrict__ gain, float eps, uint16_t* mixed,
+                                                                    int8_t* __restrict__ q, float* __restrict__ scale, int M, int D) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowWarps + warp;
+    if (row >= M) return;
+    const size_t base = static_cast<size_t>(row) * D;
+    float rs = 0.0f, is = 0.0f;
+    if constexpr (MIX) {
+        rs = h2f_bits(*residual_scale);
+        is = h2f_bits(*input_scale);
+    }
+    float v[CHUNKS][8];
+    float squares = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < D) {
+            unpack8(*reinterpret_cast<const uint4*>(x + base + col), v[c]);
+            if constexpr (MIX) {
+                float o[8];
+                unpack8(*reinterpret_cast<const uint4*>(original + base + col), o);
+                uint16_t packed[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    packed[i] = f2h_bits(__fmaf_rn(rs, v[c][i], __fmul_rn(is, o[i])));
+                    v[c][i] = h2f_bits(packed[i]);
+                }
+                *reinterpret_cast<uint4*>(mixed + base + col) = *reinterpret_cast<const uint4*>(packed);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[c][i] = 0.0f;
+        }
+    }
+    squares = warp_sum(squares);
+    const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(D)), eps));
+    float absmax = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < D) {
+            float g[8];
+            unpack8(*reinterpret_cast<const uint4*>(gain + col), g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[i]);
+                absmax = fmaxf(absmax, fabsf(v[c][i]));
+            }
+        }
+    }
+    absmax = fmaxf(warp_max(absmax), 1e-20f);
+    const float step_inverse = __fdiv_rn(127.0f, absmax);
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < D) {
+            uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int value = __float2int_rn(__fmul_rn(v[c][i], step_inverse));
+                packed[i / 4] |= (static_cast<uint32_t>(value) & 0xffu) << (8 * (i % 4));
+            }
+            *reinterpret_cast<uint2*>(q + base + col) = make_uint2(packed[0], packed[1]);
+        }
+    }
+    if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
+}
+
+template <int CHUNKS>
+__global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gain, float eps,
+                                                                  uint16_t* __restrict__ y, int M, int D) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowWarps + warp;
+    if (row >= M) return;
+    const size_t base = static_cast<size_t>(row) * D;
+    float v[CHUNKS][8];
+    float squares = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < D) {
+            unpack8(*reinterpret_cast<const uint4*>(x + base + col), v[c]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
+        }
+    }
+    squares = warp_sum(squares);
+    const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(D)), eps));
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < D) {
+            float g[8];
+            unpack8(*reinterpret_cast<const uint4*>(gain + col), g);
+            uint16_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) packed[i] = f2h_bits(__fmul_rn(__fmul_rn(v[c][i], inverse), g[i]));
+            *reinterpret_cast<uint4*>(y + base + col) = *reinterpret_cast<const uint4*>(packed);
+        }
+    }
+}
+
+// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M]. Lane l owns Hadamard block l.
+__global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
+                                                                      float* __restrict__ scale, int M, int hidden, int width) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowWarps + warp;
+    if (row >= M) return;
+    const int first = lane * 32;
+    float v[32];
+#pragma unroll
+    for (int part = 0; part < 4; ++part) {
+        const int col = first + part * 8;
+        if (col < hidden) {
+            float u[8];
+            unpack8(*reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * hidden + col), u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[part * 8 + i] = u[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[part * 8 + i] = 0.0f;
+        }
+    }
+    // y = H32 v, H32[i][j] = (-1)^popcount(i & j): the butterfly (a, b) -> (a + b, a - b) over each index bit
+#pragma unroll
+    for (int span = 1; span < 32; span <<= 1)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if ((i & span) == 0) {
+                const float a = v[i], b = v[i + span];
+                v[i] = __fadd_rn(a, b);
+                v[i + span] = __fsub_rn(a, b);
+            }
+    float absmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) absmax = fmaxf(absmax, fabsf(v[i]));
+    absmax = fmaxf(warp_max(absmax), 1e-20f);
+    const float step_inverse = __fdiv_rn(127.0f, absmax);
+    if (first < width) {
+        uint32_t packed[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            packed[w] = 0u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                packed[w] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[w * 4 + i], step_inverse))) & 0xffu) << (8 * i);
+        }
+        uint4* out = reinterpret_cast<uint4*>(q + static_cast<size_t>(row) * width + first);
+        out[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        out[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    }
+    if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
+}
+
+// ---- embedding ------------------------------------------------------------------------------------------------
+
+constexpr int kTokens = 70, kSquares = 64, kFeatures = 23, kVocab = 81, kPieceCodes = 13, kEdge = 13, kNoPiece = 225;
+// each feature's first row in the table: 4 x 226 offsets, 8 x 14 neighbours, 8 x 85 lines, 9 knights, 2 x 15 pawns
+__constant__ int kFeatureRowOffset[kFeatures] = {0,    226,  452,  678,  904,  918,  932,  946,  960,  974,  988,  1002,
+                                                 1016, 1101, 1186, 1271, 1356, 1441, 1526, 1611, 1696, 1705, 1720};
+__constant__ int kDirections[8][2] = {{0, 1}, {0, -1}, {1, 0}, {-1, 0}, {1, 1}, {-1, 1}, {1, -1}, {-1, -1}};
+__constant__ int kKnightJumps[8][2] = {{1, 2}, {2, 1}, {2, -1}, {1, -2}, {-1, -2}, {-2, -1}, {-2, 1}, {-1, 2}};
+
+FRY_DEVICE int code_at(const int* codes, int file, int rank) {
+    return (file >= 0 && file < 8 && rank >= 0 && rank < 8) ? codes[rank * 8 + file] : kEdge;
+}
+
+// One CTA per board: the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
+__global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ boards, const uint16_t* __restrict__ embed,
+                                                        const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
+                                                        uint16_t* __restrict__ out, int D) {
+    __shared__ int codes[kTokens];
+    __shared__ int firsts[4];
+    __shared__ int rows[kSquares][kFeatures];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    for (int t = tid; t < kTokens; t += blockDim.x) {
+        const int64_t token = boards[static_cast<size_t>(b) * kTokens + t];
+        const bool ok = t < kSquares ? (token >= 0 && token < kPieceCodes) : (token >= 0 && token < kVocab);
+        if (!ok) record_error(kBadToken, b);
+        codes[t] = ok ? static_cast<int>(token) : 0;
+    }
+    __syncthreads();
+    if (tid < 4) {
+        const int wanted[4] = {6, 12, 5, 11};  // our king, their king, our queen, their queen
+        int first = kSquares;
+        for (int s = 0; s < kSquares; ++s)
+            if (codes[s] == wanted[tid]) {
+                first = s;
+                break;
+            }
+        firsts[tid] = first;
+    }
+    __syncthreads();
+    {
+        const int s = tid & 63, part = tid >> 6, file = s & 7, rank = s >> 3;
+        int* r = rows[s];
+        if (part == 0) {
+            for (int i = 0; i < 4; ++i) {
+                const int p = firsts[i];
+                r[i] = kFeatureRowOffset[i] + (p < kSquares ? (rank - (p >> 3) + 7) * 15 + file - (p & 7) + 7 : kNoPiece);
+            }
+            int ours = 0, theirs = 0;
+            for (int j = 0; j < 8; ++j) {
+                const int c = code_at(codes, file + kKnightJumps[j][0], rank + kKnightJumps[j][1]);
+                ours += c == 2;
+                theirs += c == 8;
+            }
+            r[20] = kFeatureRowOffset[20] + min(ours, 2) * 3 + min(theirs, 2);
+        } else if (part == 1) {
+            for (int d = 0; d < 8; ++d) r[4 + d] = kFeatureRowOffset[4 + d] + code_at(codes, file + kDirections[d][0], rank + kDirections[d][1]);
+        } else if (part == 2) {
+            for (int d = 0; d < 8; ++d) {
+                int line = 0;
+                for (int k = 1; k <= 7; ++k) {
+                    const int c = code_at(codes, file + kDirections[d][0] * k, rank + kDirections[d][1] * k);
+                    if (c == kEdge) break;
+                    if (c != 0) {
+                        line = 1 + (c - 1) * 7 + (k - 1);
+                        break;
+                    }
+                }
+                r[12 + d] = kFeatureRowOffset[12 + d] + line;
+            }
+        } else {
+            for (int d = 0; d < 2; ++d) {  // up and down the file: the nearest pawn of either side, others do not block
+                int pawn = 0;
+                for (int k = 1; k <= 7; ++k) {
+                    const int c = code_at(codes, file, rank + kDirections[d][1] * k);
+                    if (c == kEdge) break;
+                    if (c == 1 || c == 7) {
+                        pawn = 1 + (c == 7) * 7 + (k - 1);
+                        break;
+                    }
+                }
+                r[21 + d] = kFeatureRowOffset[21 + d] + pawn;
+            }
+        }
+    }
+    __syncthreads();
+    const int vectors = D / 8;
+    for (int idx = tid; idx < kTokens * vectors; idx += blockDim.x) {
+        const int t = idx / vectors, col = (idx % vectors) * 8;
+        float e[8], p[8];
+        unpack8(*reinterpret_cast<const uint4*>(embed + static_cast<size_t>(codes[t]) * D + col), e);
+        unpack8(*reinterpret_cast<const uint4*>(position + static_cast<size_t>(t) * D + col), p);
+        float features[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (t < kSquares) {
+            for (int f = 0; f < kFeatures; ++f) {
+                float row[8];
+                unpack8(*reinterpret_cast<const uint4*>(table + static_cast<size_t>(rows[t][f]) * D + col), row);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) features[i] = __fadd_rn(features[i], row[i]);
+            }
+        }
+        uint16_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            packed[i] = f2h_bits(__fadd_rn(__fadd_rn(e[i], p[i]), h2f_bits(f2h_bits(features[i]))));
+        *reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * kTokens + t) * D + col) = *reinterpret_cast<const uint4*>(packed);
+    }
+}
+
+// ---- launchers ------------------------------------------------------------------------------------------------
+
+cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                       const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
+    const dim3 grid((M + kRowWarps - 1) / kRowWarps);
+    const int chunks = (D + 255) / 256;
+    const bool mix = original != nullptr;
+#define FRY_NQ(C)                                                                                                                 \
+    (mix ? (norm_quant_kernel<C, true><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
+                                                                             mixed, q, scale, M, D), 0)                           \
+         : (norm_quant_kernel<C, false><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
+                                                                              mixed, q, scale, M, D), 0))
+    switch (chunks) {
+        case 1: FRY_NQ(1); break;
+        case 2: FRY_NQ(2); break;
+        case 3: FRY_NQ(3); break;
+        default: FRY_NQ(4); break;
+    }
+#undef FRY_NQ
+    return cudaGetLastError();
+}
+
+cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
+    const dim3 grid((M + kRowWarps - 1) / kRowWarps);
+    switch ((D + 255) / 256) {
+        case 1: rms_norm_kernel<1><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
+        case 2: rms_norm_kernel<2><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
+        case 3: rms_norm_kernel<3><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
+        default: rms_norm_kernel<4><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    if (hidden % 8 != 0 || width % 32 != 0 || width > 1024 || hidden > width) return cudaErrorInvalidValue;
+    rotate_quant_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, stream>>>(h, q, scale, M, hidden, width);
+    return cudaGetLastError();
+}
+
+cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
+                            uint16_t* out, int B, int D, cudaStream_t stream) {
+    if (B <= 0) return cudaSuccess;
+    if (D % 8 != 0) return cudaErrorInvalidValue;
+    embedding_kernel<<<B, 256, 0, stream>>>(boards, embed, position, table, out, D);
+    return cudaGetLastError();
+}
+
+}  // namespace fry

@@ -1,0 +1,224 @@
+"""The int8 network as the engine's search sees it: the drop-in for the reference's `engine.inference.int8_model`.
+
+`int8_model(checkpoint_path, fp16_blocks, weights)` (engine/inference.py:267-272) loads a checkpoint in the reference's
+format (`{"model_settings", "state_dict"}`, model/checkpoint.py:22-42) and int8 weights in the reference's
+`Int8Weights` layout (engine/quantization.py:21,124-140), and returns an `Int8Network` whose
+`forward(boards: LongTensor[B, 70] cuda) -> Tensor[B, 1969] fp32` gives the answer rows that `answer_rows`
+(engine/inference.py:19-23) would give, and which has `.d_model` (engine/engine_search.py:198).
+
+Set-up follows `fp16_model` and `quantize_blocks` (engine/inference.py:242-249, model/int8_blocks.py:254-298): the residual
+stream is scaled by 1/16 (embedding tables, combine_heads, down's scale), everything but the heads is fp16, the heads'
+weights are folded in fp64 (model/fused_blocks.py:815-824). The whole forward is one C-ABI call (fry_forward) that
+enqueues every kernel on the current stream, so the module records into CUDA graphs like the reference's.
+"""
+import ctypes
+import math
+from pathlib import Path
+
+import numpy as np
+import torch
+from torch import nn
+
+from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
+from .library import FryBlock, FryError, FryNetwork, library
+from .ops import heads_struct
+
+FP16_RESIDUAL_SCALE = 1 / 16      # engine/inference.py:239
+HADAMARD_BLOCK = 32               # model/int8_blocks.py:15
+DOWN_INPUT_MULTIPLE = 128         # model/int8_blocks.py:17
+INT8_MAX = 127                    # engine/quantization.py:47
+EPS = 1e-5
+
+# Fry's shipped geometry (fry-final-117): 28 blocks, d 768, 24 query heads of 32, 12 key/value heads, SwiGLU 992 wide,
+# 128 value bins; the query/key width cycles 8/16/24 over the blocks
+FRY_SETTINGS = {"d_model": 768, "num_layers": 28, "n_heads": 24, "kv_heads": 12, "qk_ratio": [0.25, 0.5, 0.75] * 9 + [0.25],
+                "mlp_hidden": 992, "value_bins": 128}
+
+
+def geometry(settings: dict) -> dict:
+    """The shapes ChessTransformer(**settings) builds (model/model.py:38-53,178-199)."""
+    d = settings.get("d_model", 128)
+    layers = settings.get("num_layers", 4)
+    heads = settings.get("n_heads", 4)
+    ratio = settings.get("qk_ratio", 1.0)
+    ratios = list(ratio) if isinstance(ratio, (list, tuple)) else [ratio] * layers
+    d_head = d // heads
+    hidden = settings.get("mlp_hidden") or max(32, int(8 / 3 * d) // 32 * 32)
+    return {"d": d, "layers": layers, "heads": heads, "kv_heads": settings.get("kv_heads") or heads, "dv": d_head,
+            "dqs": [max(1, round(r * d_head)) for r in ratios], "hidden": hidden, "templates": settings.get("position_templates", 8),
+            "bins": settings.get("value_bins", 128)}
+
+
+def hadamard(size: int) -> torch.Tensor:
+    """Sylvester's +-1 Hadamard matrix (model/int8_blocks.py:54-58)."""
+    matrix = torch.ones(1, 1)
+    while matrix.shape[0] < size:
+        matrix = torch.cat([torch.cat([matrix, matrix], 1), torch.cat([matrix, -matrix], 1)], 0)
+    return matrix
+
+
+def down_inputs(hidden: int) -> int:
+    return -(-hidden // DOWN_INPUT_MULTIPLE) * DOWN_INPUT_MULTIPLE
+
+
+def round_to_nearest(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric int8 rows, scale = absmax / 127: GPTQ (engine/quantization.py:76-99) with a diagonal Hessian."""
+    weight = weight.double()
+    scale = weight.abs().amax(dim=1).clamp(min=1e-20) / INT8_MAX
+    return (weight / scale[:, None]).round().clamp(-INT8_MAX, INT8_MAX).to(torch.int8), scale.float()
+
+
+def quantize(state: dict, settings: dict, layers: list[int] | None = None) -> dict:
+    """Int8Weights of a state dict, laid out as engine/quantization.py:129-139 lays them out (projection = Q|K|V|template
+    mix rows, gate_up = gate rows then up rows, down zero-padded to a multiple of 128 inputs and rotated by the
+    block-diagonal Hadamard matrix / 32), rounded to nearest."""
+    g = geometry(settings)
+    weights = {}
+    for i in (range(g["layers"]) if layers is None else layers):
+        p = f"encoder.{i}."
+        projection = torch.cat([state[p + n + ".weight"].double() for n in ("Q", "K", "V", "template_mix")])
+        gate_up = torch.cat([state[p + "mlp.gate_projection.weight"].double(), state[p + "mlp.up_projection.weight"].double()])
+        width = down_inputs(g["hidden"])
+        rotation = torch.block_diag(*[hadamard(HADAMARD_BLOCK)] * (width // HADAMARD_BLOCK)).double()
+        down = nn.functional.pad(state[p + "mlp.down_projection.weight"].double().cpu(), (0, width - g["hidden"])) @ rotation / HADAMARD_BLOCK
+        weights[i] = {"projection": round_to_nearest(projection), "gate_up": round_to_nearest(gate_up), "down": round_to_nearest(down)}
+    return weights
+
+
+def synthetic_state_dict(settings: dict, seed: int, std: float = 0.02) -> dict[str, torch.Tensor]:
+    """Random-init fp32 weights of a network with these settings (the benchmark configs' N(0, 0.02)), named as the
+    reference's ChessTransformer.state_dict() names them. Gains 1, the input skip's scales 0.8 and 0.5."""
+    g = geometry(settings)
+    d, H, KV, dv, P = g["d"], g["heads"], g["kv_heads"], g["dv"], g["templates"]
+    generator = torch.Generator().manual_seed(seed)
+    normal = lambda *shape: std * torch.randn(*shape, generator=generator)
+    state = {"embed.weight": torch.randn(BOARD_VOCAB_SIZE, d, generator=generator), "position_embed": torch.randn(TOKENS_PER_BOARD, d, generator=generator),
+             "square_features.table": normal(FEATURE_TABLE_ROWS, d), "templates": normal(P, 64, 64), "ln.weight": torch.ones(d)}
+    for i, dq in enumerate(g["dqs"]):
+        p = f"encoder.{i}."
+        state.update({p + "Q.weight": normal(H * dq, d), p + "Q.bias": normal(H * dq), p + "K.weight": normal(KV * dq, d),
+                      p + "K.bias": normal(KV * dq), p + "V.weight": normal(KV * dv, d), p + "V.bias": normal(KV * dv),
+                      p + "q_norm.weight": torch.ones(dq), p + "k_norm.weight": torch.ones(dq), p + "ln1.weight": torch.ones(d),
+                      p + "ln2.weight": torch.ones(d), p + "combine_heads.weight": normal(d, d), p + "combine_heads.bias": normal(d),
+                      p + "mlp.up_projection.weight": normal(g["hidden"], d), p + "mlp.gate_projection.weight": normal(g["hidden"], d),
+                      p + "mlp.down_projection.weight": normal(d, g["hidden"]), p + "template_mix.weight": normal(P * H, d),
+                      p + "template_mix.bias": normal(P * H), p + "residual_scale": torch.full((1,), 0.8),
+                      p + "input_scale": torch.full((1,), 0.5)})
+    state.update({"board_down_project.0.weight": normal(VALUE_TOKEN_DIM, d), "board_down_project.0.bias": normal(VALUE_TOKEN_DIM),
+                  "eval_head.0.weight": normal(d, TOKENS_PER_BOARD * VALUE_TOKEN_DIM), "eval_head.0.bias": normal(d),
+                  "eval_head.2.weight": normal(g["bins"], d), "eval_head.2.bias": normal(g["bins"]),
+                  "from_projection.weight": normal(d, d), "from_projection.bias": normal(d), "to_projection.weight": normal(d, d),
+                  "to_projection.bias": normal(d), "promotion_projection.weight": normal(4, d), "promotion_projection.bias": normal(4)})
+    return state
+
+
+def _pointer(tensor: torch.Tensor) -> int:
+    return tensor.data_ptr()
+
+
+class Int8Network(nn.Module):
+    """Fry's network with every block in int8, on one GPU. forward(boards [B, 70] int64 cuda) -> rows [B, 1969] fp32."""
+
+    def __init__(self, state: dict, settings: dict, weights: dict, device: torch.device | str | None = None):
+        super().__init__()
+        device = torch.device(device if device is not None else "cuda")
+        if device.type != "cuda":
+            raise FryError("Int8Network runs on a CUDA device only")
+        g = geometry(settings)
+        missing = [layer for layer in range(g["layers"]) if layer not in weights]
+        if missing:
+            raise FryError(f"Int8Network runs every block in int8; no int8 weights for blocks {missing} "
+                           "(the reference keeps those blocks in fp16, which this engine does not run)")
+        self.settings, self.geometry, self.d_model, self.eps = settings, g, g["d"], EPS
+        s = FP16_RESIDUAL_SCALE
+        half = lambda t: t.detach().to(device=device, dtype=torch.float16).contiguous()
+        single = lambda t: t.detach().to(device=device, dtype=torch.float32).contiguous()
+        self.tensors = {"embed": half(state["embed.weight"].float() * s), "position": half(state["position_embed"].float() * s),
+                        "table": half(state["square_features.table"].float() * s), "templates": half(state["templates"]),
+                        "ln": half(state["ln.weight"])}
+        self.blocks = []
+        for i, dq in enumerate(g["dqs"]):
+            p = f"encoder.{i}."
+            w = weights[i]
+            width = w["down"][0].shape[1]
+            block = {"ln1": half(state[p + "ln1.weight"]), "ln2": half(state[p + "ln2.weight"]),
+                     "residual_scale": half(state[p + "residual_scale"]), "input_scale": half(state[p + "input_scale"]),
+                     "q_gain": half(state[p + "q_norm.weight"]), "k_gain": half(state[p + "k_norm.weight"]),
+                     "projection": w["projection"][0].to(device).contiguous(), "projection_scale": single(w["projection"][1]),
+                     "projection_bias": half(torch.cat([state[p + n + ".bias"] for n in ("Q", "K", "V", "template_mix")])),
+                     "combine_heads": half(state[p + "combine_heads.weight"].float() * s),
+                     "combine_heads_bias": half(state[p + "combine_heads.bias"].float() * s),
+                     "gate_up": w["gate_up"][0].to(device).contiguous(), "gate_up_scale": single(w["gate_up"][1]),
+                     "down": w["down"][0].to(device).contiguous(), "down_scale": single(w["down"][1].float() * s)}
+            if width != down_inputs(g["hidden"]):
+                raise FryError(f"block {i}'s down takes {width} inputs, not the padded hidden width {down_inputs(g['hidden'])}")
+            self.blocks.append(block)
+        # heads (model/fused_blocks.py:815-824), folded in fp64
+        from_w, from_b = state["from_projection.weight"].double(), state["from_projection.bias"].double()
+        to_w, to_b = state["to_projection.weight"].double(), state["to_projection.bias"].double()
+        scale = 1 / math.sqrt(g["d"])
+        self.tensors.update({
+            "a_weight": half(to_w.T @ from_w * scale),   # row n = column n of A = W_f^T W_t / sqrt d
+            "a_bias": single(to_w.T @ from_b * scale),
+            "narrow_weight": single(torch.cat([(to_b @ from_w)[None] * scale, state["promotion_projection.weight"].double(),
+                                               state["board_down_project.0.weight"].double()])),
+            "narrow_bias": single(torch.cat([(from_b @ to_b)[None] * scale, state["promotion_projection.bias"].double(),
+                                             state["board_down_project.0.bias"].double()])),
+            "hidden_weight": single(state["eval_head.0.weight"]), "hidden_bias": single(state["eval_head.0.bias"]),
+            "out_weight": single(state["eval_head.2.weight"]), "out_bias": single(state["eval_head.2.bias"])})
+        self.device = device
+        self._network = self._struct()
+
+    def _struct(self) -> FryNetwork:
+        g, t = self.geometry, self.tensors
+        blocks = (FryBlock * len(self.blocks))()
+        for i, (dq, b) in enumerate(zip(g["dqs"], self.blocks)):
+            blocks[i] = FryBlock(dq, *(_pointer(b[name]) for name in ("ln1", "ln2", "residual_scale", "input_scale", "q_gain", "k_gain",
+                                                                      "projection", "projection_scale", "projection_bias", "combine_heads",
+                                                                      "combine_heads_bias", "gate_up", "gate_up_scale", "down",
+                                                                      "down_scale")))
+        self._blocks_array = blocks
+        return FryNetwork(g["d"], g["layers"], g["heads"], g["kv_heads"], g["dv"], g["templates"], g["hidden"], down_inputs(g["hidden"]),
+                          self.eps, _pointer(t["embed"]), _pointer(t["position"]), _pointer(t["table"]), _pointer(t["templates"]),
+                          ctypes.cast(blocks, ctypes.POINTER(FryBlock)),
+                          heads_struct(t["ln"], t["a_weight"], t["a_bias"], t["narrow_weight"], t["narrow_bias"], t["hidden_weight"],
+                                       t["hidden_bias"], t["out_weight"], t["out_bias"]))
+
+    def workspace_bytes(self, boards: int) -> int:
+        return library().fry_forward_workspace_bytes(ctypes.byref(self._network), boards)
+
+    def forward(self, board_state: torch.Tensor) -> torch.Tensor:
+        if not board_state.is_cuda or board_state.device != self.device:
+            raise FryError(f"Int8Network on {self.device} got boards on {board_state.device}")
+        boards = board_state.to(torch.int64).contiguous()
+        B = boards.shape[0]
+        if boards.dim() != 2 or boards.shape[1] != TOKENS_PER_BOARD:
+            raise FryError(f"boards are [B, {TOKENS_PER_BOARD}] tokens, got {tuple(boards.shape)}")
+        rows = torch.empty(B, 1969, device=self.device, dtype=torch.float32)
+        lib = library()
+        size = lib.fry_forward_workspace_bytes(ctypes.byref(self._network), B)
+        workspace = torch.empty(max(size, 1), device=self.device, dtype=torch.uint8)
+        lib.fry_forward(ctypes.byref(self._network), ctypes.c_void_p(boards.data_ptr()), B, ctypes.c_void_p(rows.data_ptr()),
+                        ctypes.c_void_p(workspace.data_ptr()), size, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        return rows
+
+
+def load_checkpoint(checkpoint_path: Path) -> tuple[dict, dict]:
+    """(state_dict, model_settings) of a checkpoint written by the reference's save_checkpoint (model/checkpoint.py:22-38)."""
+    checkpoint = torch.load(checkpoint_path, map_location="cpu", weights_only=False)
+    settings = dict(checkpoint["model_settings"])
+    if settings.pop("loops", 1) != 1:
+        raise FryError(f"{checkpoint_path} runs its blocks more than once, which the network here cannot")
+    return {name: tensor.float() if tensor.is_floating_point() else tensor for name, tensor in checkpoint["state_dict"].items()}, settings
+
+
+def int8_model(checkpoint_path: Path, fp16_blocks: int = 0, weights: dict | None = None, device: torch.device | str | None = None) -> Int8Network:
+    """`engine.inference.int8_model` (engine/inference.py:267-272) on this engine. `weights` are Int8Weights (the reference's
+    cached GPTQ weights load unchanged); None rounds the checkpoint's weights to nearest. Every block must be int8:
+    fp16_blocks > 0, or weights missing a block, are refused (the reference runs those blocks in fp16)."""
+    if fp16_blocks:
+        raise FryError("this engine runs every block in int8: fp16_blocks must be 0")
+    state, settings = load_checkpoint(Path(checkpoint_path))
+    if weights is None:
+        weights = quantize(state, settings)
+    return Int8Network(state, settings, weights, device)

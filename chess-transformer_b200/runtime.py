@@ -1,0 +1,94 @@
+"""The batch runtime around the network: CUDA graphs per batch size on lanes of their own stream, fed from pinned host
+buffers. Mirrors the reference's `GraphedBatches` and `Lane` (engine/inference.py:62-225, non-lean lanes): `launch`
+copies a batch of boards in and replays the smallest graph that holds it and returns at once; `collect` copies the answer
+rows out and waits for them. At most `in_flight` batches are out at a time, one a lane.
+"""
+import numpy as np
+import torch
+from torch import nn
+
+from .boards import START_BOARD
+from .encoding import ANSWER_WIDTH, TOKENS_PER_BOARD
+
+
+def small_graph_sizes(max_batch: int, chunk: int | None = None) -> list[int]:
+    """engine/inference.py:62-68: sizes 1..max_batch, doubling to 16, then steps of a sixteenth."""
+    chunk = min(chunk or max_batch, max_batch)
+    steps = [1]
+    while steps[-1] < chunk:
+        steps.append(min(chunk, steps[-1] * 2 if steps[-1] < 16 else steps[-1] + max(4, steps[-1] // 16)))
+    sizes = [whole + step for whole in range(0, max_batch, chunk) for step in steps]
+    return sizes[:next(index for index, size in enumerate(sizes) if size >= max_batch) + 1]
+
+
+class Lane:
+    """One stream with a graph per size, its own memory pool, and pinned buffers for the boards in and the rows out."""
+
+    def __init__(self, model: nn.Module, sizes: list[int]):
+        self.stream = torch.cuda.Stream()
+        self.device = torch.cuda.current_device()
+        self.pending = False
+        largest = sizes[-1]
+        # recorded on real boards, as the reference records its lanes
+        self.boards = torch.from_numpy(np.tile(START_BOARD, (largest, 1))).long().cuda()
+        self.boards_host = torch.zeros(largest, TOKENS_PER_BOARD, dtype=torch.long, pin_memory=True)
+        self.answers_host = torch.zeros(largest, ANSWER_WIDTH, dtype=torch.float32, pin_memory=True)
+        self.done = torch.cuda.Event(blocking=True)
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream), torch.no_grad():
+            for size in sizes:
+                model(self.boards[:size])
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self.pool = torch.cuda.graph_pool_handle()
+        self.graphs, self.answers = {}, {}
+        for size in reversed(sizes):
+            self.graphs[size] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graphs[size], pool=self.pool, stream=self.stream), torch.no_grad():
+                self.answers[size] = model(self.boards[:size])
+        self.done.record(self.stream)
+        self.done.synchronize()
+
+
+class GraphedBatches:
+    """engine/inference.py:148-225: launch(boards uint8/int64 [n, 70]) -> handle; collect(handle) -> float32 [n, 1969]."""
+
+    def __init__(self, model: nn.Module, sizes: list[int], in_flight: int = 2, blocking_wait: bool = False):
+        self.model, self.sizes, self.blocking_wait = model, sizes, blocking_wait
+        self.lanes = [Lane(model, sizes) for _ in range(in_flight)]
+
+    def free_lane(self) -> Lane:
+        lane = next((lane for lane in self.lanes if not lane.pending), None)
+        if lane is None:
+            raise RuntimeError("more batches in flight than lanes")
+        return lane
+
+    def launch(self, boards: np.ndarray) -> tuple[Lane, int, int]:
+        lane = self.free_lane()
+        lane.boards_host[:len(boards)] = torch.from_numpy(np.asarray(boards))
+        return self.launch_filled(lane, len(boards))
+
+    def launch_filled(self, lane: Lane, count: int) -> tuple[Lane, int, int]:
+        size = next(size for size in self.sizes if size >= count)
+        lane.pending = True
+        with torch.cuda.stream(lane.stream):
+            lane.boards[:count].copy_(lane.boards_host[:count], non_blocking=True)
+            lane.graphs[size].replay()
+            if self.blocking_wait:
+                lane.done.record(lane.stream)
+        return lane, size, count
+
+    def collect(self, launched: tuple[Lane, int, int]) -> np.ndarray:
+        lane, size, count = launched
+        if self.blocking_wait:
+            lane.done.synchronize()
+        with torch.cuda.stream(lane.stream):
+            lane.answers_host[:count].copy_(lane.answers[size][:count])
+        lane.stream.synchronize()
+        lane.pending = False
+        return lane.answers_host[:count].numpy()
+
+    def settle(self) -> None:
+        for lane in self.lanes:
+            if lane.pending:
+                lane.stream.synchronize()
+                lane.pending = False

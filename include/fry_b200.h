@@ -1,0 +1,158 @@
+/* fry_b200: the C ABI of the B200 (sm_100a) int8 inference engine for Fry's network (GilliamWong/chess-transformer).
+ *
+ * Every pointer argument is a device pointer unless stated otherwise; fp16 tensors are passed as uint16_t bit patterns;
+ * every array is dense row-major. `stream` is a cudaStream_t (NULL: the legacy default stream). Work is only enqueued:
+ * nothing here synchronises the stream, allocates device memory or changes a pointer between calls, so every entry point
+ * may be captured in a CUDA graph. Each returns 0 on success or a nonzero code; fry_last_error() gives the calling
+ * thread's last message. Shapes a kernel does not take are refused on the host with FRY_ERROR_SHAPE before anything is
+ * enqueued (the reference raises ValueError for these, model/int8_blocks.py:111-112, model/fused_blocks.py:116-117).
+ *
+ * Faults the kernels can detect (a wait that timed out, a board token outside the vocabulary) are recorded in a device
+ * status word that fry_device_status() reads; the kernels never trap.
+ */
+#ifndef FRY_B200_H
+#define FRY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FRY_OK 0
+#define FRY_ERROR_SHAPE 1   /* a shape or alignment the kernels do not take */
+#define FRY_ERROR_CUDA 2    /* a CUDA runtime or driver call failed */
+
+/* The calling thread's last error message ("" after a success). */
+const char* fry_last_error(void);
+
+/* The library version string. */
+const char* fry_version(void);
+
+/* Reads the current device's status word: *code 0 if no kernel recorded a fault, else the code (1 a bounded wait timed
+ * out, 2 a board token outside the vocabulary) and *where its site. clear != 0 resets it. Synchronous. */
+int fry_device_status(int* code, int* where, int clear);
+
+/* ---- block ops: each replaces one torch custom op of the reference ----------------------------------------------- */
+
+/* `chess::int8_linear` (model/int8_blocks.py:132-139, kernels :66-128 and model/int8_cuda.py:34-183):
+ * out[M, N] fp16 = epilogue(x[M, K] int8 . weight^T), weight int8 [N, K] ([2N, K], gate rows then up rows, if gated).
+ * The epilogue is picked as the reference picks it (model/int8_cuda.py:163-178):
+ *   gated                      fp16((g * sigmoid(g)) * u), g and u = (acc * x_scale) * weight_scale
+ *   residual == NULL           fp16(fma(acc * x_scale, weight_scale, bias))        (bias may be NULL: zero)
+ *   residual, original NULL    fp16(fma(acc * x_scale, weight_scale, residual))
+ *   residual and original      the above rounded to fp16, then fp16(fma(stream, *residual_scale, original * *input_scale))
+ * x_scale fp32 [M], weight_scale fp32 [N] ([2N] gated); out may alias residual. N must be a multiple of 8, K of 16. */
+int fry_int8_linear(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
+                    const uint16_t* residual, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                    uint16_t* out, int M, int N, int K, int gated, void* stream);
+
+/* The int32 sums x[M, K] . weight[N, K]^T of the same tensor-core kernel, for bit-exact checks. No reference
+ * counterpart exposes them; they are the `acc` of model/int8_blocks.py:85-92. */
+int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int M, int N, int K, void* stream);
+
+/* `chess::norm_quant` (model/int8_blocks.py:191-193, kernel :156-175): q[M, D] int8, scale[M] fp32 of
+ * RMSNorm(x) * gain, a row's scale its absmax / 127. D a multiple of 8 up to 1024. */
+int fry_norm_quant(const uint16_t* x, const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int D, void* stream);
+
+/* `chess::mix_norm_quant` (model/int8_blocks.py:201-207): mixed = fp16(*residual_scale * x + *input_scale * original),
+ * then norm_quant of mixed. */
+int fry_mix_norm_quant(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                       const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, void* stream);
+
+/* `chess::rotate_quant` (model/int8_blocks.py:234-246, kernel :216-231): h[M, hidden] fp16 zero-padded to width, times the
+ * block-diagonal 32x32 Sylvester Hadamard matrix (the reference's hadamard_signs, model/int8_blocks.py:54-58, built in),
+ * then int8 rows q[M, width] and scale[M]. width a multiple of 32 up to 1024, hidden a multiple of 8. */
+int fry_rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, void* stream);
+
+/* `chess::template_attention` (model/fused_blocks.py:104-171; model/attention_cuda.py:444-461): projected [B, 70, W] fp16
+ * with W = heads*dq + kv_heads*dq + kv_heads*dv + heads*templates_count (q | k | v | template mix), templates fp16
+ * [templates_count, 64, 64], q_gain and k_gain fp16 [dq] -> out [B, 70, heads*dv] fp16. Takes dv 32, 8 templates, even
+ * dq up to 32, heads/kv_heads groups that fit 8 query heads a CTA. */
+int fry_template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+                           uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps, void* stream);
+
+/* `chess::linear` (model/fused_blocks.py:308-313, kernel :229-304) for fp16 inputs: out[M, N] = (x[M, K] . weight^T + bias)
+ * + residual, fp32 accumulation, fp16 out (out_fp32 == 0) or fp32 out without residual (out_fp32 != 0, the reference's
+ * accumulate_fp32). weight is [N, K] fp16 (the reference stores it transposed, [K, N]). bias fp16 [N] (fp32 [N] when
+ * out_fp32) and residual [M, N] may be NULL; out may alias residual. N a multiple of 8, K of 8. */
+int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, const uint16_t* residual, void* out, int M, int N, int K,
+               int out_fp32, void* stream);
+
+/* `chess::board_embedding` / `chess::input_embedding` (model/fused_blocks.py:397-406,495-507, SquareFeatures.indices
+ * model/model.py:147-169): boards int64 [B, 70] -> out [B, 70, D] fp16 = embed[token] + position[t] + fp16(sum of the 23
+ * square-feature rows of table). embed [81, D], position [70, D], table [1735, D] fp16. A token outside the vocabulary
+ * (0..12 on squares, 0..80 on the metadata) is read as 0 and recorded in the device status word. */
+int fry_board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table, uint16_t* out,
+                        int B, int D, void* stream);
+
+/* The heads after the last block, as the reference runs them on B200 (model/fused_blocks.py:863-874, weights folded by
+ * head_weights :815-824) with answer_rows (engine/inference.py:19-23). stream [B, 70, D] fp16 -> rows [B, 1969] fp32.
+ * workspace: device scratch of fry_heads_workspace_bytes(B, D) bytes. */
+typedef struct FryHeads {
+    const uint16_t* ln_gain;       /* fp16 [D], the final RMSNorm's gain */
+    const uint16_t* a_weight;      /* fp16 [D, D]: (W_f^T W_t / sqrt D)^T, row n = output column n */
+    const float* a_bias;           /* fp32 [D]: W_t^T b_f / sqrt D */
+    const float* narrow_weight;    /* fp32 [21, D]: (b_t W_f)/sqrt D, promotion_projection, board_down_project */
+    const float* narrow_bias;      /* fp32 [21] */
+    const float* hidden_weight;    /* fp32 [D, 1120]: eval_head[0] */
+    const float* hidden_bias;      /* fp32 [D] */
+    const float* out_weight;       /* fp32 [bins, D]: eval_head[2] */
+    const float* out_bias;         /* fp32 [bins] */
+    int bins;
+} FryHeads;
+
+size_t fry_heads_workspace_bytes(int B, int D);
+int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
+              int D, void* stream);
+
+/* ---- the whole forward ------------------------------------------------------------------------------------------- */
+
+/* One int8 block as `Int8Block` holds it (model/int8_blocks.py:254-272) with the layout of engine/quantization.py:129-139. */
+typedef struct FryBlock {
+    int dq;
+    const uint16_t* ln1;                 /* fp16 [D] */
+    const uint16_t* ln2;                 /* fp16 [D] */
+    const uint16_t* residual_scale;      /* fp16 [1] */
+    const uint16_t* input_scale;         /* fp16 [1] */
+    const uint16_t* q_gain;              /* fp16 [dq] */
+    const uint16_t* k_gain;              /* fp16 [dq] */
+    const int8_t* projection;            /* int8 [36*dq + 576 (generally heads*dq + kv*dq + kv*dv + heads*templates), D] */
+    const float* projection_scale;       /* fp32 [rows of projection] */
+    const uint16_t* projection_bias;     /* fp16 [rows of projection] */
+    const uint16_t* combine_heads;       /* fp16 [D, D], row n = output column n (the reference's [K, N] transposed) */
+    const uint16_t* combine_heads_bias;  /* fp16 [D] */
+    const int8_t* gate_up;               /* int8 [2*hidden, D], gate rows then up rows */
+    const float* gate_up_scale;          /* fp32 [2*hidden] */
+    const int8_t* down;                  /* int8 [D, width], padded and Hadamard-rotated */
+    const float* down_scale;             /* fp32 [D], times the stream's 1/16 */
+} FryBlock;
+
+/* The int8 network: FusedTransformer with every block an Int8Block (model/fused_blocks.py:829-878,
+ * model/int8_blocks.py:292-298), each down mixing the next block's input (link_input_mixes, model/fused_blocks.py:358-363).
+ * This struct and the blocks array live in host memory; every tensor pointer in them is a device pointer. */
+typedef struct FryNetwork {
+    int d_model, layers, heads, kv_heads, dv, templates_count, hidden, down_width;
+    float eps;
+    const uint16_t* embed;      /* fp16 [81, D], times 1/16 */
+    const uint16_t* position;   /* fp16 [70, D], times 1/16 */
+    const uint16_t* table;      /* fp16 [1735, D], times 1/16 */
+    const uint16_t* templates;  /* fp16 [templates_count, 64, 64] */
+    const FryBlock* blocks;     /* [layers], host memory */
+    FryHeads head_weights;      /* the heads' weights */
+} FryNetwork;
+
+/* Device scratch the forward needs for B boards. */
+size_t fry_forward_workspace_bytes(const FryNetwork* network, int B);
+
+/* `FusedTransformer.forward` + `answer_rows` (model/fused_blocks.py:856-862, engine/inference.py:19-23): boards int64
+ * [B, 70] -> rows fp32 [B, 1969] (1968 move logits, then the expected score). */
+int fry_forward(const FryNetwork* network, const int64_t* boards, int B, float* rows, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRY_B200_H */

@@ -1,0 +1,117 @@
+"""Host-side checks that need no GPU: the C-ABI library builds, loads and exports every entry point include/fry_b200.h
+declares; the product's move table, weight layout and synthetic boards agree with the oracle; CPU tensors are refused."""
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import chess_transformer_b200 as fry
+from chess_transformer_b200 import boards as fry_boards, encoding as fry_encoding, network as fry_network
+from chess_transformer_b200.build import build
+from chess_transformer_b200.library import LIBRARY_PATH, SIGNATURES, FryError, library
+from oracle import encoding, int8 as oi, model as om
+from tests.conftest import ROOT, SMALL
+
+HEADER = ROOT / "include" / "fry_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(fry_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return library()
+
+
+def test_the_library_exports_every_declared_entry_point(lib):
+    declared = declared_functions()
+    assert len(declared) >= 15
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(LIBRARY_PATH)], capture_output=True, text=True, check=True).stdout
+    names = {line.split()[-1] for line in exported.splitlines() if line.strip()}
+    assert set(declared) <= names
+    assert set(declared) == set(SIGNATURES)
+    assert lib.fry_version().decode().startswith("fry_b200")
+
+
+def test_the_library_is_built_for_sm_100a_only():
+    from chess_transformer_b200.build import FLAGS
+    assert "arch=compute_100a,code=sm_100a" in FLAGS and sum(flag.startswith("arch=") for flag in FLAGS) == 1
+
+
+def test_shapes_are_refused_on_the_host_before_any_launch(lib):
+    with pytest.raises(FryError, match="multiple of 8"):
+        lib.fry_int8_linear(None, None, None, None, None, None, None, None, None, None, 70, 12, 256, 0, None)
+    with pytest.raises(FryError, match="template attention"):
+        lib.fry_template_attention(None, None, None, None, None, 1, 24, 12, 8, 64, 8, 1e-5, None)
+    assert "template attention" in lib.fry_last_error().decode()
+
+
+def test_the_ops_refuse_cpu_tensors():
+    from chess_transformer_b200 import ops
+    x = torch.zeros(2, 70, 128, dtype=torch.float16)
+    with pytest.raises(FryError, match="GPU only"):
+        ops.norm_quant(x, torch.ones(128, dtype=torch.float16), 1e-5)
+
+
+def test_the_move_table_is_the_oracles():
+    assert fry_encoding.NUM_MOVE_IDS == encoding.NUM_MOVE_IDS == 1968
+    assert np.array_equal(fry_encoding.MOVE_FROM_SQUARES, encoding.MOVE_FROM_SQUARES)
+    assert np.array_equal(fry_encoding.MOVE_TO_SQUARES, encoding.MOVE_TO_SQUARES)
+    promotions = np.full(1968, -1)
+    promotions[encoding.PROMOTION_MOVE_IDS] = encoding.PROMOTION_PIECES
+    assert np.array_equal(fry_encoding.MOVE_PROMOTION_PIECES, promotions)
+
+
+def test_the_compiled_move_table_is_current():
+    assert (ROOT / "chess-transformer_b200" / "csrc" / "moves.h").read_text() == fry_encoding.moves_header()
+
+
+def test_the_weight_layout_is_the_oracles():
+    state = om.seeded_state_dict(SMALL, 10)
+    ours, theirs = fry_network.quantize(state, SMALL), oi.int8_weights(state, SMALL)
+    for layer in theirs:
+        for name in ("projection", "gate_up", "down"):
+            assert torch.equal(ours[layer][name][0], theirs[layer][name][0])
+            assert torch.equal(ours[layer][name][1], theirs[layer][name][1])
+
+
+def test_synthetic_boards_are_legal_looking_and_seeded():
+    boards = fry_boards.random_boards(512, 7)
+    assert boards.shape == (512, 70) and boards.dtype == np.uint8
+    assert np.array_equal(boards, fry_boards.random_boards(512, 7))
+    assert not np.array_equal(boards, fry_boards.random_boards(512, 8))
+    squares = boards[:, :64]
+    assert ((squares == 6).sum(1) == 1).all() and ((squares == 12).sum(1) == 1).all()
+    others = ((squares > 0) & (squares != 6) & (squares != 12)).sum(1)
+    assert others.min() >= 2 and others.max() <= 30
+    assert not np.isin(squares[:, :8], [1, 7]).any() and not np.isin(squares[:, 56:], [1, 7]).any()
+    assert np.isin(boards[:, 64], [13, 14]).all() and np.isin(boards[:, 65:69], [15, 16]).all()
+    assert ((boards[:, 69] == 17) | ((boards[:, 69] >= 57) & (boards[:, 69] < 65))).all()
+    # the oracle's square features take them
+    om.square_feature_indices(torch.from_numpy(boards[:8]))
+
+
+def test_start_board_is_the_initial_position():
+    start = fry_boards.START_BOARD
+    assert start[4] == 6 and start[60] == 12 and (start[8:16] == 1).all() and (start[48:56] == 7).all() and start[64] == 14
+
+
+def test_the_synthetic_checkpoint_loads_into_the_oracles_shapes():
+    state = fry_network.synthetic_state_dict(SMALL, 0)
+    shapes = om.parameter_shapes(SMALL)
+    assert set(shapes) == set(state)
+    assert all(tuple(state[name].shape) == shape for name, shape in shapes.items())
+
+
+def test_int8_model_refuses_fp16_blocks(tmp_path):
+    torch.save({"model_settings": SMALL, "state_dict": om.seeded_state_dict(SMALL, 0)}, tmp_path / "model.pt")
+    with pytest.raises(FryError, match="int8"):
+        fry_network.int8_model(tmp_path / "model.pt", fp16_blocks=1)
+    with pytest.raises(FryError, match="CUDA"):
+        fry_network.int8_model(tmp_path / "model.pt", device="cpu")
