@@ -115,13 +115,19 @@ int fry_rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidd
     return check(fry::rotate_quant(h, q, scale, M, hidden, width, as_stream(stream)), "fry_rotate_quant");
 }
 
-int fry_template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+int fry_pair_templates(const uint16_t* templates, uint16_t* paired, int templates_count, void* stream) {
+    if (templates_count != 8) return fail(FRY_ERROR_SHAPE, "fry_pair_templates pairs 8 templates");
+    if (!aligned16(paired)) return fail(FRY_ERROR_SHAPE, "fry_pair_templates needs a 16-byte aligned output");
+    return check(fry::pair_templates(templates, paired, as_stream(stream)), "fry_pair_templates");
+}
+
+int fry_template_attention(const uint16_t* projected, const uint16_t* paired_templates, const uint16_t* q_gain, const uint16_t* k_gain,
                            uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps, void* stream) {
     if (B < 0) return fail(FRY_ERROR_SHAPE, "fry_template_attention takes B >= 0");
-    if (!aligned16(projected) || !aligned16(out) || (reinterpret_cast<uintptr_t>(templates) & 3u))
-        return fail(FRY_ERROR_SHAPE, "fry_template_attention needs 16-byte aligned projections and outputs");
+    if (!aligned16(projected) || !aligned16(out) || !aligned16(paired_templates))
+        return fail(FRY_ERROR_SHAPE, "fry_template_attention needs 16-byte aligned projections, templates and outputs");
     std::string detail;
-    return check(fry::template_attention(projected, templates, q_gain, k_gain, out, B, heads, kv_heads, dq, dv, templates_count, eps,
+    return check(fry::template_attention(projected, paired_templates, q_gain, k_gain, out, B, heads, kv_heads, dq, dv, templates_count, eps,
                                          as_stream(stream), &detail),
                  "fry_template_attention", detail);
 }

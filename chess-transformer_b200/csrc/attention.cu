@@ -6,10 +6,15 @@
 // fp16(sum_t c[i, h, t] * T[t, i, j]); softmax over the 70 keys; probabilities rounded to fp16 for the value product,
 // whose fp32 sums are divided by the unrounded total. Grouped-query: head h reads key/value head h / (heads / kv_heads).
 //
-// One CTA per (position, group of up to 8 query heads), one warp per query head. The CTA stages its key/value heads'
-// normalised keys and transposed values in shared memory; each warp walks its head's 5 row tiles of 16 queries with
-// mma.sync m16n8k16 (fp16 in, fp32 accumulate): 70 x 80 scores and 16 x 32 outputs per tile are too small for
-// tcgen05's 128-row tiles, and the bias is formed in registers from the templates (never materialised in HBM).
+// One CTA per (position, group of up to 8 query heads), one warp per query head, in 5 phases: the 4 slabs of 16 square
+// rows, then the metadata rows. The CTA stages its key/value heads' normalised keys and raw values in shared memory.
+// Before a square slab, the warps form its template bias for all the CTA's heads with mma.sync: for a pair of squares
+// (i0, i1), A = the 8 heads' coefficients block-diagonally over (i0's 8 templates | i1's 8 templates) and B = the pair's
+// templates, paired per key as [square][key][template] (fry_pair_templates, as the reference pairs them,
+// model/attention_cuda.py:412-434), so one m16n8k16 gives 8 heads x 2 squares x 8 keys of bias. Each warp then takes
+// its head's 16 rows: scores over 10 key tiles, bias added from the slab, softmax in registers, P.V with the values'
+// B fragments read by ldmatrix.trans. 70 x 80 scores and 16 x 32 outputs per tile are too small for tcgen05's 128-row
+// tiles; the legacy mma.sync keeps them in registers.
 #include <cmath>
 #include <string>
 
@@ -19,6 +24,7 @@
 namespace fry {
 
 constexpr int kAttnTokens = 70, kAttnSquares = 64, kAttnKeys = 80, kAttnDv = 32, kAttnTemplates = 8, kMaxHeadsPerCta = 8;
+constexpr int kSlab = 16, kBiasRow = 72, kValueRow = 40;
 
 FRY_DEVICE void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -28,6 +34,8 @@ FRY_DEVICE void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
 FRY_DEVICE uint32_t pack_half2(float lo, float hi) {
     return static_cast<uint32_t>(f2h_bits(lo)) | (static_cast<uint32_t>(f2h_bits(hi)) << 16);
 }
+FRY_DEVICE float low_half(uint32_t pair) { return h2f_bits(static_cast<uint16_t>(pair & 0xffff)); }
+FRY_DEVICE float high_half(uint32_t pair) { return h2f_bits(static_cast<uint16_t>(pair >> 16)); }
 FRY_DEVICE float quad_sum(float v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     return v + __shfl_xor_sync(0xffffffffu, v, 2);
@@ -37,59 +45,127 @@ FRY_DEVICE float quad_max(float v) {
     return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
 }
 
-// DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values^T [kv][32][80 + 8] (fp16).
+// paired[i][j][t] = templates[t][i][j]: a key's 8 templates side by side, the B operand of the bias MMA.
+__global__ void pair_templates_kernel(const uint16_t* __restrict__ templates, uint16_t* __restrict__ paired) {
+    const int index = blockIdx.x * blockDim.x + threadIdx.x;  // over 64 x 64 (i, j)
+    if (index >= kAttnSquares * kAttnSquares) return;
+    uint16_t row[kAttnTemplates];
+#pragma unroll
+    for (int t = 0; t < kAttnTemplates; ++t) row[t] = templates[t * kAttnSquares * kAttnSquares + index];
+    *reinterpret_cast<uint4*>(paired + index * kAttnTemplates) = *reinterpret_cast<const uint4*>(row);
+}
+
+// The template bias of square rows [16 * slab, 16 * slab + 16) for the CTA's heads into bias [head][16][kBiasRow] (fp16).
+FRY_DEVICE void make_bias_slab(uint16_t* bias, const uint16_t* board, const uint16_t* paired, int slab, int width, int c_offset,
+                               int first_head, int heads_here, int warp, int warps, int g, int t) {
+    for (int pair = warp; pair < kSlab / 2; pair += warps) {
+        const int i0 = slab * kSlab + 2 * pair, i1 = i0 + 1;
+        uint32_t a0 = 0, a3 = 0;
+        if (g < heads_here) {
+            a0 = *reinterpret_cast<const uint32_t*>(board + i0 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t);
+            a3 = *reinterpret_cast<const uint32_t*>(board + i1 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t);
+        }
+        const uint16_t* t0 = paired + (i0 * kAttnSquares + g) * kAttnTemplates + 2 * t;
+        const uint16_t* t1 = paired + (i1 * kAttnSquares + g) * kAttnTemplates + 2 * t;
+#pragma unroll
+        for (int j = 0; j < kAttnSquares / 8; ++j) {
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            mma_f16(c, a0, 0u, 0u, a3, *reinterpret_cast<const uint32_t*>(t0 + j * 8 * kAttnTemplates),
+                    *reinterpret_cast<const uint32_t*>(t1 + j * 8 * kAttnTemplates));
+            if (g < heads_here) {
+                uint16_t* to = bias + (g * kSlab + 2 * pair) * kBiasRow + j * 8 + 2 * t;
+                *reinterpret_cast<uint32_t*>(to) = pack_half2(c[0], c[1]);
+                *reinterpret_cast<uint32_t*>(to + kBiasRow) = pack_half2(c[2], c[3]);
+            }
+        }
+    }
+}
+
+// Queries of rows [first, first + 16) for one head, raw (the A layout of m16n8k16: rows g and g + 8, depth 2t and 2t + 8).
+template <int KS>
+FRY_DEVICE void load_queries(uint32_t (&raw)[KS][2][2], const uint16_t* board, int first, int width, int head, int dq, int g, int t) {
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int row = first + g + 8 * r, col = ks * 16 + half * 8 + 2 * t;
+                raw[ks][r][half] = (row < kAttnTokens && col < dq) ? *reinterpret_cast<const uint32_t*>(board + row * width + head * dq + col) : 0u;
+            }
+}
+
+// DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values [kv][80][40], two bias slabs.
 template <int DQP>
-__global__ void __launch_bounds__(kMaxHeadsPerCta * 32) attention_kernel(const uint16_t* __restrict__ projected,
-                                                                         const uint16_t* __restrict__ templates,
-                                                                         const uint16_t* __restrict__ q_gain,
-                                                                         const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out,
-                                                                         int heads, int kv_heads, int dq, float eps, float scale) {
-    constexpr int KROW = DQP + 8, VROW = kAttnKeys + 8, KS = DQP / 16;
+__global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
+    attention_kernel(const uint16_t* __restrict__ projected, const uint16_t* __restrict__ paired, const uint16_t* __restrict__ q_gain,
+                     const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out, int heads, int kv_heads, int dq, float eps, float scale) {
+    constexpr int KROW = DQP + 8, KS = DQP / 16;
     extern __shared__ __align__(16) uint16_t attn_smem[];
-    const int heads_per_cta = blockDim.x / 32;
+    const int heads_here = blockDim.x / 32, warps = heads_here;
     const int group = heads / kv_heads;
-    const int kv_per_cta = heads_per_cta / group;
-    uint16_t* keys = attn_smem;                                  // [kv_per_cta][80][KROW]
-    uint16_t* values = keys + kv_per_cta * kAttnKeys * KROW;     // [kv_per_cta][32][VROW]
+    const int kv_here = heads_here / group;
+    uint16_t* keys = attn_smem;                                   // [kv_here][80][KROW]
+    uint16_t* values = keys + kv_here * kAttnKeys * KROW;         // [kv_here][80][kValueRow]
+    uint16_t* bias = values + kv_here * kAttnKeys * kValueRow;    // [2][heads_here][16][kBiasRow]
+    const int slab_size = heads_here * kSlab * kBiasRow;
 
     const int b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int width = (heads + kv_heads) * dq + kv_heads * kAttnDv + heads * kAttnTemplates;
     const int k_offset = heads * dq, v_offset = (heads + kv_heads) * dq, c_offset = v_offset + kv_heads * kAttnDv;
-    const int first_kv = blockIdx.x * kv_per_cta;
+    const int first_head = blockIdx.x * heads_here, first_kv = blockIdx.x * kv_here;
     const uint16_t* board = projected + static_cast<size_t>(b) * kAttnTokens * width;
 
-    // normalised keys, zero past dq and past the 70th key
-    for (int item = tid; item < kv_per_cta * kAttnKeys; item += blockDim.x) {
+    // normalised keys (zero past dq and past the 70th key), 16-byte loads and stores
+    for (int item = tid; item < kv_here * kAttnKeys; item += blockDim.x) {
         const int kv = item / kAttnKeys, key = item % kAttnKeys;
-        uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
         float k[DQP];
-        float squares = 0.0f;
 #pragma unroll
-        for (int i = 0; i < DQP; ++i) {
-            k[i] = (key < kAttnTokens && i < dq) ? h2f_bits(board[key * width + k_offset + (first_kv + kv) * dq + i]) : 0.0f;
-            squares = __fmaf_rn(k[i], k[i], squares);
+        for (int i = 0; i < DQP; ++i) k[i] = 0.0f;
+        float squares = 0.0f;
+        if (key < kAttnTokens) {
+            const uint16_t* from = board + key * width + k_offset + (first_kv + kv) * dq;
+#pragma unroll
+            for (int part = 0; part < DQP / 8; ++part)
+                if (part * 8 < dq) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(from + part * 8);
+                    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        k[part * 8 + 2 * w] = low_half(words[w]);
+                        k[part * 8 + 2 * w + 1] = high_half(words[w]);
+                    }
+                }
+#pragma unroll
+            for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
         }
         const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(dq)), eps));
+        uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
 #pragma unroll
-        for (int i = 0; i < DQP; ++i)
-            row[i] = (key < kAttnTokens && i < dq) ? f2h_bits(__fmul_rn(__fmul_rn(k[i], inverse), h2f_bits(k_gain[i]))) : 0;
+        for (int part = 0; part < DQP / 8; ++part) {
+            uint32_t words[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const int i = part * 8 + 2 * w;
+                const float g0 = i < dq ? h2f_bits(k_gain[i]) : 0.0f, g1 = i + 1 < dq ? h2f_bits(k_gain[i + 1]) : 0.0f;
+                words[w] = key < kAttnTokens ? pack_half2(__fmul_rn(__fmul_rn(k[i], inverse), g0), __fmul_rn(__fmul_rn(k[i + 1], inverse), g1))
+                                             : 0u;
+            }
+            *reinterpret_cast<uint4*>(row + part * 8) = make_uint4(words[0], words[1], words[2], words[3]);
+        }
     }
-    // values transposed: [kv][dv][key]
-    for (int item = tid; item < kv_per_cta * kAttnKeys * (kAttnDv / 8); item += blockDim.x) {
+    // values as they are, [kv][key][dv], zero past the 70th key
+    for (int item = tid; item < kv_here * kAttnKeys * (kAttnDv / 8); item += blockDim.x) {
         const int kv = item / (kAttnKeys * 4), rest = item % (kAttnKeys * 4), key = rest / 4, part = rest % 4;
         uint4 raw = make_uint4(0, 0, 0, 0);
-        if (key < kAttnTokens)
-            raw = *reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8);
-        const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) values[(kv * kAttnDv + part * 8 + i) * VROW + key] = h[i];
+        if (key < kAttnTokens) raw = *reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8);
+        *reinterpret_cast<uint4*>(values + (kv * kAttnKeys + key) * kValueRow + part * 8) = raw;
     }
-    __syncthreads();
+    make_bias_slab(bias, board, paired, 0, width, c_offset, first_head, heads_here, warp, warps, g, t);
 
-    const int head = blockIdx.x * heads_per_cta + warp;
-    const int kv = warp / group;
-    const uint16_t* kv_keys = keys + kv * kAttnKeys * KROW;
-    const uint16_t* kv_values = values + kv * kAttnDv * VROW;
+    const int head = first_head + warp;
+    const uint16_t* kv_keys = keys + (warp / group) * kAttnKeys * KROW;
+    const uint16_t* kv_values = values + (warp / group) * kAttnKeys * kValueRow;
     float qg[KS][2][2];
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks)
@@ -100,39 +176,39 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32) attention_kernel(const u
                 const int col = ks * 16 + half * 8 + 2 * t + e;
                 qg[ks][half][e] = col < dq ? h2f_bits(q_gain[col]) : 0.0f;
             }
+    uint32_t raw_q[KS][2][2];
+    load_queries<KS>(raw_q, board, 0, width, head, dq, g, t);
+    __syncthreads();
 
-    for (int tile = 0; tile < 5; ++tile) {
-        const int rows[2] = {tile * 16 + g, tile * 16 + g + 8};
-        // queries: a[ks][0..3] per the m16n8k16 A layout, normalised per row (the row's dq values sit on the quad)
-        float q[2][KS][2][2];
-        float squares[2] = {0.0f, 0.0f};
+    for (int phase = 0; phase < 5; ++phase) {
+        const bool squares_phase = phase < 4;
+        const int first = phase * kSlab;
+        // the next slab's bias into the other buffer, and the next phase's queries, ahead of this phase's work
+        if (phase + 1 < 4)
+            make_bias_slab(bias + ((phase + 1) & 1) * slab_size, board, paired, phase + 1, width, c_offset, first_head, heads_here, warp,
+                           warps, g, t);
+        uint32_t next_q[KS][2][2];
+        if (phase + 1 < 5) load_queries<KS>(next_q, board, first + kSlab, width, head, dq, g, t);
+
+        uint32_t a[KS][4];
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int r = 0; r < 2; ++r) {
+            float squares = 0.0f;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
-                    const int col = ks * 16 + half * 8 + 2 * t;
-                    uint32_t raw = 0;
-                    if (rows[r] < kAttnTokens && col < dq)
-                        raw = *reinterpret_cast<const uint32_t*>(board + rows[r] * width + head * dq + col);
-                    q[r][ks][half][0] = h2f_bits(static_cast<uint16_t>(raw & 0xffff));
-                    q[r][ks][half][1] = h2f_bits(static_cast<uint16_t>(raw >> 16));
-                    squares[r] = __fmaf_rn(q[r][ks][half][0], q[r][ks][half][0], squares[r]);
-                    squares[r] = __fmaf_rn(q[r][ks][half][1], q[r][ks][half][1], squares[r]);
+                    const float x0 = low_half(raw_q[ks][r][half]), x1 = high_half(raw_q[ks][r][half]);
+                    squares = __fmaf_rn(x1, x1, __fmaf_rn(x0, x0, squares));
                 }
-        uint32_t a[KS][4];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(quad_sum(squares[r]), static_cast<float>(dq)), eps));
+            const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(quad_sum(squares), static_cast<float>(dq)), eps));
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
                 for (int half = 0; half < 2; ++half)
-                    a[ks][r + 2 * half] = pack_half2(__fmul_rn(__fmul_rn(q[r][ks][half][0], inverse), qg[ks][half][0]),
-                                                     __fmul_rn(__fmul_rn(q[r][ks][half][1], inverse), qg[ks][half][1]));
+                    a[ks][r + 2 * half] = pack_half2(__fmul_rn(__fmul_rn(low_half(raw_q[ks][r][half]), inverse), qg[ks][half][0]),
+                                                     __fmul_rn(__fmul_rn(high_half(raw_q[ks][r][half]), inverse), qg[ks][half][1]));
         }
-        // scores over 10 key tiles of 8
         float s[10][4];
 #pragma unroll
         for (int j = 0; j < 10; ++j) {
@@ -143,38 +219,18 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32) attention_kernel(const u
                 mma_f16(s[j], a[ks][0], a[ks][1], a[ks][2], a[ks][3], *reinterpret_cast<const uint32_t*>(key_row + ks * 16),
                         *reinterpret_cast<const uint32_t*>(key_row + ks * 16 + 8));
         }
-        // scale, template bias on the square block, mask past the 70th key
-        float coefficient[2][kAttnTemplates];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            if (rows[r] < kAttnSquares) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(board + rows[r] * width + c_offset + head * kAttnTemplates);
-                const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-                for (int i = 0; i < kAttnTemplates; ++i) coefficient[r][i] = h2f_bits(h[i]);
-            }
-        }
+        const uint16_t* head_bias = bias + (phase & 1) * slab_size + warp * kSlab * kBiasRow;
         float top[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int j = 0; j < 10; ++j)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const int col = j * 8 + 2 * t;
-                float bias[2] = {0.0f, 0.0f};
-                if (rows[r] < kAttnSquares && col < kAttnSquares) {
-#pragma unroll
-                    for (int i = 0; i < kAttnTemplates; ++i) {
-                        const uint32_t pair = *reinterpret_cast<const uint32_t*>(templates + (i * kAttnSquares + rows[r]) * kAttnSquares + col);
-                        bias[0] = __fmaf_rn(coefficient[r][i], h2f_bits(static_cast<uint16_t>(pair & 0xffff)), bias[0]);
-                        bias[1] = __fmaf_rn(coefficient[r][i], h2f_bits(static_cast<uint16_t>(pair >> 16)), bias[1]);
-                    }
-                    bias[0] = h2f_bits(f2h_bits(bias[0]));
-                    bias[1] = h2f_bits(f2h_bits(bias[1]));
-                }
+                uint32_t pair = 0u;
+                if (squares_phase && j < 8) pair = *reinterpret_cast<const uint32_t*>(head_bias + (g + 8 * r) * kBiasRow + j * 8 + 2 * t);
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    float value = __fadd_rn(__fmul_rn(s[j][2 * r + e], scale), bias[e]);
-                    if (col + e >= kAttnTokens) value = -INFINITY;
+                    float value = __fadd_rn(__fmul_rn(s[j][2 * r + e], scale), e ? high_half(pair) : low_half(pair));
+                    if (j * 8 + 2 * t + e >= kAttnTokens) value = -INFINITY;
                     s[j][2 * r + e] = value;
                     top[r] = fmaxf(top[r], value);
                 }
@@ -192,7 +248,6 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32) attention_kernel(const u
             }
 #pragma unroll
         for (int r = 0; r < 2; ++r) total[r] = quad_sum(total[r]);
-        // out = P V over 5 key steps of 16
         float o[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
@@ -201,49 +256,71 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32) attention_kernel(const u
             const uint32_t p0 = pack_half2(s[2 * kk][0], s[2 * kk][1]), p1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
             const uint32_t p2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]), p3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-            for (int n = 0; n < 4; ++n) {
-                const uint16_t* value_row = kv_values + (n * 8 + g) * VROW + kk * 16 + 2 * t;
-                mma_f16(o[n], p0, p1, p2, p3, *reinterpret_cast<const uint32_t*>(value_row), *reinterpret_cast<const uint32_t*>(value_row + 8));
+            for (int n = 0; n < 4; n += 2) {
+                const uint16_t* rows = kv_values + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kValueRow + n * 8 + (lane >> 4) * 8;
+                uint32_t b0, b1, b2, b3;
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
+                             : "r"(smem_addr(rows)));
+                mma_f16(o[n], p0, p1, p2, p3, b0, b1);
+                mma_f16(o[n + 1], p0, p1, p2, p3, b2, b3);
             }
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            if (rows[r] >= kAttnTokens) continue;
-            uint16_t* to = out + (static_cast<size_t>(b) * kAttnTokens + rows[r]) * (heads * kAttnDv) + head * kAttnDv + 2 * t;
+            const int row = first + g + 8 * r;
+            if (row >= kAttnTokens) continue;
+            uint16_t* to = out + (static_cast<size_t>(b) * kAttnTokens + row) * (heads * kAttnDv) + head * kAttnDv + 2 * t;
 #pragma unroll
             for (int n = 0; n < 4; ++n)
-                *reinterpret_cast<uint32_t*>(to + n * 8) =
-                    pack_half2(__fdiv_rn(o[n][2 * r], total[r]), __fdiv_rn(o[n][2 * r + 1], total[r]));
+                *reinterpret_cast<uint32_t*>(to + n * 8) = pack_half2(__fdiv_rn(o[n][2 * r], total[r]), __fdiv_rn(o[n][2 * r + 1], total[r]));
         }
+        if (phase + 1 < 5) {
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) raw_q[ks][r][half] = next_q[ks][r][half];
+        }
+        __syncthreads();
     }
 }
 
-cudaError_t template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream) {
+    pair_templates_kernel<<<(kAttnSquares * kAttnSquares + 255) / 256, 256, 0, stream>>>(templates, paired);
+    return cudaGetLastError();
+}
+
+cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
                                cudaStream_t stream, std::string* error) {
     if (B <= 0) return cudaSuccess;
     const int group = kv_heads > 0 ? heads / kv_heads : 0;
     const int per_cta = heads < kMaxHeadsPerCta ? heads : kMaxHeadsPerCta;
     const int width = (heads + kv_heads) * dq + kv_heads * dv + heads * templates_count;
-    if (dv != kAttnDv || templates_count != kAttnTemplates || dq < 1 || dq > 32 || dq % 2 || kv_heads <= 0 || heads % kv_heads ||
+    if (dv != kAttnDv || templates_count != kAttnTemplates || dq < 1 || dq > 32 || dq % 8 || kv_heads <= 0 || heads % kv_heads ||
         heads % per_cta || per_cta % group || ((heads + kv_heads) * dq) % 8 || width % 8) {
         if (error)
-            *error = "template attention takes dv 32, 8 templates, an even dq up to 32, and head groups that fit 8 heads a CTA; got heads " +
-                     std::to_string(heads) + ", kv heads " + std::to_string(kv_heads) + ", dq " + std::to_string(dq) + ", dv " +
-                     std::to_string(dv);
+            *error = "template attention takes dv 32, 8 templates, dq a multiple of 8 up to 32, and head groups that fit 8 heads a CTA; "
+                     "got heads " + std::to_string(heads) + ", kv heads " + std::to_string(kv_heads) + ", dq " + std::to_string(dq) +
+                     ", dv " + std::to_string(dv);
         return cudaErrorInvalidValue;
     }
     const int kv_per_cta = per_cta / group;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dq)));  // 1 / math.sqrt(dq), rounded once to fp32
     const dim3 grid(heads / per_cta, B);
-    if (dq <= 16) {
-        const size_t bytes = (kv_per_cta * kAttnKeys * (16 + 8) + kv_per_cta * kAttnDv * (kAttnKeys + 8)) * sizeof(uint16_t);
-        attention_kernel<16><<<grid, per_cta * 32, bytes, stream>>>(projected, templates, q_gain, k_gain, out, heads, kv_heads, dq, eps,
-                                                                    scale);
+    const int dqp = dq <= 16 ? 16 : 32;
+    const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
+                          2 * static_cast<size_t>(per_cta) * kSlab * kBiasRow) * sizeof(uint16_t);
+    if (dqp == 16) {
+        const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<16>), static_cast<int>(bytes));
+        if (attribute != cudaSuccess) return attribute;
+        attention_kernel<16><<<grid, per_cta * 32, bytes, stream>>>(projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps, scale);
     } else {
-        const size_t bytes = (kv_per_cta * kAttnKeys * (32 + 8) + kv_per_cta * kAttnDv * (kAttnKeys + 8)) * sizeof(uint16_t);
-        attention_kernel<32><<<grid, per_cta * 32, bytes, stream>>>(projected, templates, q_gain, k_gain, out, heads, kv_heads, dq, eps,
-                                                                    scale);
+        const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<32>), static_cast<int>(bytes));
+        if (attribute != cudaSuccess) return attribute;
+        attention_kernel<32><<<grid, per_cta * 32, bytes, stream>>>(projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps, scale);
     }
     return cudaGetLastError();
 }

@@ -45,7 +45,9 @@ cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const 
                             uint16_t* out, int B, int D, cudaStream_t stream);
 
 // Template attention (attention.cu).
-cudaError_t template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+// paired [64][64][8] fp16: templates[t][i][j] at paired[i][j][t]
+cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream);
+cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
                                cudaStream_t stream, std::string* error);
 

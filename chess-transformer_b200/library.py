@@ -46,6 +46,7 @@ SIGNATURES = {
     "fry_norm_quant": ([_ptr, _ptr, _c_float, _ptr, _ptr, _c_int, _c_int, _ptr], _c_int),
     "fry_mix_norm_quant": ([_ptr] * 5 + [_c_float] + [_ptr] * 3 + [_c_int, _c_int, _ptr], _c_int),
     "fry_rotate_quant": ([_ptr] * 3 + [_c_int] * 3 + [_ptr], _c_int),
+    "fry_pair_templates": ([_ptr, _ptr, _c_int, _ptr], _c_int),
     "fry_template_attention": ([_ptr] * 5 + [_c_int] * 6 + [_c_float, _ptr], _c_int),
     "fry_linear": ([_ptr] * 5 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_board_embedding": ([_ptr] * 5 + [_c_int, _c_int, _ptr], _c_int),

@@ -21,7 +21,7 @@ from torch import nn
 
 from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
 from .library import FryBlock, FryError, FryNetwork, library
-from .ops import heads_struct
+from .ops import heads_struct, pair_templates
 
 FP16_RESIDUAL_SCALE = 1 / 16      # engine/inference.py:239
 HADAMARD_BLOCK = 32               # model/int8_blocks.py:15
@@ -124,6 +124,8 @@ class Int8Network(nn.Module):
         device = torch.device(device if device is not None else "cuda")
         if device.type != "cuda":
             raise FryError("Int8Network runs on a CUDA device only")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         g = geometry(settings)
         missing = [layer for layer in range(g["layers"]) if layer not in weights]
         if missing:
@@ -167,6 +169,9 @@ class Int8Network(nn.Module):
             "hidden_weight": single(state["eval_head.0.weight"]), "hidden_bias": single(state["eval_head.0.bias"]),
             "out_weight": single(state["eval_head.2.weight"]), "out_bias": single(state["eval_head.2.bias"])})
         self.device = device
+        with torch.cuda.device(device):
+            self.tensors["templates"] = pair_templates(self.tensors["templates"])
+            torch.cuda.current_stream(device).synchronize()
         self._network = self._struct()
 
     def _struct(self) -> FryNetwork:

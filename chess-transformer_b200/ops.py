@@ -145,9 +145,23 @@ def template_attention(projected: torch.Tensor, templates: torch.Tensor, q_gain:
     if T != 70:
         raise FryError(f"template_attention takes 70 tokens a position, got {T}")
     out = projected.new_empty(B, T, heads * dv)
-    library().fry_template_attention(_ptr(projected), _ptr(templates.contiguous()), _ptr(q_gain.contiguous()), _ptr(k_gain.contiguous()),
+    paired = pair_templates(templates)
+    library().fry_template_attention(_ptr(projected), _ptr(paired), _ptr(q_gain.contiguous()), _ptr(k_gain.contiguous()),
                                      _ptr(out), B, heads, kv_heads, dq, dv, templates_count, eps, _stream(projected))
     return out
+
+
+def pair_templates(templates: torch.Tensor) -> torch.Tensor:
+    """The templates [8, 64, 64] re-laid as [64, 64, 8] for the attention kernel (the reference's `paired_templates`,
+    model/attention_cuda.py:412-434). Paired afresh on every call here, on the current stream, so that the op records
+    into CUDA graphs; the network pairs its templates once."""
+    _cuda("pair_templates", templates)
+    if tuple(templates.shape) != (8, 64, 64) or templates.dtype != torch.float16:
+        raise FryError(f"the attention takes 8 fp16 templates of 64 x 64, got {tuple(templates.shape)} {templates.dtype}")
+    templates = templates.contiguous()
+    paired = templates.new_empty(64, 64, 8)
+    library().fry_pair_templates(_ptr(templates), _ptr(paired), 8, _stream(templates))
+    return paired
 
 
 @template_attention.register_fake

@@ -66,11 +66,16 @@ int fry_mix_norm_quant(const uint16_t* x, const uint16_t* original, const uint16
  * then int8 rows q[M, width] and scale[M]. width a multiple of 32 up to 1024, hidden a multiple of 8. */
 int fry_rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, void* stream);
 
+/* `paired_templates` (model/attention_cuda.py:412-434): the position templates fp16 [8, 64, 64] re-laid as
+ * paired [64, 64, 8] (paired[i][j][t] = templates[t][i][j]), the operand fry_template_attention reads. Run it once per
+ * set of templates (the reference caches its pairing per tensor). */
+int fry_pair_templates(const uint16_t* templates, uint16_t* paired, int templates_count, void* stream);
+
 /* `chess::template_attention` (model/fused_blocks.py:104-171; model/attention_cuda.py:444-461): projected [B, 70, W] fp16
- * with W = heads*dq + kv_heads*dq + kv_heads*dv + heads*templates_count (q | k | v | template mix), templates fp16
- * [templates_count, 64, 64], q_gain and k_gain fp16 [dq] -> out [B, 70, heads*dv] fp16. Takes dv 32, 8 templates, even
- * dq up to 32, heads/kv_heads groups that fit 8 query heads a CTA. */
-int fry_template_attention(const uint16_t* projected, const uint16_t* templates, const uint16_t* q_gain, const uint16_t* k_gain,
+ * with W = heads*dq + kv_heads*dq + kv_heads*dv + heads*templates_count (q | k | v | template mix), paired_templates from
+ * fry_pair_templates, q_gain and k_gain fp16 [dq] -> out [B, 70, heads*dv] fp16. Takes dv 32, 8 templates, dq a multiple
+ * of 8 up to 32, heads/kv_heads groups that fit 8 query heads a CTA. */
+int fry_template_attention(const uint16_t* projected, const uint16_t* paired_templates, const uint16_t* q_gain, const uint16_t* k_gain,
                            uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps, void* stream);
 
 /* `chess::linear` (model/fused_blocks.py:308-313, kernel :229-304) for fp16 inputs: out[M, N] = (x[M, K] . weight^T + bias)
@@ -138,7 +143,7 @@ typedef struct FryNetwork {
     const uint16_t* embed;      /* fp16 [81, D], times 1/16 */
     const uint16_t* position;   /* fp16 [70, D], times 1/16 */
     const uint16_t* table;      /* fp16 [1735, D], times 1/16 */
-    const uint16_t* templates;  /* fp16 [templates_count, 64, 64] */
+    const uint16_t* templates;  /* fp16 [64, 64, 8]: the position templates paired by fry_pair_templates */
     const FryBlock* blocks;     /* [layers], host memory */
     FryHeads head_weights;      /* the heads' weights */
 } FryNetwork;
