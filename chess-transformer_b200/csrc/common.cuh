@@ -9,8 +9,8 @@
 #include <stdint.h>
 
 #include <mutex>
-#include <set>
-#include <tuple>
+#include <map>
+#include <utility>
 
 #define FRY_DEVICE __device__ __forceinline__
 
@@ -211,17 +211,20 @@ FRY_DEVICE float h2f(__half h) { return __half2float(h); }
 FRY_DEVICE float h2f_bits(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
 FRY_DEVICE uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
-// Raises a kernel's dynamic shared memory limit once per (kernel, device, size); safe from several host threads.
+// Raises a kernel's dynamic shared memory limit on the current device to at least `bytes` (it is never lowered, so
+// launches of other sizes keep working); safe from several host threads.
 inline cudaError_t ensure_smem(const void* kernel, int bytes) {
     static std::mutex mutex;
-    static std::set<std::tuple<const void*, int, int>> done;
+    static std::map<std::pair<const void*, int>, int> raised;
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return status;
+    if (bytes <= 48 * 1024) return cudaSuccess;
     std::lock_guard<std::mutex> lock(mutex);
-    if (done.count({kernel, device, bytes})) return cudaSuccess;
+    int& current = raised[{kernel, device}];
+    if (bytes <= current) return cudaSuccess;
     status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (status == cudaSuccess) done.insert({kernel, device, bytes});
+    if (status == cudaSuccess) current = bytes;
     return status;
 }
 

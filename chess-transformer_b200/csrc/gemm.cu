@@ -5,10 +5,13 @@
 //  kind::f16 (fp16 x fp16 -> fp32 in TMEM): `linear` (model/fused_blocks.py:229-318): attention-out (combine_heads,
 //            + bias + residual, fp16 out) and the policy head's `a` matmul (+ bias, fp32 out).
 //
-// One CTA computes one 128 x BN output tile. Warp 4 streams 128-byte-wide K slices of A and B into a ring of shared
-// memory stages with TMA (128-byte swizzle); warp 5 issues tcgen05.mma from one elected thread and frees each stage with
-// tcgen05.commit; warps 0-3 wait for the accumulator, read it with tcgen05.ld (one TMEM lane = one output row per
-// thread) and apply the epilogue in the reference's op order (model/int8_cuda.py:163-178). No TMA load multicasts.
+// A persistent CTA per SM walks its share of the 128 x BN output tiles (tile = blockIdx.x, += gridDim.x). Warp 8 streams
+// 128-byte-wide K slices of A and B into a ring of shared-memory stages with TMA (128-byte swizzle), running on into
+// the next tile; warp 9 issues tcgen05.mma from one elected thread into one of two TMEM accumulators, frees each stage
+// with tcgen05.commit and hands the finished accumulator to the epilogue; warps 0-7 read it with tcgen05.ld (warp w owns
+// TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread, and every other 16-column chunk) and apply the epilogue
+// in the reference's op order (model/int8_cuda.py:163-178), while the MMAs of the next tile fill the other accumulator.
+// No TMA load multicasts.
 #include <mutex>
 #include <string>
 
@@ -19,7 +22,9 @@ namespace fry {
 
 constexpr int kBlockM = 128;
 constexpr int kTileKBytes = 128;  // one swizzle row: the K bytes a stage holds
-constexpr int kGemmThreads = 192;
+constexpr int kEpilogueWarps = 8;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kGemmThreads = 320;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
 
 template <int KIND, int BN, bool GATED>
@@ -31,8 +36,9 @@ struct GemmShape {
     static constexpr int kStageBytes = kABytes + kBBytes * (GATED ? 2 : 1);
     static constexpr int kStagesFit = (200 * 1024) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-    static constexpr int kAccCols = BN * (GATED ? 2 : 1);
-    static constexpr int kTmemCols = kAccCols <= 32 ? 32 : kAccCols <= 64 ? 64 : kAccCols <= 128 ? 128 : kAccCols <= 256 ? 256 : 512;
+    static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
+    static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
+    static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
@@ -124,11 +130,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
     uint64_t* empty = full + S::kStages;
-    uint64_t* acc_full = empty + S::kStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
+    uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * kBlockM, n0 = blockIdx.x * BN;
+    const int n_blocks = (N + BN - 1) / BN;
+    const int tiles = ((M + kBlockM - 1) / kBlockM) * n_blocks;
     const int k_tiles = (K * S::kElem + kTileKBytes - 1) / kTileKBytes;
 
     if (threadIdx.x == 0) {
@@ -136,14 +144,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], kEpilogueWarps);
+        }
         fence_barrier_init();
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, S::kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 4 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         prefetch_tensor_map(&map_a);
         prefetch_tensor_map(&map_b);
     }
@@ -152,48 +163,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         if (elect_one()) {
-            for (int kt = 0; kt < k_tiles; ++kt) {
-                const int s = kt % S::kStages;
-                const uint32_t phase = (kt / S::kStages) & 1;
-                if (!mbar_wait(&empty[s], phase ^ 1, 10)) break;
-                uint8_t* a = smem + s * S::kStageBytes;
-                uint8_t* b = a + S::kABytes;
-                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-                tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
-                tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
-                if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
+                for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+                    const int s = it % S::kStages;
+                    const uint32_t phase = (it / S::kStages) & 1;
+                    if (!mbar_wait(&empty[s], phase ^ 1, 10)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* a = smem + s * S::kStageBytes;
+                    uint8_t* b = a + S::kABytes;
+                    mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+                    tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
+                    tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
+                    if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
+                }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         if (elect_one()) {
             constexpr uint32_t idesc = instr_desc<KIND>(BN);
-            for (int kt = 0; kt < k_tiles; ++kt) {
-                const int s = kt % S::kStages;
-                const uint32_t phase = (kt / S::kStages) & 1;
-                if (!mbar_wait(&full[s], phase, 11)) break;
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+                const int buffer = local & 1;
+                if (!mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)) break;
                 tc_fence_after();
-                const uint32_t a = smem_addr(smem + s * S::kStageBytes);
-                const uint32_t b = a + S::kABytes;
+                const uint32_t accumulator = tmem + buffer * S::kAccCols;
+                for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+                    const int s = it % S::kStages;
+                    const uint32_t phase = (it / S::kStages) & 1;
+                    if (!mbar_wait(&full[s], phase, 12)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_addr(smem + s * S::kStageBytes);
+                    const uint32_t b = a + S::kABytes;
 #pragma unroll
-                for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
-                    const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
-                    const uint32_t accumulate = (kt > 0 || k > 0) ? 1u : 0u;
-                    mma_ss<KIND>(tmem, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
-                    if constexpr (GATED) mma_ss<KIND>(tmem + BN, da, smem_desc_sw128(b + S::kBBytes + k * kMmaKBytes), idesc, accumulate);
+                    for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
+                        const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
+                        const uint32_t accumulate = (kt > 0 || k > 0) ? 1u : 0u;
+                        mma_ss<KIND>(accumulator, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
+                        if constexpr (GATED)
+                            mma_ss<KIND>(accumulator + BN, da, smem_desc_sw128(b + S::kBBytes + k * kMmaKBytes), idesc, accumulate);
+                    }
+                    mma_commit(&empty[s]);
                 }
-                mma_commit(&empty[s]);
+                mma_commit(&tmem_full[buffer]);
             }
-            mma_commit(acc_full);
         }
     } else {
-        // warps 0-3: TMEM lanes 32w..32w+31 are rows m0 + 32w + lane
-        if (mbar_wait(acc_full, 0, 12)) {
+        // warps 0-7: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks c
+        // with (c / 16) % 2 == w / 4
+        const int quarter = warp & 3, half = warp >> 2;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int buffer = local & 1;
+            if (!mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) break;
             tc_fence_after();
-            const int m = m0 + warp * 32 + lane;
-            const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-            for (int c = 0; c < BN; c += 16) {
+            const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
+            const int m = m0 + quarter * 32 + lane;
+            const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int c = half * 16; c < BN; c += 32) {
                 if (n0 + c >= N) break;  // uniform across the warp
                 uint32_t acc[16], up[16];
                 tmem_load16(lane_base + c, acc);
@@ -201,6 +238,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tmem_load_wait();
                 if (m < M) epilogue16<EPI>(args, m, n0 + c, N, acc, up);
             }
+            // this warp's reads of the accumulator are complete: the MMA warp may fill it again
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
         }
     }
     tc_fence_before();
@@ -260,30 +301,42 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
     CUtensorMap map_a, map_b;
     if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error) || !make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error))
         return cudaErrorInvalidValue;
-    const dim3 grid((N + BN - 1) / BN, (M + kBlockM - 1) / kBlockM);
-    kernel<<<grid, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, args, M, N, K);
+    const int tiles = ((M + kBlockM - 1) / kBlockM) * ((N + BN - 1) / BN);
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    kernel<<<tiles < multiprocessors ? tiles : multiprocessors, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, args, M, N, K);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 128 everywhere else.
+// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 256 the 768-wide outputs (down,
+// attention-out); 128 everywhere else (gate_up's 128 columns hold 256 accumulators, its gate and its up).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
+    const bool wide = N % 256 == 0;
     if (kind == 0) {
         switch (epilogue) {
             case kEpiBias:
                 return N % 144 == 0 ? launch<0, 144, false, kEpiBias>(a, b, args, M, N, K, stream, error)
                                     : launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
             case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
-            case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
-            case kEpiMix: return launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
+            case kEpiResidual:
+                return wide ? launch<0, 256, false, kEpiResidual>(a, b, args, M, N, K, stream, error)
+                            : launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
+            case kEpiMix:
+                return wide ? launch<0, 256, false, kEpiMix>(a, b, args, M, N, K, stream, error)
+                            : launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {
         switch (epilogue) {
-            case kEpiLinearF16: return launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF16:
+                return wide ? launch<1, 256, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error)
+                            : launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
