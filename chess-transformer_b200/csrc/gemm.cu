@@ -27,28 +27,76 @@ constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kGemmThreads = 320;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
 
-template <int KIND, int BN, bool GATED>
+template <int KIND, int BN, bool GATED, int EPI>
 struct GemmShape {
     static constexpr int kElem = KIND == 0 ? 1 : 2;
     static constexpr int kBoxK = kTileKBytes / kElem;
     static constexpr int kABytes = kBlockM * kTileKBytes;
     static constexpr int kBBytes = BN * kTileKBytes;
     static constexpr int kStageBytes = kABytes + kBBytes * (GATED ? 2 : 1);
-    static constexpr int kStagesFit = (200 * 1024) / kStageBytes;
+    // the epilogue's row operands (residual, and original when mixing) for the tile, one padded row per output row
+    static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
+    static constexpr int kRowStride = BN + 8;  // halves: 16-byte accesses of 8 consecutive rows fall in distinct banks
+    static constexpr int kRowBytes = kRowTensors * kBlockM * kRowStride * 2;
+    static constexpr int kStagesFit = (200 * 1024 - kRowBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+    static_assert(kStages >= 2, "at least two pipeline stages");
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kRowBytes + 1024 + 256;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
 
-// Applies the epilogue to 16 consecutive columns [n, n + 16) of one row m; acc holds the raw TMEM words.
+FRY_DEVICE void cp_async16(void* smem, const void* global) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(global) : "memory");
+}
+FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+FRY_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Starts the copies of one output row's residual (and original) for this thread's chunks of the tile into its shared
+// row buffers; every 16-byte piece is copied by the thread that reads it, so no barrier is needed, only the wait.
+template <int EPI, int BN>
+FRY_DEVICE void copy_tile_rows(const GemmArgs& p, uint16_t* residual_row, uint16_t* original_row, int m, int n0, int c0, int N) {
+    const bool has_residual = EPI == kEpiResidual || EPI == kEpiMix || (EPI == kEpiLinearF16 && p.residual != nullptr);
+    if (!has_residual) return;
+    for (int c = c0; c < BN && n0 + c < N; c += 32) {
+        const size_t offset = static_cast<size_t>(m) * N + n0 + c;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (n0 + c + 8 * h >= N) break;
+            cp_async16(residual_row + c + 8 * h, p.residual + offset + 8 * h);
+            if constexpr (EPI == kEpiMix) cp_async16(original_row + c + 8 * h, p.original + offset + 8 * h);
+        }
+    }
+    cp_async_commit();
+}
+
+// 16 consecutive fp32 column operands from [from, from + valid), zero past valid (valid is 8 or 16).
+FRY_DEVICE void load16f(const float* from, int valid, float (&to)[16]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 v = q * 4 < valid ? *reinterpret_cast<const float4*>(from + 4 * q) : make_float4(0, 0, 0, 0);
+        to[4 * q] = v.x, to[4 * q + 1] = v.y, to[4 * q + 2] = v.z, to[4 * q + 3] = v.w;
+    }
+}
+FRY_DEVICE void load16h(const uint16_t* from, int valid, float (&to)[16]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint4 v = h * 8 < valid ? *reinterpret_cast<const uint4*>(from + 8 * h) : make_uint4(0, 0, 0, 0);
+        const uint16_t* halves = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) to[8 * h + i] = h2f_bits(halves[i]);
+    }
+}
+
+// Applies the epilogue to 16 consecutive columns [n, n + valid) of one row (row = m * N + n); acc holds the raw TMEM
+// words, xs the row's activation scale, rs and is the next block's input-mix scales; residual_chunk and original_chunk
+// point at the chunk's 16 halves in shared memory.
 template <int EPI>
-FRY_DEVICE void epilogue16(const GemmArgs& p, int m, int n, int N, const uint32_t (&acc)[16], const uint32_t (&up)[16]) {
-    const size_t row = static_cast<size_t>(m) * N + n;
-    const int valid = N - n >= 16 ? 16 : N - n;  // 8 or 16: N is a multiple of 8
+FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int n, int N, int valid, float xs, float rs, float is, const uint32_t (&acc)[16],
+                           const uint32_t (&up)[16], const uint16_t* residual_chunk, const uint16_t* original_chunk) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -57,59 +105,63 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, int m, int n, int N, const uint32_
                 reinterpret_cast<int4*>(out)[v] = make_int4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
         return;
     } else if constexpr (EPI == kEpiLinearF32) {
+        float bias[16] = {};
+        if (p.bias_f32) load16f(p.bias_f32 + n, valid, bias);
         float* out = static_cast<float*>(p.out) + row;
-        float v[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(acc[e]) + (p.bias_f32 ? p.bias_f32[n + e < N ? n + e : N - 1] : 0.0f);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            if (q * 4 < valid) reinterpret_cast<float4*>(out)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            if (q * 4 < valid)
+                reinterpret_cast<float4*>(out)[q] =
+                    make_float4(__fadd_rn(__uint_as_float(acc[4 * q]), bias[4 * q]), __fadd_rn(__uint_as_float(acc[4 * q + 1]), bias[4 * q + 1]),
+                                __fadd_rn(__uint_as_float(acc[4 * q + 2]), bias[4 * q + 2]),
+                                __fadd_rn(__uint_as_float(acc[4 * q + 3]), bias[4 * q + 3]));
         return;
     } else {
-        uint16_t res[16], orig[16];
+        float ws[16], second[16];
+        if constexpr (EPI != kEpiLinearF16) load16f(p.w_scale + n, valid, ws);
+        if constexpr (EPI == kEpiGated) load16f(p.w_scale + N + n, valid, second);                       // up's scales
+        if constexpr (EPI == kEpiBias || EPI == kEpiLinearF16) {
+            if (p.bias) load16h(p.bias + n, valid, second);                                              // the bias
+            else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) second[e] = 0.0f;
+            }
+        }
+        uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if constexpr (EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16) {
             if (EPI != kEpiLinearF16 || p.residual != nullptr) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
-                    if (h * 8 < valid) *reinterpret_cast<uint4*>(res + 8 * h) = *reinterpret_cast<const uint4*>(p.residual + row + 8 * h);
+                    if (h * 8 < valid) residual_words[h] = *reinterpret_cast<const uint4*>(residual_chunk + 8 * h);
             }
         }
         if constexpr (EPI == kEpiMix) {
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-                if (h * 8 < valid) *reinterpret_cast<uint4*>(orig + 8 * h) = *reinterpret_cast<const uint4*>(p.original + row + 8 * h);
+                if (h * 8 < valid) original_words[h] = *reinterpret_cast<const uint4*>(original_chunk + 8 * h);
         }
-        float xs = 0.0f;
-        if constexpr (EPI <= kEpiMix) xs = p.x_scale[m];
-        float rs = 0.0f, is = 0.0f;
-        if constexpr (EPI == kEpiMix) {
-            rs = h2f_bits(*p.residual_scale);
-            is = h2f_bits(*p.input_scale);
-        }
+        const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
+        const uint16_t* orig = reinterpret_cast<const uint16_t*>(original_words);
         uint16_t result[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-            const int col = n + e < N ? n + e : N - 1;
             float value;
             if constexpr (EPI == kEpiBias) {
-                value = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs);
-                value = __fmaf_rn(value, p.w_scale[col], p.bias ? h2f_bits(p.bias[col]) : 0.0f);
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e], second[e]);
             } else if constexpr (EPI == kEpiGated) {
-                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), p.w_scale[col]);
-                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), p.w_scale[N + col]);
+                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e]);
+                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), second[e]);
                 // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
                 const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
                 value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
-                value = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs);
-                value = __fmaf_rn(value, p.w_scale[col], h2f_bits(res[e]));
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e], h2f_bits(res[e]));
                 if constexpr (EPI == kEpiMix) {
                     const float stream = __half2float(__float2half_rn(value));
                     value = __fmaf_rn(stream, rs, __fmul_rn(h2f_bits(orig[e]), is));
                 }
             } else {  // kEpiLinearF16: (acc + bias) + residual
-                value = __uint_as_float(acc[e]);
-                if (p.bias) value = __fadd_rn(value, h2f_bits(p.bias[col]));
+                value = __fadd_rn(__uint_as_float(acc[e]), second[e]);
                 if (p.residual) value = __fadd_rn(value, h2f_bits(res[e]));
             }
             result[e] = f2h_bits(value);
@@ -125,10 +177,11 @@ template <int KIND, int BN, bool GATED, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmArgs args, int M, int N,
                 int K) {
-    using S = GemmShape<KIND, BN, GATED>;
+    using S = GemmShape<KIND, BN, GATED, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+    uint16_t* row_buffers = reinterpret_cast<uint16_t*>(smem + S::kStages * S::kStageBytes);  // [tensors][128][kRowStride]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRowBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
@@ -222,21 +275,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // warps 0-7: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks c
         // with (c / 16) % 2 == w / 4
         const int quarter = warp & 3, half = warp >> 2;
+        float rs = 0.0f, is = 0.0f;
+        if constexpr (EPI == kEpiMix) {
+            rs = h2f_bits(*args.residual_scale);
+            is = h2f_bits(*args.input_scale);
+        }
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int buffer = local & 1;
-            if (!mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) break;
-            tc_fence_after();
             const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
             const int m = m0 + quarter * 32 + lane;
+            const bool row_ok = m < M;
+            float xs = 0.0f;
+            if constexpr (EPI <= kEpiMix) xs = row_ok ? args.x_scale[m] : 0.0f;
+            // the tile's row operands for this thread's chunks travel while the MMAs finish
+            const int c0 = half * 16;
+            uint16_t* residual_row = row_buffers + (quarter * 32 + lane) * S::kRowStride;
+            uint16_t* original_row = residual_row + kBlockM * S::kRowStride;
+            if constexpr (S::kRowTensors > 0) {
+                if (row_ok) copy_tile_rows<EPI, BN>(args, residual_row, original_row, m, n0, c0, N);
+            }
+            if (!mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) break;
+            if constexpr (S::kRowTensors > 0) cp_async_wait_all();
+            tc_fence_after();
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-            for (int c = half * 16; c < BN; c += 32) {
-                if (n0 + c >= N) break;  // uniform across the warp
-                uint32_t acc[16], up[16];
-                tmem_load16(lane_base + c, acc);
-                if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
+            // two register sets: chunk c's math runs while chunk c + 32's accumulator and rows load
+            uint32_t acc[2][16], up[2][16];
+            if (n0 + c0 < N) {
+                tmem_load16(lane_base + c0, acc[0]);
+                if constexpr (GATED) tmem_load16(lane_base + BN + c0, up[0]);
+            }
+#pragma unroll 2
+            for (int c = c0, set = 0; c < BN && n0 + c < N; c += 32, set ^= 1) {  // uniform across the warp
                 tmem_load_wait();
-                if (m < M) epilogue16<EPI>(args, m, n0 + c, N, acc, up);
+                const int next = c + 32;
+                const bool more = next < BN && n0 + next < N;
+                if (more) {
+                    tmem_load16(lane_base + next, acc[set ^ 1]);
+                    if constexpr (GATED) tmem_load16(lane_base + BN + next, up[set ^ 1]);
+                }
+                const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
+                if (row_ok)
+                    epilogue16<EPI>(args, static_cast<size_t>(m) * N + n0 + c, n0 + c, N, valid, xs, rs, is, acc[set], up[set],
+                                    residual_row + c, original_row + c);
             }
             // this warp's reads of the accumulator are complete: the MMA warp may fill it again
             tc_fence_before();
@@ -294,7 +375,7 @@ bool make_map(CUtensorMap* map, const void* base, int elem_bytes, int k, int row
 
 template <int KIND, int BN, bool GATED, int EPI>
 cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
-    using S = GemmShape<KIND, BN, GATED>;
+    using S = GemmShape<KIND, BN, GATED, EPI>;
     auto kernel = gemm_kernel<KIND, BN, GATED, EPI>;
     const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
     if (attribute != cudaSuccess) return attribute;
@@ -312,8 +393,9 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 
 }  // namespace
 
-// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 256 the 768-wide outputs (down,
-// attention-out); 128 everywhere else (gate_up's 128 columns hold 256 accumulators, its gate and its up).
+// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 256 attention-out (768 wide, one
+// residual row buffer); 128 everywhere else: gate_up's 128 columns hold 256 accumulators (its gate and its up), down keeps
+// two row buffers (residual and original) beside four pipeline stages.
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
     const bool wide = N % 256 == 0;
@@ -323,12 +405,8 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 return N % 144 == 0 ? launch<0, 144, false, kEpiBias>(a, b, args, M, N, K, stream, error)
                                     : launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
             case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
-            case kEpiResidual:
-                return wide ? launch<0, 256, false, kEpiResidual>(a, b, args, M, N, K, stream, error)
-                            : launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
-            case kEpiMix:
-                return wide ? launch<0, 256, false, kEpiMix>(a, b, args, M, N, K, stream, error)
-                            : launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
+            case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
+            case kEpiMix: return launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             default: break;
         }

@@ -8,8 +8,8 @@
 //   value = Linear(GELU(Linear(GELU(board-down) flattened))) ; score = softmax(value) . bin centres.
 //
 // Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel, policy_kernel (per board: the 64x64
-// logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay fp32-exact), hidden_kernel (the eval head's
-// first layer over all boards), value_kernel (second layer, softmax, expected score). fp32 arithmetic throughout, where the
+// logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay fp32-exact), eval_linear_kernel (the eval head's
+// two layers over all boards), expected_score_kernel (softmax times the bin centres). fp32 arithmetic throughout, where the
 // reference uses tf32 matmuls.
 #include <string>
 
@@ -25,7 +25,8 @@ constexpr float kLoScale = 2048.0f;
 size_t heads_workspace_bytes(int B, int D) {
     const size_t M = static_cast<size_t>(B) * kHeadTokens;
     auto up = [](size_t bytes) { return (bytes + 255) / 256 * 256; };
-    return up(M * D * 2) + up(M * D * 4) + up(M * kNarrowStride * 4) + up(static_cast<size_t>(B) * D * 4);
+    // y, a, narrow, then the eval head's hidden units [B, D] and value logits [B, up to 256 bins]
+    return up(M * D * 2) + up(M * D * 4) + up(M * kNarrowStride * 4) + up(static_cast<size_t>(B) * (D + 256) * 4);
 }
 
 // narrow[m, 0..20] = y[m] . N^T + n_bias, 8 warps a CTA, the weights staged in shared memory.
@@ -113,85 +114,72 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 
 FRY_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
-// hidden[b, u] = GELU(h_bias[u] + sum_i W1[u, i] * GELU(narrow[b, i / 16, 5 + i % 16])), 64 boards x 64 units a CTA.
-__global__ void __launch_bounds__(256) hidden_kernel(const float* __restrict__ narrow, const float* __restrict__ weight,
-                                                     const float* __restrict__ bias, float* __restrict__ hidden, int B, int D) {
-    constexpr int TB = 64, TU = 64, TK = 32, INPUTS = kHeadTokens * kDown;
+// The eval head's two layers as one tiled fp32 kernel over all boards, 32 boards x 32 outputs a CTA, 2 x 2 a thread:
+//   FROM_NARROW: out[b, u] = GELU(bias[u] + sum_i W[u, i] * GELU(narrow[b, i / 16, 5 + i % 16]))   (K = 70 x 16)
+//   otherwise:   out[b, u] = bias[u] + sum_i W[u, i] * x[b, i]                                    (K = d)
+template <bool FROM_NARROW>
+__global__ void __launch_bounds__(256) eval_linear_kernel(const float* __restrict__ x, const float* __restrict__ weight,
+                                                          const float* __restrict__ bias, float* __restrict__ out, int B, int K, int N) {
+    constexpr int TB = 32, TU = 32, TK = 32;
     __shared__ float xs[TK][TB + 1];
     __shared__ float ws[TK][TU + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int b0 = blockIdx.y * TB, u0 = blockIdx.x * TU;
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < INPUTS; k0 += TK) {
+    float acc[2][2] = {};
+    for (int k0 = 0; k0 < K; k0 += TK) {
         for (int i = threadIdx.x; i < TK * TB; i += 256) {
             const int kk = i % TK, bb = i / TK, input = k0 + kk, board = b0 + bb;
             float v = 0.0f;
-            if (board < B && input < INPUTS)
-                v = gelu(narrow[(static_cast<size_t>(board) * kHeadTokens + input / kDown) * kNarrowStride + 5 + input % kDown]);
+            if (board < B && input < K) {
+                if constexpr (FROM_NARROW)
+                    v = gelu(x[(static_cast<size_t>(board) * kHeadTokens + input / kDown) * kNarrowStride + 5 + input % kDown]);
+                else
+                    v = x[static_cast<size_t>(board) * K + input];
+            }
             xs[kk][bb] = v;
         }
         for (int i = threadIdx.x; i < TK * TU; i += 256) {
             const int kk = i % TK, uu = i / TK, input = k0 + kk, unit = u0 + uu;
-            ws[kk][uu] = (unit < D && input < INPUTS) ? weight[static_cast<size_t>(unit) * INPUTS + input] : 0.0f;
+            ws[kk][uu] = (unit < N && input < K) ? weight[static_cast<size_t>(unit) * K + input] : 0.0f;
         }
         __syncthreads();
 #pragma unroll 8
         for (int kk = 0; kk < TK; ++kk)
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 2; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xs[kk][ty * 4 + i], ws[kk][tx * 4 + j], acc[i][j]);
+                for (int j = 0; j < 2; ++j) acc[i][j] = __fmaf_rn(xs[kk][ty * 2 + i], ws[kk][tx * 2 + j], acc[i][j]);
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int board = b0 + ty * 4 + i, unit = u0 + tx * 4 + j;
-            if (board < B && unit < D) hidden[static_cast<size_t>(board) * D + unit] = gelu(__fadd_rn(acc[i][j], bias[unit]));
+        for (int j = 0; j < 2; ++j) {
+            const int board = b0 + ty * 2 + i, unit = u0 + tx * 2 + j;
+            if (board < B && unit < N) {
+                const float value = __fadd_rn(acc[i][j], bias[unit]);
+                out[static_cast<size_t>(board) * N + unit] = FROM_NARROW ? gelu(value) : value;
+            }
         }
 }
 
-// One CTA per board: the bins' logits, their softmax and the expected score into the row's last column.
-__global__ void __launch_bounds__(128) value_kernel(const float* __restrict__ hidden, const float* __restrict__ weight,
-                                                    const float* __restrict__ bias, float* __restrict__ rows, int D, int bins) {
-    extern __shared__ float value_smem[];  // hidden row [D], then logits [bins]
-    float* h = value_smem;
-    float* logits = value_smem + D;
-    __shared__ float reduce[3][4];  // per warp: the largest logit, the softmax total, the weighted total
-    const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) h[i] = hidden[static_cast<size_t>(b) * D + i];
-    __syncthreads();
-    for (int bin = threadIdx.x; bin < bins; bin += blockDim.x) {
-        float acc = 0.0f;
-        for (int k = 0; k < D; ++k) acc = __fmaf_rn(h[k], weight[static_cast<size_t>(bin) * D + k], acc);
-        logits[bin] = __fadd_rn(acc, bias[bin]);
-    }
-    __syncthreads();
+// One warp per board: the softmax of its value logits times the bin centres (2i + 1) / 2bins, into the row's last column.
+__global__ void __launch_bounds__(256) expected_score_kernel(const float* __restrict__ logits, float* __restrict__ rows, int B, int bins) {
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (b >= B) return;
+    const float* row = logits + static_cast<size_t>(b) * bins;
     float top = -INFINITY;
-    for (int bin = threadIdx.x; bin < bins; bin += blockDim.x) top = fmaxf(top, logits[bin]);
+    for (int bin = lane; bin < bins; bin += 32) top = fmaxf(top, row[bin]);
     top = warp_max(top);
-    if (lane == 0) reduce[0][warp] = top;
-    __syncthreads();
-    top = fmaxf(fmaxf(reduce[0][0], reduce[0][1]), fmaxf(reduce[0][2], reduce[0][3]));
     float total = 0.0f, weighted = 0.0f;
-    for (int bin = threadIdx.x; bin < bins; bin += blockDim.x) {
-        const float p = expf(__fsub_rn(logits[bin], top));
+    for (int bin = lane; bin < bins; bin += 32) {
+        const float p = expf(__fsub_rn(row[bin], top));
         total = __fadd_rn(total, p);
         weighted = __fmaf_rn(p, __fdiv_rn(static_cast<float>(2 * bin + 1), static_cast<float>(2 * bins)), weighted);
     }
     total = warp_sum(total);
     weighted = warp_sum(weighted);
-    if (lane == 0) {
-        reduce[1][warp] = total;
-        reduce[2][warp] = weighted;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const float all = reduce[1][0] + reduce[1][1] + reduce[1][2] + reduce[1][3];
-        const float sum = reduce[2][0] + reduce[2][1] + reduce[2][2] + reduce[2][3];
-        rows[static_cast<size_t>(b) * (kMoves + 1) + kMoves] = __fdiv_rn(sum, all);
-    }
+    if (lane == 0) rows[static_cast<size_t>(b) * (kMoves + 1) + kMoves] = __fdiv_rn(weighted, total);
 }
 
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
@@ -201,8 +189,8 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
         if (error) *error = "the heads' workspace is smaller than fry_heads_workspace_bytes";
         return cudaErrorInvalidValue;
     }
-    if (D % 16 != 0 || D > 1024) {
-        if (error) *error = "the heads take d_model a multiple of 16 up to 1024";
+    if (D % 16 != 0 || D > 1024 || w.bins < 2 || w.bins > 256) {
+        if (error) *error = "the heads take d_model a multiple of 16 up to 1024 and 2 to 256 value bins";
         return cudaErrorInvalidValue;
     }
     const int M = B * kHeadTokens;
@@ -226,8 +214,12 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     const int narrow_blocks = (M + 31) / 32 < 148 * 4 ? (M + 31) / 32 : 148 * 4;
     narrow_kernel<<<narrow_blocks, 256, narrow_smem, stream>>>(y, w.narrow_weight, w.narrow_bias, narrow, M, D);
     policy_kernel<<<B, 256, 0, stream>>>(a, y, narrow, rows, D);
-    hidden_kernel<<<dim3((D + 63) / 64, (B + 63) / 64), 256, 0, stream>>>(narrow, w.hidden_weight, w.hidden_bias, hidden, B, D);
-    value_kernel<<<B, 128, (D + w.bins) * sizeof(float), stream>>>(hidden, w.out_weight, w.out_bias, rows, D, w.bins);
+    float* value_logits = hidden + static_cast<size_t>(B) * D;
+    eval_linear_kernel<true><<<dim3((D + 31) / 32, (B + 31) / 32), 256, 0, stream>>>(narrow, w.hidden_weight, w.hidden_bias, hidden, B,
+                                                                                      kHeadTokens * kDown, D);
+    eval_linear_kernel<false><<<dim3((w.bins + 31) / 32, (B + 31) / 32), 256, 0, stream>>>(hidden, w.out_weight, w.out_bias, value_logits, B,
+                                                                                          D, w.bins);
+    expected_score_kernel<<<(B + 7) / 8, 256, 0, stream>>>(value_logits, rows, B, w.bins);
     return cudaGetLastError();
 }
 

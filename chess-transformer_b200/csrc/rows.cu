@@ -194,7 +194,7 @@ FRY_DEVICE int code_at(const int* codes, int file, int rank) {
     return (file >= 0 && file < 8 && rank >= 0 && rank < 8) ? codes[rank * 8 + file] : kEdge;
 }
 
-// One CTA per board: the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
+// One CTA per (board, 256 columns): the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
 __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ boards, const uint16_t* __restrict__ embed,
                                                         const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
                                                         uint16_t* __restrict__ out, int D) {
@@ -266,9 +266,11 @@ __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restric
         }
     }
     __syncthreads();
-    const int vectors = D / 8;
+    // this CTA's slice of the columns: [blockIdx.y * 256, + 256)
+    const int first = blockIdx.y * 256, width = D - first < 256 ? D - first : 256;
+    const int vectors = width / 8;
     for (int idx = tid; idx < kTokens * vectors; idx += blockDim.x) {
-        const int t = idx / vectors, col = (idx % vectors) * 8;
+        const int t = idx / vectors, col = first + (idx % vectors) * 8;
         float e[8], p[8];
         unpack8(*reinterpret_cast<const uint4*>(embed + static_cast<size_t>(codes[t]) * D + col), e);
         unpack8(*reinterpret_cast<const uint4*>(position + static_cast<size_t>(t) * D + col), p);
@@ -337,7 +339,7 @@ cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const 
                             uint16_t* out, int B, int D, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
     if (D % 8 != 0) return cudaErrorInvalidValue;
-    embedding_kernel<<<B, 256, 0, stream>>>(boards, embed, position, table, out, D);
+    embedding_kernel<<<dim3(B, (D + 255) / 256), 256, 0, stream>>>(boards, embed, position, table, out, D);
     return cudaGetLastError();
 }
 
