@@ -24,7 +24,8 @@
 namespace fry {
 
 constexpr int kAttnTokens = 70, kAttnSquares = 64, kAttnKeys = 80, kAttnDv = 32, kAttnTemplates = 8, kMaxHeadsPerCta = 8;
-constexpr int kSlab = 16, kBiasRow = 72, kValueRow = 40;
+// a head's bias slab is 16 rows of 72 halves plus 8: its stores from 8 heads at once fall in distinct banks
+constexpr int kSlab = 16, kBiasRow = 72, kBiasHead = kSlab * kBiasRow + 8, kValueRow = 40;
 
 FRY_DEVICE void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -55,7 +56,7 @@ __global__ void pair_templates_kernel(const uint16_t* __restrict__ templates, ui
     *reinterpret_cast<uint4*>(paired + index * kAttnTemplates) = *reinterpret_cast<const uint4*>(row);
 }
 
-// The template bias of square rows [16 * slab, 16 * slab + 16) for the CTA's heads into bias [head][16][kBiasRow] (fp16).
+// The template bias of square rows [16 * slab, 16 * slab + 16) for the CTA's heads into bias [head][kBiasHead] (fp16).
 FRY_DEVICE void make_bias_slab(uint16_t* bias, const uint16_t* board, const uint16_t* paired, int slab, int width, int c_offset,
                                int first_head, int heads_here, int warp, int warps, int g, int t) {
     for (int pair = warp; pair < kSlab / 2; pair += warps) {
@@ -73,7 +74,7 @@ FRY_DEVICE void make_bias_slab(uint16_t* bias, const uint16_t* board, const uint
             mma_f16(c, a0, 0u, 0u, a3, *reinterpret_cast<const uint32_t*>(t0 + j * 8 * kAttnTemplates),
                     *reinterpret_cast<const uint32_t*>(t1 + j * 8 * kAttnTemplates));
             if (g < heads_here) {
-                uint16_t* to = bias + (g * kSlab + 2 * pair) * kBiasRow + j * 8 + 2 * t;
+                uint16_t* to = bias + g * kBiasHead + 2 * pair * kBiasRow + j * 8 + 2 * t;
                 *reinterpret_cast<uint32_t*>(to) = pack_half2(c[0], c[1]);
                 *reinterpret_cast<uint32_t*>(to + kBiasRow) = pack_half2(c[2], c[3]);
             }
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     uint16_t* keys = attn_smem;                                   // [kv_here][80][KROW]
     uint16_t* values = keys + kv_here * kAttnKeys * KROW;         // [kv_here][80][kValueRow]
     uint16_t* bias = values + kv_here * kAttnKeys * kValueRow;    // [2][heads_here][16][kBiasRow]
-    const int slab_size = heads_here * kSlab * kBiasRow;
+    const int slab_size = heads_here * kBiasHead;
 
     const int b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int width = (heads + kv_heads) * dq + kv_heads * kAttnDv + heads * kAttnTemplates;
@@ -209,9 +210,11 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
                     a[ks][r + 2 * half] = pack_half2(__fmul_rn(__fmul_rn(low_half(raw_q[ks][r][half]), inverse), qg[ks][half][0]),
                                                      __fmul_rn(__fmul_rn(high_half(raw_q[ks][r][half]), inverse), qg[ks][half][1]));
         }
-        float s[10][4];
+        // scores over the 9 key tiles that hold real keys (keys 72-79 never exist: their probabilities are 0)
+        constexpr int kTiles = 9;
+        float s[kTiles][4];
 #pragma unroll
-        for (int j = 0; j < 10; ++j) {
+        for (int j = 0; j < kTiles; ++j) {
             s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
             const uint16_t* key_row = kv_keys + (j * 8 + g) * KROW + 2 * t;
 #pragma unroll
@@ -219,42 +222,48 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
                 mma_f16(s[j], a[ks][0], a[ks][1], a[ks][2], a[ks][3], *reinterpret_cast<const uint32_t*>(key_row + ks * 16),
                         *reinterpret_cast<const uint32_t*>(key_row + ks * 16 + 8));
         }
-        const uint16_t* head_bias = bias + (phase & 1) * slab_size + warp * kSlab * kBiasRow;
+        // s * scale + bias (the bias on the square block only), keys 70 and 71 masked
+        const uint16_t* head_bias = bias + (phase & 1) * slab_size + warp * kBiasHead;
         float top[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int j = 0; j < 10; ++j)
+        for (int j = 0; j < kTiles; ++j)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 uint32_t pair = 0u;
                 if (squares_phase && j < 8) pair = *reinterpret_cast<const uint32_t*>(head_bias + (g + 8 * r) * kBiasRow + j * 8 + 2 * t);
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    float value = __fadd_rn(__fmul_rn(s[j][2 * r + e], scale), e ? high_half(pair) : low_half(pair));
-                    if (j * 8 + 2 * t + e >= kAttnTokens) value = -INFINITY;
+                    float value = __fmaf_rn(s[j][2 * r + e], scale, e ? high_half(pair) : low_half(pair));
+                    if (j == kTiles - 1 && 2 * t + e >= kAttnTokens - 64) value = -INFINITY;
                     s[j][2 * r + e] = value;
                     top[r] = fmaxf(top[r], value);
                 }
             }
-        float total[2] = {0.0f, 0.0f};
+        float total[2] = {0.0f, 0.0f}, shift[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) top[r] = quad_max(top[r]);
+        for (int r = 0; r < 2; ++r) {
+            top[r] = quad_max(top[r]);
+            shift[r] = -top[r] * 1.4426950408889634f;
+        }
 #pragma unroll
-        for (int j = 0; j < 10; ++j)
+        for (int j = 0; j < kTiles; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float p = ex2_approx(__fmul_rn(__fsub_rn(s[j][e], top[e >> 1]), 1.4426950408889634f));
+                const float p = ex2_approx(__fmaf_rn(s[j][e], 1.4426950408889634f, shift[e >> 1]));  // e^(s - top)
                 s[j][e] = p;
                 total[e >> 1] = __fadd_rn(total[e >> 1], p);
             }
+        float inverse[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) total[r] = quad_sum(total[r]);
+        for (int r = 0; r < 2; ++r) inverse[r] = __frcp_rn(quad_sum(total[r]));
         float o[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < 5; ++kk) {
             const uint32_t p0 = pack_half2(s[2 * kk][0], s[2 * kk][1]), p1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
-            const uint32_t p2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]), p3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+            const uint32_t p2 = 2 * kk + 1 < kTiles ? pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]) : 0u;
+            const uint32_t p3 = 2 * kk + 1 < kTiles ? pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]) : 0u;
 #pragma unroll
             for (int n = 0; n < 4; n += 2) {
                 const uint16_t* rows = kv_values + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kValueRow + n * 8 + (lane >> 4) * 8;
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             uint16_t* to = out + (static_cast<size_t>(b) * kAttnTokens + row) * (heads * kAttnDv) + head * kAttnDv + 2 * t;
 #pragma unroll
             for (int n = 0; n < 4; ++n)
-                *reinterpret_cast<uint32_t*>(to + n * 8) = pack_half2(__fdiv_rn(o[n][2 * r], total[r]), __fdiv_rn(o[n][2 * r + 1], total[r]));
+                *reinterpret_cast<uint32_t*>(to + n * 8) = pack_half2(__fmul_rn(o[n][2 * r], inverse[r]), __fmul_rn(o[n][2 * r + 1], inverse[r]));
         }
         if (phase + 1 < 5) {
 #pragma unroll
@@ -312,7 +321,7 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     const dim3 grid(heads / per_cta, B);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
-                          2 * static_cast<size_t>(per_cta) * kSlab * kBiasRow) * sizeof(uint16_t);
+                          2 * static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
     if (dqp == 16) {
         const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<16>), static_cast<int>(bytes));
         if (attribute != cudaSuccess) return attribute;
