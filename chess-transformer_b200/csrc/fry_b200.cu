@@ -5,3 +5,4 @@
 #include "attention.cu"
 #include "heads.cu"
 #include "abi.cu"
+#include "noalloc.cu"

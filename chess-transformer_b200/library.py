@@ -52,6 +52,7 @@ SIGNATURES = {
     "fry_board_embedding": ([_ptr] * 5 + [_c_int, _c_int, _ptr], _c_int),
     "fry_heads_workspace_bytes": ([_c_int, _c_int], _size),
     "fry_heads": ([_ptr, ctypes.POINTER(FryHeads), _c_float, _ptr, _ptr, _size, _c_int, _c_int, _ptr], _c_int),
+    "fry_heads_noalloc": ([_ptr, ctypes.POINTER(FryHeads), _c_float, _ptr, _c_int, _c_int, _ptr], _c_int),
     "fry_forward_workspace_bytes": ([ctypes.POINTER(FryNetwork), _c_int], _size),
     "fry_forward": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
 }

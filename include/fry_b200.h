@@ -112,6 +112,19 @@ size_t fry_heads_workspace_bytes(int B, int D);
 int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
               int D, void* stream);
 
+/* fry_heads without a workspace, for callers that cannot allocate device memory when they evaluate positions (a
+ * thread in the middle of a stream capture, where cudaMalloc is not allowed; a latency-bound search loop that must not
+ * risk the device-wide synchronisation an allocation can cause; a host in another language with no device allocator).
+ * No counterpart in the reference: its heads always allocate through torch.
+ * The scratch is a fixed array inside the library (about 5.1 MiB, held by every GPU that loads the library until
+ * exit), so a call takes at most FRY_HEADS_NOALLOC_MAX_BOARDS boards of d_model up to FRY_HEADS_NOALLOC_MAX_D_MODEL;
+ * larger calls return FRY_ERROR_SHAPE before anything is enqueued. All calls on a device share the array, which keeps
+ * the last call's contents: calls whose work overlaps on the GPU race and must be ordered by the caller. The first call
+ * on a device looks up the array's device address; make it before any stream capture on that device. */
+#define FRY_HEADS_NOALLOC_MAX_BOARDS 16
+#define FRY_HEADS_NOALLOC_MAX_D_MODEL 768
+int fry_heads_noalloc(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, int B, int D, void* stream);
+
 /* ---- the whole forward ------------------------------------------------------------------------------------------- */
 
 /* One int8 block as `Int8Block` holds it (model/int8_blocks.py:254-272) with the layout of engine/quantization.py:129-139. */
