@@ -5,12 +5,14 @@
 //  kind::f16 (fp16 x fp16 -> fp32 in TMEM): `linear` (model/fused_blocks.py:229-318): attention-out (combine_heads,
 //            + bias + residual, fp16 out) and the policy head's `a` matmul (+ bias, fp32 out).
 //
-// A persistent CTA per SM walks its share of the 128 x BN output tiles (tile = blockIdx.x, += gridDim.x). Warp 8 streams
-// 128-byte-wide K slices of A and B into a ring of shared-memory stages with TMA (128-byte swizzle), running on into
-// the next tile; warp 9 issues tcgen05.mma from one elected thread into one of two TMEM accumulators, frees each stage
-// with tcgen05.commit and hands the finished accumulator to the epilogue; warps 0-7 read it with tcgen05.ld (warp w owns
-// TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread, and every other 16-column chunk) and apply the epilogue
-// in the reference's op order (model/int8_cuda.py:163-178), while the MMAs of the next tile fill the other accumulator.
+// A persistent CTA per SM walks its share of the 128 x BN output tiles (tile = blockIdx.x, += gridDim.x). Warp 16
+// streams 128-byte-wide K slices of A and B into a ring of shared-memory stages with TMA (128-byte swizzle), running on
+// into the next tile; warp 17 issues tcgen05.mma from one elected thread into one of two TMEM accumulators, frees each
+// stage with tcgen05.commit and hands the finished accumulator to the epilogue. Warps 0-15 are the epilogue: warp w reads
+// TMEM lanes 32 (w % 4) .. +31 (one output row per thread) and every fourth 16-column chunk, starting at chunk w / 4, with
+// tcgen05.ld, and applies the epilogue in the reference's op order (model/int8_cuda.py:163-178) while the MMAs of the
+// next tile fill the other accumulator. A tile's column operands (weight scales, bias) are staged once in shared memory;
+// its row operands (residual, original) are copied by each thread for its own row with cp.async while the MMAs run.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
@@ -22,10 +24,13 @@ namespace fry {
 
 constexpr int kBlockM = 128;
 constexpr int kTileKBytes = 128;  // one swizzle row: the K bytes a stage holds
-constexpr int kEpilogueWarps = 8;
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
-constexpr int kGemmThreads = 320;
+constexpr int kEpilogueWarps = 16;
+constexpr int kEpilogueThreads = kEpilogueWarps * 32;
+constexpr int kChunkParts = kEpilogueWarps / 4;  // warps sharing one TMEM lane quarter, each taking every kChunkParts-th chunk
+constexpr int kProducerWarp = kEpilogueWarps, kMmaWarp = kEpilogueWarps + 1;
+constexpr int kGemmThreads = (kEpilogueWarps + 2) * 32;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
+constexpr int kEpilogueBarrier = 1;  // named barrier of the epilogue warps (0 is __syncthreads)
 
 template <int KIND, int BN, bool GATED, int EPI>
 struct GemmShape {
@@ -38,13 +43,15 @@ struct GemmShape {
     static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
     static constexpr int kRowStride = BN + 8;  // halves: 16-byte accesses of 8 consecutive rows fall in distinct banks
     static constexpr int kRowBytes = kRowTensors * kBlockM * kRowStride * 2;
-    static constexpr int kStagesFit = (200 * 1024 - kRowBytes) / kStageBytes;
+    // the tile's column operands, double-buffered by tile: [2][3][BN] floats (weight scales, up's scales or the bias)
+    static constexpr int kColumnBytes = 2 * 3 * BN * 4;
+    static constexpr int kStagesFit = (200 * 1024 - kRowBytes - kColumnBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kStages * kStageBytes + kRowBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kRowBytes + kColumnBytes + 1024 + 256;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
@@ -54,6 +61,7 @@ FRY_DEVICE void cp_async16(void* smem, const void* global) {
 }
 FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 FRY_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads) : "memory"); }
 
 // Starts the copies of one output row's residual (and original) for this thread's chunks of the tile into its shared
 // row buffers; every 16-byte piece is copied by the thread that reads it, so no barrier is needed, only the wait.
@@ -61,7 +69,7 @@ template <int EPI, int BN>
 FRY_DEVICE void copy_tile_rows(const GemmArgs& p, uint16_t* residual_row, uint16_t* original_row, int m, int n0, int c0, int N) {
     const bool has_residual = EPI == kEpiResidual || EPI == kEpiMix || (EPI == kEpiLinearF16 && p.residual != nullptr);
     if (!has_residual) return;
-    for (int c = c0; c < BN && n0 + c < N; c += 32) {
+    for (int c = c0; c < BN && n0 + c < N; c += 16 * kChunkParts) {
         const size_t offset = static_cast<size_t>(m) * N + n0 + c;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -73,30 +81,30 @@ FRY_DEVICE void copy_tile_rows(const GemmArgs& p, uint16_t* residual_row, uint16
     cp_async_commit();
 }
 
-// 16 consecutive fp32 column operands from [from, from + valid), zero past valid (valid is 8 or 16).
-FRY_DEVICE void load16f(const float* from, int valid, float (&to)[16]) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 v = q * 4 < valid ? *reinterpret_cast<const float4*>(from + 4 * q) : make_float4(0, 0, 0, 0);
-        to[4 * q] = v.x, to[4 * q + 1] = v.y, to[4 * q + 2] = v.z, to[4 * q + 3] = v.w;
-    }
-}
-FRY_DEVICE void load16h(const uint16_t* from, int valid, float (&to)[16]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint4 v = h * 8 < valid ? *reinterpret_cast<const uint4*>(from + 8 * h) : make_uint4(0, 0, 0, 0);
-        const uint16_t* halves = reinterpret_cast<const uint16_t*>(&v);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) to[8 * h + i] = h2f_bits(halves[i]);
+// The tile's column operands into shared memory (all epilogue threads together): columns[0] the weight scales,
+// columns[1] up's scales (gated) or the bias as floats, zero past N.
+template <int EPI, int BN>
+FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, int tid) {
+    for (int i = tid; i < BN; i += kEpilogueThreads) {
+        const int n = n0 + i;
+        const bool ok = n < N;
+        float scale = 0.0f, second = 0.0f;
+        if constexpr (EPI <= kEpiMix) scale = ok ? p.w_scale[n] : 0.0f;
+        if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
+        if constexpr (EPI == kEpiBias || EPI == kEpiLinearF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
+        if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
+        columns[i] = scale;
+        columns[BN + i] = second;
     }
 }
 
 // Applies the epilogue to 16 consecutive columns [n, n + valid) of one row (row = m * N + n); acc holds the raw TMEM
-// words, xs the row's activation scale, rs and is the next block's input-mix scales; residual_chunk and original_chunk
-// point at the chunk's 16 halves in shared memory.
+// words, xs the row's activation scale, rs and is the next block's input-mix scales; scale and second point at the
+// chunk's column operands in shared memory, residual_chunk and original_chunk at its row operands.
 template <int EPI>
-FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int n, int N, int valid, float xs, float rs, float is, const uint32_t (&acc)[16],
-                           const uint32_t (&up)[16], const uint16_t* residual_chunk, const uint16_t* original_chunk) {
+FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, float rs, float is, const uint32_t (&acc)[16],
+                           const uint32_t (&up)[16], const float* scale, const float* second, const uint16_t* residual_chunk,
+                           const uint16_t* original_chunk) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -105,28 +113,16 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int n, int N, int vali
                 reinterpret_cast<int4*>(out)[v] = make_int4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
         return;
     } else if constexpr (EPI == kEpiLinearF32) {
-        float bias[16] = {};
-        if (p.bias_f32) load16f(p.bias_f32 + n, valid, bias);
         float* out = static_cast<float*>(p.out) + row;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
             if (q * 4 < valid)
                 reinterpret_cast<float4*>(out)[q] =
-                    make_float4(__fadd_rn(__uint_as_float(acc[4 * q]), bias[4 * q]), __fadd_rn(__uint_as_float(acc[4 * q + 1]), bias[4 * q + 1]),
-                                __fadd_rn(__uint_as_float(acc[4 * q + 2]), bias[4 * q + 2]),
-                                __fadd_rn(__uint_as_float(acc[4 * q + 3]), bias[4 * q + 3]));
+                    make_float4(__fadd_rn(__uint_as_float(acc[4 * q]), second[4 * q]), __fadd_rn(__uint_as_float(acc[4 * q + 1]), second[4 * q + 1]),
+                                __fadd_rn(__uint_as_float(acc[4 * q + 2]), second[4 * q + 2]),
+                                __fadd_rn(__uint_as_float(acc[4 * q + 3]), second[4 * q + 3]));
         return;
     } else {
-        float ws[16], second[16];
-        if constexpr (EPI != kEpiLinearF16) load16f(p.w_scale + n, valid, ws);
-        if constexpr (EPI == kEpiGated) load16f(p.w_scale + N + n, valid, second);                       // up's scales
-        if constexpr (EPI == kEpiBias || EPI == kEpiLinearF16) {
-            if (p.bias) load16h(p.bias + n, valid, second);                                              // the bias
-            else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) second[e] = 0.0f;
-            }
-        }
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if constexpr (EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16) {
             if (EPI != kEpiLinearF16 || p.residual != nullptr) {
@@ -147,15 +143,15 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int n, int N, int vali
         for (int e = 0; e < 16; ++e) {
             float value;
             if constexpr (EPI == kEpiBias) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e], second[e]);
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e], second[e]);
             } else if constexpr (EPI == kEpiGated) {
-                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e]);
+                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e]);
                 const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), second[e]);
                 // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
                 const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
                 value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), ws[e], h2f_bits(res[e]));
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e], h2f_bits(res[e]));
                 if constexpr (EPI == kEpiMix) {
                     const float stream = __half2float(__float2half_rn(value));
                     value = __fmaf_rn(stream, rs, __fmul_rn(h2f_bits(orig[e]), is));
@@ -181,7 +177,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint16_t* row_buffers = reinterpret_cast<uint16_t*>(smem + S::kStages * S::kStageBytes);  // [tensors][128][kRowStride]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRowBytes);
+    float* column_buffers = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes + S::kRowBytes);  // [2][3 * BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRowBytes + S::kColumnBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
@@ -272,51 +269,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     } else {
-        // warps 0-7: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks c
-        // with (c / 16) % 2 == w / 4
-        const int quarter = warp & 3, half = warp >> 2;
+        // warps 0-15: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks
+        // w / 4, w / 4 + 4, ...
+        const int quarter = warp & 3, part = warp >> 2;
+        const int row_in_tile = quarter * 32 + lane;
+        uint16_t* residual_row = row_buffers + row_in_tile * S::kRowStride;
+        uint16_t* original_row = residual_row + kBlockM * S::kRowStride;
         float rs = 0.0f, is = 0.0f;
         if constexpr (EPI == kEpiMix) {
             rs = h2f_bits(*args.residual_scale);
             is = h2f_bits(*args.input_scale);
         }
+        // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
+        // epilogue warps never wait at the barrier for it
+        bool alive = true;
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
             const int buffer = local & 1;
             const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
-            const int m = m0 + quarter * 32 + lane;
-            const bool row_ok = m < M;
-            float xs = 0.0f;
-            if constexpr (EPI <= kEpiMix) xs = row_ok ? args.x_scale[m] : 0.0f;
-            // the tile's row operands for this thread's chunks travel while the MMAs finish
-            const int c0 = half * 16;
-            uint16_t* residual_row = row_buffers + (quarter * 32 + lane) * S::kRowStride;
-            uint16_t* original_row = residual_row + kBlockM * S::kRowStride;
+            const int m = m0 + row_in_tile;
+            const bool row_ok = alive && m < M;
+            const int c0 = part * 16;
+            // the tile's operands travel while the MMAs run: this thread's row operands, the scale of its row, and
+            // (all epilogue threads together) the column operands, double-buffered by tile
             if constexpr (S::kRowTensors > 0) {
                 if (row_ok) copy_tile_rows<EPI, BN>(args, residual_row, original_row, m, n0, c0, N);
             }
-            if (!mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) break;
+            float xs = 0.0f;
+            if constexpr (EPI <= kEpiMix) xs = row_ok ? args.x_scale[m] : 0.0f;
+            float* columns = column_buffers + buffer * 3 * BN;
+            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, columns, n0, N, threadIdx.x);
+            epilogue_sync();
+            if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             if constexpr (S::kRowTensors > 0) cp_async_wait_all();
+            if (!alive) continue;
             tc_fence_after();
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-            // two register sets: chunk c's math runs while chunk c + 32's accumulator and rows load
-            uint32_t acc[2][16], up[2][16];
-            if (n0 + c0 < N) {
-                tmem_load16(lane_base + c0, acc[0]);
-                if constexpr (GATED) tmem_load16(lane_base + BN + c0, up[0]);
-            }
-#pragma unroll 2
-            for (int c = c0, set = 0; c < BN && n0 + c < N; c += 32, set ^= 1) {  // uniform across the warp
+            for (int c = c0; c < BN && n0 + c < N; c += 16 * kChunkParts) {  // uniform across the warp
+                uint32_t acc[16], up[16];
+                tmem_load16(lane_base + c, acc);
+                if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
                 tmem_load_wait();
-                const int next = c + 32;
-                const bool more = next < BN && n0 + next < N;
-                if (more) {
-                    tmem_load16(lane_base + next, acc[set ^ 1]);
-                    if constexpr (GATED) tmem_load16(lane_base + BN + next, up[set ^ 1]);
-                }
                 const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
                 if (row_ok)
-                    epilogue16<EPI>(args, static_cast<size_t>(m) * N + n0 + c, n0 + c, N, valid, xs, rs, is, acc[set], up[set],
+                    epilogue16<EPI>(args, static_cast<size_t>(m) * N + n0 + c, valid, xs, rs, is, acc, up, columns + c, columns + BN + c,
                                     residual_row + c, original_row + c);
             }
             // this warp's reads of the accumulator are complete: the MMA warp may fill it again
