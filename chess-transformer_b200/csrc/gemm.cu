@@ -116,11 +116,12 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, f
         float* out = static_cast<float*>(p.out) + row;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            if (q * 4 < valid)
+            if (q * 4 < valid) {
+                const float4 b = reinterpret_cast<const float4*>(second)[q];
                 reinterpret_cast<float4*>(out)[q] =
-                    make_float4(__fadd_rn(__uint_as_float(acc[4 * q]), second[4 * q]), __fadd_rn(__uint_as_float(acc[4 * q + 1]), second[4 * q + 1]),
-                                __fadd_rn(__uint_as_float(acc[4 * q + 2]), second[4 * q + 2]),
-                                __fadd_rn(__uint_as_float(acc[4 * q + 3]), second[4 * q + 3]));
+                    make_float4(__fadd_rn(__uint_as_float(acc[4 * q]), b.x), __fadd_rn(__uint_as_float(acc[4 * q + 1]), b.y),
+                                __fadd_rn(__uint_as_float(acc[4 * q + 2]), b.z), __fadd_rn(__uint_as_float(acc[4 * q + 3]), b.w));
+            }
         return;
     } else {
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
@@ -138,34 +139,54 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, f
         }
         const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
         const uint16_t* orig = reinterpret_cast<const uint16_t*>(original_words);
-        uint16_t result[16];
+        // the chunk's column operands as 4 x float4 each (the chunk starts on a 64-byte boundary of the staged columns)
+        float scale_v[16], second_v[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if constexpr (EPI != kEpiLinearF16) {
+                const float4 a = reinterpret_cast<const float4*>(scale)[q];
+                scale_v[4 * q] = a.x, scale_v[4 * q + 1] = a.y, scale_v[4 * q + 2] = a.z, scale_v[4 * q + 3] = a.w;
+            }
+            if constexpr (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearF16) {
+                const float4 b = reinterpret_cast<const float4*>(second)[q];
+                second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
+            }
+        }
+        float values[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
             float value;
             if constexpr (EPI == kEpiBias) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e], second[e]);
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], second_v[e]);
             } else if constexpr (EPI == kEpiGated) {
-                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e]);
-                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), second[e]);
+                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e]);
+                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), second_v[e]);
                 // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
                 const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
                 value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale[e], h2f_bits(res[e]));
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], h2f_bits(res[e]));
                 if constexpr (EPI == kEpiMix) {
                     const float stream = __half2float(__float2half_rn(value));
                     value = __fmaf_rn(stream, rs, __fmul_rn(h2f_bits(orig[e]), is));
                 }
             } else {  // kEpiLinearF16: (acc + bias) + residual
-                value = __fadd_rn(__uint_as_float(acc[e]), second[e]);
+                value = __fadd_rn(__uint_as_float(acc[e]), second_v[e]);
                 if (p.residual) value = __fadd_rn(value, h2f_bits(res[e]));
             }
-            result[e] = f2h_bits(value);
+            values[e] = value;
+        }
+        // two fp16 roundings an instruction
+        uint32_t result[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const __half2 pair = __floats2half2_rn(values[2 * i], values[2 * i + 1]);
+            result[i] = *reinterpret_cast<const uint32_t*>(&pair);
         }
         uint16_t* out = static_cast<uint16_t*>(p.out) + row;
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-            if (h * 8 < valid) reinterpret_cast<uint4*>(out)[h] = *reinterpret_cast<const uint4*>(result + 8 * h);
+            if (h * 8 < valid) reinterpret_cast<uint4*>(out)[h] = make_uint4(result[4 * h], result[4 * h + 1], result[4 * h + 2], result[4 * h + 3]);
     }
 }
 

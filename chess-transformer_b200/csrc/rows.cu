@@ -4,8 +4,8 @@
 //                       gain in fp32, per-row absmax, int8 by round-half-even, scale absmax / 127.
 //  rms_norm_kernel      the final nn.RMSNorm in fp16 (model/fused_blocks.py:863) ahead of the heads.
 //  rotate_quant_kernel  `rotate_quant` (model/int8_blocks.py:216-251): the SwiGLU output zero-padded to the down width,
-//                       times the block-diagonal 32x32 Sylvester Hadamard matrix (a 5-stage butterfly in registers, one
-//                       32-block per lane), per-row absmax, int8.
+//                       times the block-diagonal 32x32 Sylvester Hadamard matrix (butterflies in registers and across
+//                       each quad of lanes), per-row absmax, int8.
 //  embedding_kernel     `board_embedding` (model/fused_blocks.py:449-507): embed[token] + position[t] + the 23 square
 //                       feature rows of `SquareFeatures.indices` (model/model.py:147-169), found in-kernel from the board.
 #include "common.cuh"
@@ -36,13 +36,15 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_quant_kernel(const uint16
         rs = h2f_bits(*residual_scale);
         is = h2f_bits(*input_scale);
     }
-    float v[CHUNKS][8];
+    float v[CHUNKS][8], g[CHUNKS][8];
     float squares = 0.0f;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
         if (col < D) {
+            // the gain travels with the row: both loads are in flight before the reduction needs either
             unpack8(*reinterpret_cast<const uint4*>(x + base + col), v[c]);
+            unpack8(*reinterpret_cast<const uint4*>(gain + col), g[c]);
             if constexpr (MIX) {
                 float o[8];
                 unpack8(*reinterpret_cast<const uint4*>(original + base + col), o);
@@ -68,11 +70,9 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_quant_kernel(const uint16
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
         if (col < D) {
-            float g[8];
-            unpack8(*reinterpret_cast<const uint4*>(gain + col), g);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[i]);
+                v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[c][i]);
                 absmax = fmaxf(absmax, fabsf(v[c][i]));
             }
         }
@@ -102,13 +102,14 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
     const int row = blockIdx.x * kRowWarps + warp;
     if (row >= M) return;
     const size_t base = static_cast<size_t>(row) * D;
-    float v[CHUNKS][8];
+    float v[CHUNKS][8], g[CHUNKS][8];
     float squares = 0.0f;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
         if (col < D) {
             unpack8(*reinterpret_cast<const uint4*>(x + base + col), v[c]);
+            unpack8(*reinterpret_cast<const uint4*>(gain + col), g[c]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
         }
@@ -119,64 +120,72 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
         if (col < D) {
-            float g[8];
-            unpack8(*reinterpret_cast<const uint4*>(gain + col), g);
             uint16_t packed[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) packed[i] = f2h_bits(__fmul_rn(__fmul_rn(v[c][i], inverse), g[i]));
+            for (int i = 0; i < 8; ++i) packed[i] = f2h_bits(__fmul_rn(__fmul_rn(v[c][i], inverse), g[c][i]));
             *reinterpret_cast<uint4*>(y + base + col) = *reinterpret_cast<const uint4*>(packed);
         }
     }
 }
 
-// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M]. Lane l owns Hadamard block l.
+// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M]. Lane l of part p owns the
+// 8-element chunk c = 32 p + l (coalesced 16-byte loads and 8-byte stores); a Hadamard block of 32 is the chunks of
+// 4 consecutive lanes. With i = 8 q + r (q the chunk within the block, r the element within the chunk),
+// H32[i][j] = (-1)^popcount(i & j) = H4[q_i][q_j] H8[r_i][r_j]: the butterflies over r run in registers, those over q
+// across the quad by shuffles, in the same order over the index bits as a 32-element butterfly.
 __global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
                                                                       float* __restrict__ scale, int M, int hidden, int width) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowWarps + warp;
     if (row >= M) return;
-    const int first = lane * 32;
-    float v[32];
+    float v[4][8];
 #pragma unroll
     for (int part = 0; part < 4; ++part) {
-        const int col = first + part * 8;
+        const int col = (part * 32 + lane) * 8;
         if (col < hidden) {
-            float u[8];
-            unpack8(*reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * hidden + col), u);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[part * 8 + i] = u[i];
+            unpack8(*reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * hidden + col), v[part]);
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[part * 8 + i] = 0.0f;
+            for (int i = 0; i < 8; ++i) v[part][i] = 0.0f;
         }
     }
-    // y = H32 v, H32[i][j] = (-1)^popcount(i & j): the butterfly (a, b) -> (a + b, a - b) over each index bit
+    // (a, b) -> (a + b, a - b) over the element bits (registers), then over the chunk bits (the quad's lanes)
 #pragma unroll
-    for (int span = 1; span < 32; span <<= 1)
+    for (int part = 0; part < 4; ++part) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if ((i & span) == 0) {
-                const float a = v[i], b = v[i + span];
-                v[i] = __fadd_rn(a, b);
-                v[i + span] = __fsub_rn(a, b);
+        for (int span = 1; span < 8; span <<= 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if ((i & span) == 0) {
+                    const float a = v[part][i], b = v[part][i + span];
+                    v[part][i] = __fadd_rn(a, b);
+                    v[part][i + span] = __fsub_rn(a, b);
+                }
+#pragma unroll
+        for (int span = 1; span < 4; span <<= 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float partner = __shfl_xor_sync(0xffffffffu, v[part][i], span);
+                v[part][i] = (lane & span) ? __fsub_rn(partner, v[part][i]) : __fadd_rn(v[part][i], partner);
             }
+    }
     float absmax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) absmax = fmaxf(absmax, fabsf(v[i]));
+    for (int part = 0; part < 4; ++part)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) absmax = fmaxf(absmax, fabsf(v[part][i]));
     absmax = fmaxf(warp_max(absmax), 1e-20f);
     const float step_inverse = __fdiv_rn(127.0f, absmax);
-    if (first < width) {
-        uint32_t packed[8];
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            packed[w] = 0u;
+    for (int part = 0; part < 4; ++part) {
+        const int col = (part * 32 + lane) * 8;
+        if (col < width) {
+            uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                packed[w] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[w * 4 + i], step_inverse))) & 0xffu) << (8 * i);
+            for (int i = 0; i < 8; ++i)
+                packed[i / 4] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[part][i], step_inverse))) & 0xffu) << (8 * (i % 4));
+            *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * width + col) = make_uint2(packed[0], packed[1]);
         }
-        uint4* out = reinterpret_cast<uint4*>(q + static_cast<size_t>(row) * width + first);
-        out[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        out[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     }
     if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
 }
