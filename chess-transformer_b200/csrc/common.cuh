@@ -90,6 +90,20 @@ FRY_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, in
         : "memory");
 }
 
+// 2-D tiled TMA store of box {x, y} from shared memory, in this thread's current bulk async-group.
+FRY_DEVICE void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+FRY_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every bulk async-group of this thread has finished reading its shared memory
+FRY_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every bulk async-group of this thread has completed
+FRY_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// orders this thread's shared-memory accesses before later async-proxy (TMA) accesses
+FRY_DEVICE void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 FRY_DEVICE void prefetch_tensor_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -11,8 +11,12 @@
 // stage with tcgen05.commit and hands the finished accumulator to the epilogue. Warps 0-15 are the epilogue: warp w reads
 // TMEM lanes 32 (w % 4) .. +31 (one output row per thread) and every fourth 16-column chunk, starting at chunk w / 4, with
 // tcgen05.ld, and applies the epilogue in the reference's op order (model/int8_cuda.py:163-178) while the MMAs of the
-// next tile fill the other accumulator. A tile's column operands (weight scales, bias) are staged once in shared memory;
-// its row operands (residual, original) are copied by each thread for its own row with cp.async while the MMAs run.
+// next tile fill the other accumulator.
+//
+// fp16 outputs leave through shared memory: a tile is staged as 16-column boxes of 128 rows x 32 bytes, which one thread
+// writes to global memory with TMA stores, so no thread stores a row of its own. The row operands (residual, original)
+// arrive the same way, as TMA loads of the same boxes one tile ahead into the other of two slots, and each output
+// overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged in shared memory too.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
@@ -31,6 +35,10 @@ constexpr int kProducerWarp = kEpilogueWarps, kMmaWarp = kEpilogueWarps + 1;
 constexpr int kGemmThreads = (kEpilogueWarps + 2) * 32;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
 constexpr int kEpilogueBarrier = 1;  // named barrier of the epilogue warps (0 is __syncthreads)
+constexpr int kChunkCols = 16;       // columns of one epilogue chunk and of one staged box
+constexpr int kBoxBytes = kBlockM * kChunkCols * 2;  // a staged fp16 box: 128 rows x 32 bytes
+// dynamic shared memory a CTA may use (227 KB) less the 1024-byte alignment slack and the barriers
+constexpr int kSmemBudget = 227 * 1024 - 1024 - 256;
 
 template <int KIND, int BN, bool GATED, int EPI>
 struct GemmShape {
@@ -39,47 +47,30 @@ struct GemmShape {
     static constexpr int kABytes = kBlockM * kTileKBytes;
     static constexpr int kBBytes = BN * kTileKBytes;
     static constexpr int kStageBytes = kABytes + kBBytes * (GATED ? 2 : 1);
-    // the epilogue's row operands (residual, and original when mixing) for the tile, one padded row per output row
+    // fp16 outputs are staged for TMA stores; int32 and fp32 outputs are stored by their threads
+    static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
+    // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
     static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
-    static constexpr int kRowStride = BN + 8;  // halves: 16-byte accesses of 8 consecutive rows fall in distinct banks
-    static constexpr int kRowBytes = kRowTensors * kBlockM * kRowStride * 2;
+    static constexpr int kChunks = BN / kChunkCols;
+    // one slot holds a tile's row operands (the output overwrites the first) or, without row operands, its output;
+    // with row operands there are two, so the next tile's operands load while this tile is worked on
+    static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kChunks * kBoxBytes : 0;
+    static constexpr int kSlots = kRowTensors > 0 ? 2 : 1;
+    static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][3][BN] floats (weight scales, up's scales or the bias)
     static constexpr int kColumnBytes = 2 * 3 * BN * 4;
-    static constexpr int kStagesFit = (200 * 1024 - kRowBytes - kColumnBytes) / kStageBytes;
+    static constexpr int kStagesFit = (kSmemBudget - kIoBytes - kColumnBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kStages * kStageBytes + kRowBytes + kColumnBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kIoBytes + kStages * kStageBytes + kColumnBytes + 1024 + 256;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
 
-FRY_DEVICE void cp_async16(void* smem, const void* global) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(global) : "memory");
-}
-FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-FRY_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads) : "memory"); }
-
-// Starts the copies of one output row's residual (and original) for this thread's chunks of the tile into its shared
-// row buffers; every 16-byte piece is copied by the thread that reads it, so no barrier is needed, only the wait.
-template <int EPI, int BN>
-FRY_DEVICE void copy_tile_rows(const GemmArgs& p, uint16_t* residual_row, uint16_t* original_row, int m, int n0, int c0, int N) {
-    const bool has_residual = EPI == kEpiResidual || EPI == kEpiMix || (EPI == kEpiLinearF16 && p.residual != nullptr);
-    if (!has_residual) return;
-    for (int c = c0; c < BN && n0 + c < N; c += 16 * kChunkParts) {
-        const size_t offset = static_cast<size_t>(m) * N + n0 + c;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            if (n0 + c + 8 * h >= N) break;
-            cp_async16(residual_row + c + 8 * h, p.residual + offset + 8 * h);
-            if constexpr (EPI == kEpiMix) cp_async16(original_row + c + 8 * h, p.original + offset + 8 * h);
-        }
-    }
-    cp_async_commit();
-}
 
 // The tile's column operands into shared memory (all epilogue threads together): columns[0] the weight scales,
 // columns[1] up's scales (gated) or the bias as floats, zero past N.
@@ -98,13 +89,36 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
     }
 }
 
-// Applies the epilogue to 16 consecutive columns [n, n + valid) of one row (row = m * N + n); acc holds the raw TMEM
-// words, xs the row's activation scale, rs and is the next block's input-mix scales; scale and second point at the
-// chunk's column operands in shared memory, residual_chunk and original_chunk at its row operands.
+// Issues the TMA loads of one tile's row operands (the boxes of its columns below N) into a slot, completing on bar.
+template <int EPI, int BN>
+FRY_DEVICE void load_tile_rows(const CUtensorMap* map_residual, const CUtensorMap* map_original, uint8_t* slot, uint64_t* bar, int m0,
+                               int n0, int N) {
+    constexpr int kChunks = BN / kChunkCols, kTensors = EPI == kEpiMix ? 2 : 1;
+    const int chunks = (N - n0) / kChunkCols + ((N - n0) % kChunkCols != 0);
+    const int boxes = chunks < kChunks ? chunks : kChunks;
+    mbar_arrive_expect_tx(bar, boxes * kTensors * kBoxBytes);
+    for (int c = 0; c < boxes; ++c) {
+        tma_load_2d(slot + c * kBoxBytes, map_residual, bar, n0 + c * kChunkCols, m0);
+        if constexpr (EPI == kEpiMix) tma_load_2d(slot + (kChunks + c) * kBoxBytes, map_original, bar, n0 + c * kChunkCols, m0);
+    }
+}
+
+// A staged row chunk's two 16-byte halves, the one `swap` names first.
+FRY_DEVICE void read_halves(const uint16_t* chunk, int swap, uint4 (&words)[2]) {
+    const uint4 first = reinterpret_cast<const uint4*>(chunk)[swap], second = reinterpret_cast<const uint4*>(chunk)[swap ^ 1];
+    words[0] = swap ? second : first;
+    words[1] = swap ? first : second;
+}
+
+// Applies the epilogue to one row's 16 consecutive columns. acc (and up, gated) hold the raw TMEM words, xs the row's
+// activation scale, rs and is the next block's input-mix scales, scale and second the chunk's column operands in shared
+// memory. Staged epilogues read the row's residual (and original) from its 32 staged bytes and write the fp16 results
+// over them, the two 16-byte halves in the order `swap` gives (rows 4 apart alternate, so a warp's accesses spread over
+// all banks); int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
 template <int EPI>
-FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, float rs, float is, const uint32_t (&acc)[16],
-                           const uint32_t (&up)[16], const float* scale, const float* second, const uint16_t* residual_chunk,
-                           const uint16_t* original_chunk) {
+FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, const uint32_t (&acc)[16], const uint32_t (&up)[16],
+                           const float* scale, const float* second, uint16_t* staged, const uint16_t* original, int swap, size_t row,
+                           int valid) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -124,19 +138,12 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, f
             }
         return;
     } else {
+        constexpr bool kResidual = EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16;
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-        if constexpr (EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16) {
-            if (EPI != kEpiLinearF16 || p.residual != nullptr) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    if (h * 8 < valid) residual_words[h] = *reinterpret_cast<const uint4*>(residual_chunk + 8 * h);
-            }
+        if constexpr (kResidual) {
+            if (EPI != kEpiLinearF16 || p.residual != nullptr) read_halves(staged, swap, residual_words);
         }
-        if constexpr (EPI == kEpiMix) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-                if (h * 8 < valid) original_words[h] = *reinterpret_cast<const uint4*>(original_chunk + 8 * h);
-        }
+        if constexpr (EPI == kEpiMix) read_halves(original, swap, original_words);
         const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
         const uint16_t* orig = reinterpret_cast<const uint16_t*>(original_words);
         // the chunk's column operands as 4 x float4 each (the chunk starts on a 64-byte boundary of the staged columns)
@@ -176,34 +183,36 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, size_t row, int valid, float xs, f
             }
             values[e] = value;
         }
-        // two fp16 roundings an instruction
+        // two fp16 roundings an instruction, over the staged residual
         uint32_t result[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const __half2 pair = __floats2half2_rn(values[2 * i], values[2 * i + 1]);
             result[i] = *reinterpret_cast<const uint32_t*>(&pair);
         }
-        uint16_t* out = static_cast<uint16_t*>(p.out) + row;
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-            if (h * 8 < valid) reinterpret_cast<uint4*>(out)[h] = make_uint4(result[4 * h], result[4 * h + 1], result[4 * h + 2], result[4 * h + 3]);
+        const uint4 low = make_uint4(result[0], result[1], result[2], result[3]), high = make_uint4(result[4], result[5], result[6], result[7]);
+        reinterpret_cast<uint4*>(staged)[swap] = swap ? high : low;
+        reinterpret_cast<uint4*>(staged)[swap ^ 1] = swap ? low : high;
     }
 }
 
 template <int KIND, int BN, bool GATED, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmArgs args, int M, int N,
-                int K) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_residual,
+                const __grid_constant__ CUtensorMap map_original, const GemmArgs args, int M, int N, int K) {
     using S = GemmShape<KIND, BN, GATED, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint16_t* row_buffers = reinterpret_cast<uint16_t*>(smem + S::kStages * S::kStageBytes);  // [tensors][128][kRowStride]
-    float* column_buffers = reinterpret_cast<float*>(smem + S::kStages * S::kStageBytes + S::kRowBytes);  // [2][3 * BN]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kRowBytes + S::kColumnBytes);
+    uint8_t* stages = smem;                                              // [kStages][A box | B box(es)]
+    uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kChunks][128 rows][32 bytes]
+    float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][3 * BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    uint64_t* rows_full = tmem_empty + 2;       // [2]: a slot's row operands have landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rows_full + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = (N + BN - 1) / BN;
@@ -218,6 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
             mbar_init(&tmem_empty[b], kEpilogueWarps);
+            mbar_init(&rows_full[b], 1);
         }
         fence_barrier_init();
     }
@@ -247,7 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         ok = false;
                         break;
                     }
-                    uint8_t* a = smem + s * S::kStageBytes;
+                    uint8_t* a = stages + s * S::kStageBytes;
                     uint8_t* b = a + S::kABytes;
                     mbar_arrive_expect_tx(&full[s], S::kStageBytes);
                     tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a = smem_addr(smem + s * S::kStageBytes);
+                    const uint32_t a = smem_addr(stages + s * S::kStageBytes);
                     const uint32_t b = a + S::kABytes;
 #pragma unroll
                     for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
@@ -294,53 +304,86 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // w / 4, w / 4 + 4, ...
         const int quarter = warp & 3, part = warp >> 2;
         const int row_in_tile = quarter * 32 + lane;
-        uint16_t* residual_row = row_buffers + row_in_tile * S::kRowStride;
-        uint16_t* original_row = residual_row + kBlockM * S::kRowStride;
+        const int swap = (row_in_tile >> 2) & 1;
+        const bool leader = threadIdx.x == 0;  // issues the staged tiles' TMA loads and stores
         float rs = 0.0f, is = 0.0f;
         if constexpr (EPI == kEpiMix) {
             rs = h2f_bits(*args.residual_scale);
             is = h2f_bits(*args.input_scale);
+        }
+        const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
+        auto tile_origin = [&](int tile, int& m0, int& n0) {
+            m0 = (tile / n_blocks) * kBlockM;
+            n0 = (tile % n_blocks) * BN;
+        };
+        if (leader && has_rows && static_cast<int>(blockIdx.x) < tiles) {  // the first tile's row operands
+            int m0, n0;
+            tile_origin(blockIdx.x, m0, n0);
+            load_tile_rows<EPI, BN>(&map_residual, &map_original, io, &rows_full[0], m0, n0, N);
         }
         // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
         // epilogue warps never wait at the barrier for it
         bool alive = true;
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-            const int buffer = local & 1;
-            const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
+            const int buffer = local & 1, slot = S::kSlots == 2 ? local & 1 : 0;
+            int m0, n0;
+            tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
-            const bool row_ok = alive && m < M;
-            const int c0 = part * 16;
-            // the tile's operands travel while the MMAs run: this thread's row operands, the scale of its row, and
-            // (all epilogue threads together) the column operands, double-buffered by tile
-            if constexpr (S::kRowTensors > 0) {
-                if (row_ok) copy_tile_rows<EPI, BN>(args, residual_row, original_row, m, n0, c0, N);
+            const int c0 = part * kChunkCols;
+            if constexpr (S::kStaged) {
+                if (leader) {
+                    // the last tile's stores have read their slot; the next tile's row operands go into the other one
+                    if (local > 0) bulk_wait_read_all();
+                    if (has_rows && tile + static_cast<int>(gridDim.x) < tiles) {
+                        int next_m0, next_n0;
+                        tile_origin(tile + gridDim.x, next_m0, next_n0);
+                        load_tile_rows<EPI, BN>(&map_residual, &map_original, io + (slot ^ 1) * S::kSlotBytes, &rows_full[slot ^ 1],
+                                                next_m0, next_n0, N);
+                    }
+                }
             }
             float xs = 0.0f;
-            if constexpr (EPI <= kEpiMix) xs = row_ok ? args.x_scale[m] : 0.0f;
+            if constexpr (EPI <= kEpiMix) xs = (alive && m < M) ? args.x_scale[m] : 0.0f;
             float* columns = column_buffers + buffer * 3 * BN;
             if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, columns, n0, N, threadIdx.x);
             epilogue_sync();
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
-            if constexpr (S::kRowTensors > 0) cp_async_wait_all();
-            if (!alive) continue;
-            tc_fence_after();
-            const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-            for (int c = c0; c < BN && n0 + c < N; c += 16 * kChunkParts) {  // uniform across the warp
-                uint32_t acc[16], up[16];
-                tmem_load16(lane_base + c, acc);
-                if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
-                tmem_load_wait();
-                const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
-                if (row_ok)
-                    epilogue16<EPI>(args, static_cast<size_t>(m) * N + n0 + c, valid, xs, rs, is, acc, up, columns + c, columns + BN + c,
-                                    residual_row + c, original_row + c);
+            // every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
+            if (has_rows && !mbar_wait(&rows_full[slot], (local >> 1) & 1, 14)) alive = false;
+            uint8_t* staged_tile = io + slot * S::kSlotBytes;
+            if (alive) {
+                tc_fence_after();
+                const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+                for (int c = c0; c < BN && n0 + c < N; c += kChunkCols * kChunkParts) {  // uniform across the warp
+                    uint32_t acc[16], up[16];
+                    tmem_load16(lane_base + c, acc);
+                    if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
+                    tmem_load_wait();
+                    const int chunk = c / kChunkCols;
+                    uint16_t* staged = reinterpret_cast<uint16_t*>(staged_tile + chunk * kBoxBytes + row_in_tile * 32);
+                    const uint16_t* original = reinterpret_cast<const uint16_t*>(staged_tile + (S::kChunks + chunk) * kBoxBytes + row_in_tile * 32);
+                    const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
+                    if (S::kStaged || m < M)
+                        epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original, swap,
+                                        static_cast<size_t>(m) * N + n0 + c, valid);
+                }
             }
             // this warp's reads of the accumulator are complete: the MMA warp may fill it again
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
+            if constexpr (S::kStaged) {
+                // the staged tile, once every thread's writes are visible to the async proxy, leaves by TMA stores
+                fence_proxy_async_shared();
+                epilogue_sync();
+                if (leader) {
+                    for (int c = 0; c < BN && n0 + c < N; c += kChunkCols) tma_store_2d(&map_out, staged_tile + (c / kChunkCols) * kBoxBytes, n0 + c, m0);
+                    bulk_commit();
+                }
+            }
         }
+        if (leader) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
@@ -390,32 +433,60 @@ bool make_map(CUtensorMap* map, const void* base, int elem_bytes, int k, int row
     return true;
 }
 
+// An fp16 [rows, cols] row-major tensor as a TMA map with a box of 16 columns by 128 rows and no swizzle: the boxes the
+// epilogue stages.
+bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::string* error) {
+    EncodeTiled encode = encoder(error);
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunkCols), static_cast<cuuint32_t>(kBlockM)};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult result = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, element_strides,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (result != CUDA_SUCCESS) {
+        if (error) *error = "cuTensorMapEncodeTiled (fp16 [" + std::to_string(rows) + ", " + std::to_string(cols) +
+                            "] staging map) failed with CUresult " + std::to_string(static_cast<int>(result));
+        return false;
+    }
+    return true;
+}
+
 template <int KIND, int BN, bool GATED, int EPI>
 cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
     using S = GemmShape<KIND, BN, GATED, EPI>;
     auto kernel = gemm_kernel<KIND, BN, GATED, EPI>;
     const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
     if (attribute != cudaSuccess) return attribute;
-    CUtensorMap map_a, map_b;
+    CUtensorMap map_a, map_b, map_out, map_residual, map_original;
     if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error) || !make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error))
         return cudaErrorInvalidValue;
+    // the staged epilogues' maps; unused ones repeat the output's, which is always valid
+    map_out = map_residual = map_original = map_a;
+    if constexpr (S::kStaged) {
+        if (!make_box_map(&map_out, args.out, N, M, error)) return cudaErrorInvalidValue;
+        map_residual = map_original = map_out;
+        if (args.residual && !make_box_map(&map_residual, args.residual, N, M, error)) return cudaErrorInvalidValue;
+        if (EPI == kEpiMix && !make_box_map(&map_original, args.original, N, M, error)) return cudaErrorInvalidValue;
+    }
     const int tiles = ((M + kBlockM - 1) / kBlockM) * ((N + BN - 1) / BN);
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    kernel<<<tiles < multiprocessors ? tiles : multiprocessors, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, args, M, N, K);
+    kernel<<<tiles < multiprocessors ? tiles : multiprocessors, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, map_out, map_residual,
+                                                                                                         map_original, args, M, N, K);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; 256 attention-out (768 wide, one
-// residual row buffer); 128 everywhere else: gate_up's 128 columns hold 256 accumulators (its gate and its up), down keeps
-// two row buffers (residual and original) beside four pipeline stages.
+// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; gate_up's 128 columns hold 256
+// accumulators (its gate and its up); mixing's 64 keep two staged row operands in two slots beside six stages; 128
+// elsewhere. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA stores).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
-    const bool wide = N % 256 == 0;
     if (kind == 0) {
         switch (epilogue) {
             case kEpiBias:
@@ -423,15 +494,13 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                                     : launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
             case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
-            case kEpiMix: return launch<0, 128, false, kEpiMix>(a, b, args, M, N, K, stream, error);
+            case kEpiMix: return launch<0, 64, false, kEpiMix>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {
         switch (epilogue) {
-            case kEpiLinearF16:
-                return wide ? launch<1, 256, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error)
-                            : launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF16: return launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             default: break;
         }

@@ -22,77 +22,94 @@ FRY_DEVICE void unpack8(const uint4& u, float (&v)[8]) {
 }
 
 // x [M, D] fp16 -> q [M, D] int8, scale [M]; with MIX, x is first mixed with original and the mix stored to mixed.
-template <int CHUNKS, bool MIX>
+// A warp takes ROWS consecutive rows and issues all their loads (and the gain's) before working on any, so the row
+// latencies overlap; each row's arithmetic is the single-row order: per lane over its chunks, then the warp's tree.
+template <int CHUNKS, bool MIX, int ROWS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
                                                                     const uint16_t* residual_scale, const uint16_t* input_scale,
                                                                     const uint16_t* __restrict__ gain, float eps, uint16_t* mixed,
                                                                     int8_t* __restrict__ q, float* __restrict__ scale, int M, int D) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kRowWarps + warp;
-    if (row >= M) return;
-    const size_t base = static_cast<size_t>(row) * D;
+    const int first_row = (blockIdx.x * kRowWarps + warp) * ROWS;
+    if (first_row >= M) return;
     float rs = 0.0f, is = 0.0f;
     if constexpr (MIX) {
         rs = h2f_bits(*residual_scale);
         is = h2f_bits(*input_scale);
     }
-    float v[CHUNKS][8], g[CHUNKS][8];
-    float squares = 0.0f;
+    uint4 raw[ROWS][CHUNKS], raw_original[MIX ? ROWS : 1][CHUNKS], raw_gain[CHUNKS];
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
-        if (col < D) {
-            // the gain travels with the row: both loads are in flight before the reduction needs either
-            unpack8(*reinterpret_cast<const uint4*>(x + base + col), v[c]);
-            unpack8(*reinterpret_cast<const uint4*>(gain + col), g[c]);
-            if constexpr (MIX) {
-                float o[8];
-                unpack8(*reinterpret_cast<const uint4*>(original + base + col), o);
-                uint16_t packed[8];
+        raw_gain[c] = col < D ? *reinterpret_cast<const uint4*>(gain + col) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            const bool ok = col < D && first_row + r < M;
+            const size_t at = static_cast<size_t>(first_row + r) * D + col;
+            raw[r][c] = ok ? *reinterpret_cast<const uint4*>(x + at) : make_uint4(0, 0, 0, 0);
+            if constexpr (MIX) raw_original[r][c] = ok ? *reinterpret_cast<const uint4*>(original + at) : make_uint4(0, 0, 0, 0);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        const int row = first_row + r;
+        if (row >= M) break;  // uniform across the warp
+        const size_t base = static_cast<size_t>(row) * D;
+        float v[CHUNKS][8];
+        float squares = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            const int col = (c * 32 + lane) * 8;
+            unpack8(raw[r][c], v[c]);
+            if (col < D) {
+                if constexpr (MIX) {
+                    float o[8];
+                    unpack8(raw_original[r][c], o);
+                    uint16_t packed[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        packed[i] = f2h_bits(__fmaf_rn(rs, v[c][i], __fmul_rn(is, o[i])));
+                        v[c][i] = h2f_bits(packed[i]);
+                    }
+                    *reinterpret_cast<uint4*>(mixed + base + col) = *reinterpret_cast<const uint4*>(packed);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
+            }
+        }
+        squares = warp_sum(squares);
+        const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(D)), eps));
+        float absmax = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            const int col = (c * 32 + lane) * 8;
+            if (col < D) {
+                float g[8];
+                unpack8(raw_gain[c], g);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    packed[i] = f2h_bits(__fmaf_rn(rs, v[c][i], __fmul_rn(is, o[i])));
-                    v[c][i] = h2f_bits(packed[i]);
+                    v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[i]);
+                    absmax = fmaxf(absmax, fabsf(v[c][i]));
                 }
-                *reinterpret_cast<uint4*>(mixed + base + col) = *reinterpret_cast<const uint4*>(packed);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[c][i] = 0.0f;
-        }
-    }
-    squares = warp_sum(squares);
-    const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(D)), eps));
-    float absmax = 0.0f;
-#pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        if (col < D) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[c][i]);
-                absmax = fmaxf(absmax, fabsf(v[c][i]));
             }
         }
-    }
-    absmax = fmaxf(warp_max(absmax), 1e-20f);
-    const float step_inverse = __fdiv_rn(127.0f, absmax);
+        absmax = fmaxf(warp_max(absmax), 1e-20f);
+        const float step_inverse = __fdiv_rn(127.0f, absmax);
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        if (col < D) {
-            uint32_t packed[2] = {0u, 0u};
+        for (int c = 0; c < CHUNKS; ++c) {
+            const int col = (c * 32 + lane) * 8;
+            if (col < D) {
+                uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int value = __float2int_rn(__fmul_rn(v[c][i], step_inverse));
-                packed[i / 4] |= (static_cast<uint32_t>(value) & 0xffu) << (8 * (i % 4));
+                for (int i = 0; i < 8; ++i) {
+                    const int value = __float2int_rn(__fmul_rn(v[c][i], step_inverse));
+                    packed[i / 4] |= (static_cast<uint32_t>(value) & 0xffu) << (8 * (i % 4));
+                }
+                *reinterpret_cast<uint2*>(q + base + col) = make_uint2(packed[0], packed[1]);
             }
-            *reinterpret_cast<uint2*>(q + base + col) = make_uint2(packed[0], packed[1]);
         }
+        if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
     }
-    if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
 }
 
 template <int CHUNKS>
@@ -133,61 +150,70 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
 // 4 consecutive lanes. With i = 8 q + r (q the chunk within the block, r the element within the chunk),
 // H32[i][j] = (-1)^popcount(i & j) = H4[q_i][q_j] H8[r_i][r_j]: the butterflies over r run in registers, those over q
 // across the quad by shuffles, in the same order over the index bits as a 32-element butterfly.
+// A warp takes kRotateRows consecutive rows, their loads all issued first.
+constexpr int kRotateRows = 2;
 __global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
                                                                       float* __restrict__ scale, int M, int hidden, int width) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kRowWarps + warp;
-    if (row >= M) return;
-    float v[4][8];
+    const int first_row = (blockIdx.x * kRowWarps + warp) * kRotateRows;
+    if (first_row >= M) return;
+    uint4 raw[kRotateRows][4];
 #pragma unroll
-    for (int part = 0; part < 4; ++part) {
-        const int col = (part * 32 + lane) * 8;
-        if (col < hidden) {
-            unpack8(*reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * hidden + col), v[part]);
-        } else {
+    for (int r = 0; r < kRotateRows; ++r)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[part][i] = 0.0f;
+        for (int part = 0; part < 4; ++part) {
+            const int col = (part * 32 + lane) * 8;
+            raw[r][part] = (col < hidden && first_row + r < M)
+                               ? *reinterpret_cast<const uint4*>(h + static_cast<size_t>(first_row + r) * hidden + col)
+                               : make_uint4(0, 0, 0, 0);
         }
-    }
-    // (a, b) -> (a + b, a - b) over the element bits (registers), then over the chunk bits (the quad's lanes)
 #pragma unroll
-    for (int part = 0; part < 4; ++part) {
+    for (int r = 0; r < kRotateRows; ++r) {
+        const int row = first_row + r;
+        if (row >= M) break;  // uniform across the warp
+        float v[4][8];
 #pragma unroll
-        for (int span = 1; span < 8; span <<= 1)
+        for (int part = 0; part < 4; ++part) unpack8(raw[r][part], v[part]);
+        // (a, b) -> (a + b, a - b) over the element bits (registers), then over the chunk bits (the quad's lanes)
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if ((i & span) == 0) {
-                    const float a = v[part][i], b = v[part][i + span];
-                    v[part][i] = __fadd_rn(a, b);
-                    v[part][i + span] = __fsub_rn(a, b);
+        for (int part = 0; part < 4; ++part) {
+#pragma unroll
+            for (int span = 1; span < 8; span <<= 1)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if ((i & span) == 0) {
+                        const float a = v[part][i], b = v[part][i + span];
+                        v[part][i] = __fadd_rn(a, b);
+                        v[part][i + span] = __fsub_rn(a, b);
+                    }
+#pragma unroll
+            for (int span = 1; span < 4; span <<= 1)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float partner = __shfl_xor_sync(0xffffffffu, v[part][i], span);
+                    v[part][i] = (lane & span) ? __fsub_rn(partner, v[part][i]) : __fadd_rn(v[part][i], partner);
                 }
-#pragma unroll
-        for (int span = 1; span < 4; span <<= 1)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float partner = __shfl_xor_sync(0xffffffffu, v[part][i], span);
-                v[part][i] = (lane & span) ? __fsub_rn(partner, v[part][i]) : __fadd_rn(v[part][i], partner);
-            }
-    }
-    float absmax = 0.0f;
-#pragma unroll
-    for (int part = 0; part < 4; ++part)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) absmax = fmaxf(absmax, fabsf(v[part][i]));
-    absmax = fmaxf(warp_max(absmax), 1e-20f);
-    const float step_inverse = __fdiv_rn(127.0f, absmax);
-#pragma unroll
-    for (int part = 0; part < 4; ++part) {
-        const int col = (part * 32 + lane) * 8;
-        if (col < width) {
-            uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                packed[i / 4] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[part][i], step_inverse))) & 0xffu) << (8 * (i % 4));
-            *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * width + col) = make_uint2(packed[0], packed[1]);
         }
+        float absmax = 0.0f;
+#pragma unroll
+        for (int part = 0; part < 4; ++part)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) absmax = fmaxf(absmax, fabsf(v[part][i]));
+        absmax = fmaxf(warp_max(absmax), 1e-20f);
+        const float step_inverse = __fdiv_rn(127.0f, absmax);
+#pragma unroll
+        for (int part = 0; part < 4; ++part) {
+            const int col = (part * 32 + lane) * 8;
+            if (col < width) {
+                uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    packed[i / 4] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[part][i], step_inverse))) & 0xffu) << (8 * (i % 4));
+                *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * width + col) = make_uint2(packed[0], packed[1]);
+            }
+        }
+        if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
     }
-    if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
 }
 
 // ---- embedding ------------------------------------------------------------------------------------------------
@@ -306,14 +332,15 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
                        const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
-    const dim3 grid((M + kRowWarps - 1) / kRowWarps);
-    const int chunks = (D + 255) / 256;
+    constexpr int kRows = 4, kMixRows = 2;  // rows a warp
     const bool mix = original != nullptr;
-#define FRY_NQ(C)                                                                                                                 \
-    (mix ? (norm_quant_kernel<C, true><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
-                                                                             mixed, q, scale, M, D), 0)                           \
-         : (norm_quant_kernel<C, false><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
-                                                                              mixed, q, scale, M, D), 0))
+    const dim3 grid((M + kRowWarps * (mix ? kMixRows : kRows) - 1) / (kRowWarps * (mix ? kMixRows : kRows)));
+    const int chunks = (D + 255) / 256;
+#define FRY_NQ(C)                                                                                                                       \
+    (mix ? (norm_quant_kernel<C, true, kMixRows><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, \
+                                                                                       eps, mixed, q, scale, M, D), 0)                  \
+         : (norm_quant_kernel<C, false, kRows><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
+                                                                                     mixed, q, scale, M, D), 0))
     switch (chunks) {
         case 1: FRY_NQ(1); break;
         case 2: FRY_NQ(2); break;
@@ -340,7 +367,8 @@ cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uin
 cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (hidden % 8 != 0 || width % 32 != 0 || width > 1024 || hidden > width) return cudaErrorInvalidValue;
-    rotate_quant_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, stream>>>(h, q, scale, M, hidden, width);
+    const int rows_a_block = kRowWarps * kRotateRows;
+    rotate_quant_kernel<<<(M + rows_a_block - 1) / rows_a_block, kRowWarps * 32, 0, stream>>>(h, q, scale, M, hidden, width);
     return cudaGetLastError();
 }
 

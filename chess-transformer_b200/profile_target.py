@@ -2,9 +2,9 @@
 so that `ncu --profile-from-start off` captures exactly that work. Warm-up runs happen before the start.
 
     ncu --profile-from-start off --metrics gpu__time_duration.sum --clock-control none --csv \\
-        python chess-transformer_b200/profile.py --batch 256 --forwards 1
+        python chess-transformer_b200/profile_target.py --batch 256 --forwards 1
     ncu --profile-from-start off --set full --clock-control none -k regex:gemm_kernel -c 1 -o gpurun_out/gemm \\
-        python chess-transformer_b200/profile.py --gemm gate_up --batch 256
+        python chess-transformer_b200/profile_target.py --gemm gate_up --batch 256
 """
 import argparse
 import sys

@@ -82,7 +82,9 @@ def test_int8_linear_is_the_references(golden, key):
     assert np.allclose(found.cpu().double().numpy(), exact, atol=1e-3, rtol=2e-3)
 
 
-@pytest.mark.parametrize("M", [5, 70, 4480])
+# 17920 and 19001 rows take the A-resident kernels (a CTA per 128-row block; past 148 blocks a CTA takes two, the last
+# one partial)
+@pytest.mark.parametrize("M", [5, 70, 4480, 17920, 19001])
 @pytest.mark.parametrize("epilogue", ["bias", "gated", "residual", "mixing"])
 def test_int8_linear_is_the_oracle_on_fry_shapes(M, epilogue):
     N, K = {"bias": (1152, 768), "gated": (992, 768), "residual": (768, 1024), "mixing": (768, 1024)}[epilogue]
