@@ -13,10 +13,12 @@
 // tcgen05.ld, and applies the epilogue in the reference's op order (model/int8_cuda.py:163-178) while the MMAs of the
 // next tile fill the other accumulator.
 //
-// fp16 outputs leave through shared memory: a tile is staged as 16-column boxes of 128 rows x 32 bytes, which one thread
-// writes to global memory with TMA stores, so no thread stores a row of its own. The row operands (residual, original)
-// arrive the same way, as TMA loads of the same boxes one tile ahead into the other of two slots, and each output
-// overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged in shared memory too.
+// fp16 outputs leave through shared memory: a tile is staged as 64-column boxes of 128 rows x 128 bytes in the 128-byte
+// swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread over all banks), which one
+// thread writes to global memory with TMA stores; no thread stores a row of its own. The row operands (residual,
+// original) arrive the same way, as TMA loads of the same boxes one tile ahead into the other of two slots, and each
+// output overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged one tile ahead in
+// shared memory too, so one barrier a tile suffices.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
@@ -35,8 +37,9 @@ constexpr int kProducerWarp = kEpilogueWarps, kMmaWarp = kEpilogueWarps + 1;
 constexpr int kGemmThreads = (kEpilogueWarps + 2) * 32;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
 constexpr int kEpilogueBarrier = 1;  // named barrier of the epilogue warps (0 is __syncthreads)
-constexpr int kChunkCols = 16;       // columns of one epilogue chunk and of one staged box
-constexpr int kBoxBytes = kBlockM * kChunkCols * 2;  // a staged fp16 box: 128 rows x 32 bytes
+constexpr int kChunkCols = 16;       // columns of one epilogue chunk (one tcgen05.ld)
+constexpr int kBoxCols = 64;         // columns of one staged box: 128 bytes of fp16, one swizzle row
+constexpr int kBoxBytes = kBlockM * kBoxCols * 2;  // a staged fp16 box: 128 rows x 128 bytes
 // dynamic shared memory a CTA may use (227 KB) less the 1024-byte alignment slack and the barriers
 constexpr int kSmemBudget = 227 * 1024 - 1024 - 256;
 
@@ -51,14 +54,15 @@ struct GemmShape {
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
     // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
     static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
-    static constexpr int kChunks = BN / kChunkCols;
-    // one slot holds a tile's row operands (the output overwrites the first) or, without row operands, its output;
-    // with row operands there are two, so the next tile's operands load while this tile is worked on
-    static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kChunks * kBoxBytes : 0;
-    static constexpr int kSlots = kRowTensors > 0 ? 2 : 1;
+    static constexpr int kBoxes = BN / kBoxCols;
+    static_assert(!kStaged || BN % kBoxCols == 0, "a staged tile is whole 64-column boxes");
+    // one slot holds a tile's row operands (the output overwrites the first) or, without row operands, its output; there
+    // are two, so the next tile's operands load, and the last tile's stores drain, while this tile is worked on
+    static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kBoxes * kBoxBytes : 0;
+    static constexpr int kSlots = 2;
     static constexpr int kIoBytes = kSlots * kSlotBytes;
-    // the tile's column operands, double-buffered by tile: [2][3][BN] floats (weight scales, up's scales or the bias)
-    static constexpr int kColumnBytes = 2 * 3 * BN * 4;
+    // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
+    static constexpr int kColumnBytes = 2 * 2 * BN * 4;
     static constexpr int kStagesFit = (kSmemBudget - kIoBytes - kColumnBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
@@ -66,7 +70,7 @@ struct GemmShape {
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
     static constexpr int kSmemBytes = kIoBytes + kStages * kStageBytes + kColumnBytes + 1024 + 256;
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
+    static_assert(kAccCols % 16 == 0 && kAccCols >= 16 && kAccCols <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
 
@@ -93,31 +97,32 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
 template <int EPI, int BN>
 FRY_DEVICE void load_tile_rows(const CUtensorMap* map_residual, const CUtensorMap* map_original, uint8_t* slot, uint64_t* bar, int m0,
                                int n0, int N) {
-    constexpr int kChunks = BN / kChunkCols, kTensors = EPI == kEpiMix ? 2 : 1;
-    const int chunks = (N - n0) / kChunkCols + ((N - n0) % kChunkCols != 0);
-    const int boxes = chunks < kChunks ? chunks : kChunks;
+    constexpr int kBoxes = BN / kBoxCols, kTensors = EPI == kEpiMix ? 2 : 1;
+    const int in_range = (N - n0 + kBoxCols - 1) / kBoxCols;
+    const int boxes = in_range < kBoxes ? in_range : kBoxes;
     mbar_arrive_expect_tx(bar, boxes * kTensors * kBoxBytes);
-    for (int c = 0; c < boxes; ++c) {
-        tma_load_2d(slot + c * kBoxBytes, map_residual, bar, n0 + c * kChunkCols, m0);
-        if constexpr (EPI == kEpiMix) tma_load_2d(slot + (kChunks + c) * kBoxBytes, map_original, bar, n0 + c * kChunkCols, m0);
+    for (int b = 0; b < boxes; ++b) {
+        tma_load_2d(slot + b * kBoxBytes, map_residual, bar, n0 + b * kBoxCols, m0);
+        if constexpr (EPI == kEpiMix) tma_load_2d(slot + (kBoxes + b) * kBoxBytes, map_original, bar, n0 + b * kBoxCols, m0);
     }
 }
 
-// A staged row chunk's two 16-byte halves, the one `swap` names first.
-FRY_DEVICE void read_halves(const uint16_t* chunk, int swap, uint4 (&words)[2]) {
-    const uint4 first = reinterpret_cast<const uint4*>(chunk)[swap], second = reinterpret_cast<const uint4*>(chunk)[swap ^ 1];
-    words[0] = swap ? second : first;
-    words[1] = swap ? first : second;
-}
+// Where one row's 16-column chunk sits in a staged box: its two 16-byte units (2 (chunk % 4) and the next) of the row's
+// 128 bytes, each at its index XOR the row's position in its 8-row swizzle atom.
+struct StagedChunk {
+    uint8_t* row;  // the row's 128 bytes in the box
+    int unit;      // 2 (chunk % 4)
+    int swizzle;   // row % 8
+    FRY_DEVICE uint4* at(int h) const { return reinterpret_cast<uint4*>(row + (((unit + h) ^ swizzle) << 4)); }
+};
 
 // Applies the epilogue to one row's 16 consecutive columns. acc (and up, gated) hold the raw TMEM words, xs the row's
 // activation scale, rs and is the next block's input-mix scales, scale and second the chunk's column operands in shared
-// memory. Staged epilogues read the row's residual (and original) from its 32 staged bytes and write the fp16 results
-// over them, the two 16-byte halves in the order `swap` gives (rows 4 apart alternate, so a warp's accesses spread over
-// all banks); int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
+// memory. Staged epilogues read the row's residual (and original) from its staged chunk and write the fp16 results over
+// it; int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
 template <int EPI>
 FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, const uint32_t (&acc)[16], const uint32_t (&up)[16],
-                           const float* scale, const float* second, uint16_t* staged, const uint16_t* original, int swap, size_t row,
+                           const float* scale, const float* second, const StagedChunk& staged, const StagedChunk& original, size_t row,
                            int valid) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
@@ -141,9 +146,9 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
         constexpr bool kResidual = EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16;
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if constexpr (kResidual) {
-            if (EPI != kEpiLinearF16 || p.residual != nullptr) read_halves(staged, swap, residual_words);
+            if (EPI != kEpiLinearF16 || p.residual != nullptr) residual_words[0] = *staged.at(0), residual_words[1] = *staged.at(1);
         }
-        if constexpr (EPI == kEpiMix) read_halves(original, swap, original_words);
+        if constexpr (EPI == kEpiMix) original_words[0] = *original.at(0), original_words[1] = *original.at(1);
         const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
         const uint16_t* orig = reinterpret_cast<const uint16_t*>(original_words);
         // the chunk's column operands as 4 x float4 each (the chunk starts on a 64-byte boundary of the staged columns)
@@ -190,9 +195,8 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
             const __half2 pair = __floats2half2_rn(values[2 * i], values[2 * i + 1]);
             result[i] = *reinterpret_cast<const uint32_t*>(&pair);
         }
-        const uint4 low = make_uint4(result[0], result[1], result[2], result[3]), high = make_uint4(result[4], result[5], result[6], result[7]);
-        reinterpret_cast<uint4*>(staged)[swap] = swap ? high : low;
-        reinterpret_cast<uint4*>(staged)[swap ^ 1] = swap ? low : high;
+        *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
+        *staged.at(1) = make_uint4(result[4], result[5], result[6], result[7]);
     }
 }
 
@@ -205,8 +209,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* stages = smem;                                              // [kStages][A box | B box(es)]
-    uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kChunks][128 rows][32 bytes]
-    float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][3 * BN]
+    uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kBoxes][128 rows][128 bytes, swizzled]
+    float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][2 * BN]
     uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
@@ -268,7 +272,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         if (elect_one()) {
-            constexpr uint32_t idesc = instr_desc<KIND>(BN);
+            // gated: the gate's and the up's B boxes lie back to back, 2 BN rows at the swizzle's 1024 bytes per 8, so one MMA of
+            // N = 2 BN fills both accumulator halves
+            constexpr uint32_t idesc = instr_desc<KIND>(S::kAccCols);
             int it = 0, local = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
@@ -291,8 +297,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
                         const uint32_t accumulate = (kt > 0 || k > 0) ? 1u : 0u;
                         mma_ss<KIND>(accumulator, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
-                        if constexpr (GATED)
-                            mma_ss<KIND>(accumulator + BN, da, smem_desc_sw128(b + S::kBBytes + k * kMmaKBytes), idesc, accumulate);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -304,7 +308,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // w / 4, w / 4 + 4, ...
         const int quarter = warp & 3, part = warp >> 2;
         const int row_in_tile = quarter * 32 + lane;
-        const int swap = (row_in_tile >> 2) & 1;
         const bool leader = threadIdx.x == 0;  // issues the staged tiles' TMA loads and stores
         float rs = 0.0f, is = 0.0f;
         if constexpr (EPI == kEpiMix) {
@@ -321,37 +324,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tile_origin(blockIdx.x, m0, n0);
             load_tile_rows<EPI, BN>(&map_residual, &map_original, io, &rows_full[0], m0, n0, N);
         }
+        // a tile's column operands and this thread's row scale are fetched during the tile before (the first tile's here),
+        // into the other of two column buffers, so one barrier a tile publishes both the staged outputs and them
+        bool alive = true;
+        float xs_next = 0.0f;
+        auto fetch_operands = [&](int tile, int buffer) {
+            int m0, n0;
+            tile_origin(tile, m0, n0);
+            const int m = m0 + row_in_tile;
+            if constexpr (EPI <= kEpiMix) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
+            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, column_buffers + buffer * 2 * BN, n0, N, threadIdx.x);
+        };
+        fetch_operands(blockIdx.x, 0);
+        epilogue_sync();
         // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
         // epilogue warps never wait at the barrier for it
-        bool alive = true;
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-            const int buffer = local & 1, slot = S::kSlots == 2 ? local & 1 : 0;
+            // tile k stages into slot k % 2, which the stores of tile k - 2 read before the barrier that ended tile k - 1
+            const int buffer = local & 1, slot = local & 1;
+            const int next = tile + static_cast<int>(gridDim.x);
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
             const int c0 = part * kChunkCols;
-            if constexpr (S::kStaged) {
-                if (leader) {
-                    // the last tile's stores have read their slot; the next tile's row operands go into the other one
-                    if (local > 0) bulk_wait_read_all();
-                    if (has_rows && tile + static_cast<int>(gridDim.x) < tiles) {
-                        int next_m0, next_n0;
-                        tile_origin(tile + gridDim.x, next_m0, next_n0);
-                        load_tile_rows<EPI, BN>(&map_residual, &map_original, io + (slot ^ 1) * S::kSlotBytes, &rows_full[slot ^ 1],
-                                                next_m0, next_n0, N);
-                    }
+            const float xs = xs_next;
+            if (leader && has_rows) {
+                // the next tile's row operands into the other slot, once the last tile's stores have read it
+                if (local > 0) bulk_wait_read_all();
+                if (next < tiles) {
+                    int next_m0, next_n0;
+                    tile_origin(next, next_m0, next_n0);
+                    load_tile_rows<EPI, BN>(&map_residual, &map_original, io + (slot ^ 1) * S::kSlotBytes, &rows_full[slot ^ 1], next_m0,
+                                            next_n0, N);
                 }
             }
-            float xs = 0.0f;
-            if constexpr (EPI <= kEpiMix) xs = (alive && m < M) ? args.x_scale[m] : 0.0f;
-            float* columns = column_buffers + buffer * 3 * BN;
-            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, columns, n0, N, threadIdx.x);
-            epilogue_sync();
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             // every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
             if (has_rows && !mbar_wait(&rows_full[slot], (local >> 1) & 1, 14)) alive = false;
             uint8_t* staged_tile = io + slot * S::kSlotBytes;
+            const float* columns = column_buffers + buffer * 2 * BN;
             if (alive) {
                 tc_fence_after();
                 const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -360,12 +372,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tmem_load16(lane_base + c, acc);
                     if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
                     tmem_load_wait();
-                    const int chunk = c / kChunkCols;
-                    uint16_t* staged = reinterpret_cast<uint16_t*>(staged_tile + chunk * kBoxBytes + row_in_tile * 32);
-                    const uint16_t* original = reinterpret_cast<const uint16_t*>(staged_tile + (S::kChunks + chunk) * kBoxBytes + row_in_tile * 32);
+                    const int box = c / kBoxCols, unit = 2 * ((c % kBoxCols) / kChunkCols), swizzle = row_in_tile & 7;
+                    const StagedChunk staged{staged_tile + box * kBoxBytes + row_in_tile * 128, unit, swizzle};
+                    const StagedChunk original{staged_tile + (S::kBoxes + box) * kBoxBytes + row_in_tile * 128, unit, swizzle};
                     const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
                     if (S::kStaged || m < M)
-                        epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original, swap,
+                        epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original,
                                         static_cast<size_t>(m) * N + n0 + c, valid);
                 }
             }
@@ -373,12 +385,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
+            if (next < tiles) fetch_operands(next, buffer ^ 1);
             if constexpr (S::kStaged) {
-                // the staged tile, once every thread's writes are visible to the async proxy, leaves by TMA stores
+                // the stores of tile k - 1 have read slot (k + 1) % 2 before the next tile writes it
+                if (leader && !has_rows) bulk_wait_read_all();
+                // this thread's staged writes, visible to the async proxy before the stores read them
                 fence_proxy_async_shared();
-                epilogue_sync();
+            }
+            epilogue_sync();
+            if constexpr (S::kStaged) {
                 if (leader) {
-                    for (int c = 0; c < BN && n0 + c < N; c += kChunkCols) tma_store_2d(&map_out, staged_tile + (c / kChunkCols) * kBoxBytes, n0 + c, m0);
+                    for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
+                        tma_store_2d(&map_out, staged_tile + b * kBoxBytes, n0 + b * kBoxCols, m0);
                     bulk_commit();
                 }
             }
@@ -433,17 +451,17 @@ bool make_map(CUtensorMap* map, const void* base, int elem_bytes, int k, int row
     return true;
 }
 
-// An fp16 [rows, cols] row-major tensor as a TMA map with a box of 16 columns by 128 rows and no swizzle: the boxes the
-// epilogue stages.
+// An fp16 [rows, cols] row-major tensor as a TMA map with a box of 64 columns by 128 rows in the 128-byte swizzle: the
+// boxes the epilogue stages.
 bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::string* error) {
     EncodeTiled encode = encoder(error);
     if (!encode) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunkCols), static_cast<cuuint32_t>(kBlockM)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(kBlockM)};
     const cuuint32_t element_strides[2] = {1, 1};
     const CUresult result = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, element_strides,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (result != CUDA_SUCCESS) {
         if (error) *error = "cuTensorMapEncodeTiled (fp16 [" + std::to_string(rows) + ", " + std::to_string(cols) +
@@ -482,16 +500,14 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 
 }  // namespace
 
-// Tile widths: 144 divides every projection width 36*dq + 576 for dq in {8, 16, 24}; gate_up's 128 columns hold 256
-// accumulators (its gate and its up); mixing's 64 keep two staged row operands in two slots beside six stages; 128
-// elsewhere. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA stores).
+// Tile widths: whole 64-column staging boxes; gate_up's 128 columns hold 256 accumulators (its gate and its up); mixing's
+// 64 keep two staged row operands in two slots beside six stages; 128 elsewhere. An fp16 output needs N a multiple of 8
+// (its rows 16-byte aligned for the TMA maps).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
     if (kind == 0) {
         switch (epilogue) {
-            case kEpiBias:
-                return N % 144 == 0 ? launch<0, 144, false, kEpiBias>(a, b, args, M, N, K, stream, error)
-                                    : launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
+            case kEpiBias: return launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
             case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
             case kEpiMix: return launch<0, 64, false, kEpiMix>(a, b, args, M, N, K, stream, error);
