@@ -150,26 +150,20 @@ def cpu_baseline() -> dict:
 
 
 def gemm_roofline(torch, stream) -> dict:
-    """The dominant kernel, the int8 tensor-core GEMM, timed alone at the step's shapes (M = 256 x 70 tokens) with CUDA
-    events on its stream: algorithmic int8 ops per launch / mean launch time, against the int8 dense peak."""
+    """The dominant kernel, the int8 tensor-core GEMM, timed alone at the forward's shapes (M = 256 x 70 tokens, the
+    launches of profile_target.GEMMS with their counts per forward) with CUDA events on its stream, L2 flushed before
+    each launch: algorithmic int8 ops per launch / mean launch time, against the int8 dense peak."""
     from chess_transformer_b200 import ops
+    from chess_transformer_b200.profile_target import GEMMS, gemm_runner
     M = BATCH * 70
-    # per forward: projection at dq 8/16/24 (10, 9, 9 of the 28 blocks), gate_up and down in every block
-    shapes = [("projection", 864, 768, False, 10), ("projection", 1152, 768, False, 9), ("projection", 1440, 768, False, 9),
-              ("gate_up", 992, 768, True, 28), ("down", 768, 1024, False, 28)]
-    generator = torch.Generator().manual_seed(0)
     total_ops = total_seconds = 0.0
     per_shape = {}
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     with torch.cuda.stream(stream):
-        for name, N, K, gated, count in shapes:
-            x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
-            w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
-            xs = torch.rand(M, generator=generator).cuda() / 100
-            ws = torch.rand(len(w), generator=generator).cuda() / 100
-            bias = torch.randn(N, generator=generator).half().cuda() if name == "projection" else None
-            residual = torch.randn(M, N, generator=generator).half().cuda() if name == "down" else None
-            run = lambda: ops.int8_linear(x, xs, w, ws, bias, residual, gated, name)
+        for name, (N, K, kind, count) in GEMMS.items():
+            if kind == "fp16":
+                continue
+            run = gemm_runner(torch, ops, name, M)
             for _ in range(3):
                 run()
             times = []
@@ -182,7 +176,7 @@ def gemm_roofline(torch, stream) -> dict:
                 end.synchronize()
                 times.append(start.elapsed_time(end) / 1000)
             seconds = statistics.mean(times)
-            ops_per_launch = 2.0 * M * K * N * (2 if gated else 1)
+            ops_per_launch = 2.0 * M * K * N * (2 if kind == "gated" else 1)
             per_shape[f"{name}_{N}x{K}"] = round(ops_per_launch / seconds / 1e12, 1)
             total_ops += ops_per_launch * count
             total_seconds += seconds * count
@@ -291,7 +285,7 @@ def main() -> None:
             traffic = json.loads(PROFILE_SUMMARY.read_text()).get("dram_bytes_per_launch")
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
                     "frac": round(achieved / int8_peak, 4), "traffic": traffic,
-                    "kernel": "gemm_kernel<kind::i8> (projection, gate_up, down at M=17920)",
+                    "kernel": "gemm_kernel<kind::i8> (projection, gate_up, down at M=17920, weighted by launches per forward)",
                     "peak_source": f"int8 dense = 2 x {peak['source']} cuBLAS bf16 burst ({peak['bf16_tflops']} TFLOP/s), of {peak['source']}",
                     "tops_by_shape": gemm["tops_by_shape"]}
         forward_tops = 12.40e9 * BATCH / (seconds / args.steps) / 1e12

@@ -22,6 +22,7 @@ enum DeviceError : int {
     kWaitTimeout = 1,      // a bounded mbarrier wait gave up
     kBadToken = 2,         // a board token outside the vocabulary
     kBadShape = 3,         // a launch got a shape its kernel does not take
+    kMisaligned = 4,       // dynamic shared memory did not start on the 1024-byte boundary a kernel lays out from
 };
 
 // Set by kernels on a failure they can detect; read and cleared by fry_device_status(). The library is one

@@ -14,10 +14,10 @@
 // next tile fill the other accumulator.
 //
 // fp16 outputs leave through shared memory: a tile is staged as 64-column boxes of 128 rows x 128 bytes in the 128-byte
-// swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread over all banks), which one
-// thread writes to global memory with TMA stores; no thread stores a row of its own. The row operands (residual,
-// original) arrive the same way, as TMA loads of the same boxes one tile ahead into the other of two slots, and each
-// output overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged one tile ahead in
+// swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread over all banks), which warp
+// 18 writes to global memory with TMA stores; no thread stores a row of its own. The row operands (residual, original)
+// arrive the same way, as TMA loads of the same boxes that warp 18 issues a tile ahead into the other of two slots, and
+// each output overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged one tile ahead in
 // shared memory too, so one barrier a tile suffices.
 // No TMA load multicasts.
 #include <mutex>
@@ -33,15 +33,17 @@ constexpr int kTileKBytes = 128;  // one swizzle row: the K bytes a stage holds
 constexpr int kEpilogueWarps = 16;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
 constexpr int kChunkParts = kEpilogueWarps / 4;  // warps sharing one TMEM lane quarter, each taking every kChunkParts-th chunk
-constexpr int kProducerWarp = kEpilogueWarps, kMmaWarp = kEpilogueWarps + 1;
-constexpr int kGemmThreads = (kEpilogueWarps + 2) * 32;
+constexpr int kProducerWarp = kEpilogueWarps, kMmaWarp = kEpilogueWarps + 1, kStoreWarp = kEpilogueWarps + 2;
+constexpr int kGemmThreads = (kEpilogueWarps + 3) * 32;
 constexpr int kMmaKBytes = 32;    // K bytes one MMA instruction consumes (32 int8 or 16 fp16)
-constexpr int kEpilogueBarrier = 1;  // named barrier of the epilogue warps (0 is __syncthreads)
+constexpr int kEpilogueBarrier = 1;  // named barrier of the epilogue warps and the store warp (0 is __syncthreads)
 constexpr int kChunkCols = 16;       // columns of one epilogue chunk (one tcgen05.ld)
 constexpr int kBoxCols = 64;         // columns of one staged box: 128 bytes of fp16, one swizzle row
 constexpr int kBoxBytes = kBlockM * kBoxCols * 2;  // a staged fp16 box: 128 rows x 128 bytes
-// dynamic shared memory a CTA may use (227 KB) less the 1024-byte alignment slack and the barriers
-constexpr int kSmemBudget = 227 * 1024 - 1024 - 256;
+// dynamic shared memory a CTA may use (227 KB) less the barriers. It starts 1024-byte aligned (after the CTA's 1 KB of
+// reserved shared memory), as the 128-byte swizzle atoms need; a kernel checks and records kMisaligned otherwise.
+constexpr int kBarrierBytes = 256;
+constexpr int kSmemBudget = 227 * 1024 - kBarrierBytes;
 
 template <int KIND, int BN, bool GATED, int EPI>
 struct GemmShape {
@@ -69,12 +71,12 @@ struct GemmShape {
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kIoBytes + kStages * kStageBytes + kColumnBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kIoBytes + kStages * kStageBytes + kColumnBytes + kBarrierBytes;
     static_assert(kAccCols % 16 == 0 && kAccCols >= 16 && kAccCols <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
 
-FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads) : "memory"); }
+FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads + 32) : "memory"); }
 
 // The tile's column operands into shared memory (all epilogue threads together): columns[0] the weight scales,
 // columns[1] up's scales (gated) or the bias as floats, zero past N.
@@ -206,8 +208,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_residual,
                 const __grid_constant__ CUtensorMap map_original, const GemmArgs args, int M, int N, int K) {
     using S = GemmShape<KIND, BN, GATED, EPI>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if (smem_addr(smem) & 1023u) {  // uniform across the CTA: every thread leaves before any barrier
+        if (threadIdx.x == 0) record_error(kMisaligned, 20);
+        return;
+    }
     uint8_t* stages = smem;                                              // [kStages][A box | B box(es)]
     uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kBoxes][128 rows][128 bytes, swizzled]
     float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][2 * BN]
@@ -303,12 +308,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 mma_commit(&tmem_full[buffer]);
             }
         }
+    } else if (warp == kStoreWarp) {
+        // the staged tiles' TMA traffic: after tile k's barrier, its stores from slot k % 2; once they have read the slot,
+        // the row operands of tile k + 2 into it (those of tiles 0 and 1 first). Waiting for the reads before the next
+        // barrier also frees the slot for tile k + 2's outputs.
+        if constexpr (S::kStaged) {
+            const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
+            const bool issuer = lane == 0;
+            auto load_rows = [&](int tile, int slot) {
+                if (!issuer || !has_rows || tile >= tiles) return;
+                load_tile_rows<EPI, BN>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
+                                        (tile / n_blocks) * kBlockM, (tile % n_blocks) * BN, N);
+            };
+            load_rows(blockIdx.x, 0);
+            load_rows(blockIdx.x + gridDim.x, 1);
+            epilogue_sync();  // the first tile's column operands are staged
+            int local = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+                const int slot = local & 1;
+                __syncwarp();
+                epilogue_sync();  // tile k is staged
+                if (issuer) {
+                    const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
+                    uint8_t* staged_tile = io + slot * S::kSlotBytes;
+                    for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
+                        tma_store_2d(&map_out, staged_tile + b * kBoxBytes, n0 + b * kBoxCols, m0);
+                    bulk_commit();
+                    bulk_wait_read_all();
+                }
+                load_rows(tile + 2 * gridDim.x, slot);
+            }
+            if (issuer) bulk_wait_all();
+        } else {
+            epilogue_sync();
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) epilogue_sync();
+        }
     } else {
         // warps 0-15: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks
         // w / 4, w / 4 + 4, ...
         const int quarter = warp & 3, part = warp >> 2;
         const int row_in_tile = quarter * 32 + lane;
-        const bool leader = threadIdx.x == 0;  // issues the staged tiles' TMA loads and stores
         float rs = 0.0f, is = 0.0f;
         if constexpr (EPI == kEpiMix) {
             rs = h2f_bits(*args.residual_scale);
@@ -319,11 +358,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             m0 = (tile / n_blocks) * kBlockM;
             n0 = (tile % n_blocks) * BN;
         };
-        if (leader && has_rows && static_cast<int>(blockIdx.x) < tiles) {  // the first tile's row operands
-            int m0, n0;
-            tile_origin(blockIdx.x, m0, n0);
-            load_tile_rows<EPI, BN>(&map_residual, &map_original, io, &rows_full[0], m0, n0, N);
-        }
         // a tile's column operands and this thread's row scale are fetched during the tile before (the first tile's here),
         // into the other of two column buffers, so one barrier a tile publishes both the staged outputs and them
         bool alive = true;
@@ -341,7 +375,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // epilogue warps never wait at the barrier for it
         int local = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-            // tile k stages into slot k % 2, which the stores of tile k - 2 read before the barrier that ended tile k - 1
+            // tile k stages into slot k % 2, which the stores of tile k - 2 had read before the barrier that ended tile k - 1
             const int buffer = local & 1, slot = local & 1;
             const int next = tile + static_cast<int>(gridDim.x);
             int m0, n0;
@@ -349,16 +383,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int m = m0 + row_in_tile;
             const int c0 = part * kChunkCols;
             const float xs = xs_next;
-            if (leader && has_rows) {
-                // the next tile's row operands into the other slot, once the last tile's stores have read it
-                if (local > 0) bulk_wait_read_all();
-                if (next < tiles) {
-                    int next_m0, next_n0;
-                    tile_origin(next, next_m0, next_n0);
-                    load_tile_rows<EPI, BN>(&map_residual, &map_original, io + (slot ^ 1) * S::kSlotBytes, &rows_full[slot ^ 1], next_m0,
-                                            next_n0, N);
-                }
-            }
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             // every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
             if (has_rows && !mbar_wait(&rows_full[slot], (local >> 1) & 1, 14)) alive = false;
@@ -386,22 +410,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
             if (next < tiles) fetch_operands(next, buffer ^ 1);
-            if constexpr (S::kStaged) {
-                // the stores of tile k - 1 have read slot (k + 1) % 2 before the next tile writes it
-                if (leader && !has_rows) bulk_wait_read_all();
-                // this thread's staged writes, visible to the async proxy before the stores read them
-                fence_proxy_async_shared();
-            }
+            // this thread's staged writes, visible to the async proxy before the stores read them
+            if constexpr (S::kStaged) fence_proxy_async_shared();
             epilogue_sync();
-            if constexpr (S::kStaged) {
-                if (leader) {
-                    for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
-                        tma_store_2d(&map_out, staged_tile + b * kBoxBytes, n0 + b * kBoxCols, m0);
-                    bulk_commit();
-                }
-            }
         }
-        if (leader) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();

@@ -1,10 +1,12 @@
-"""A profiling target: the 28-block int8 forward (or one of its kernels) between cudaProfilerStart and cudaProfilerStop,
-so that `ncu --profile-from-start off` captures exactly that work. Warm-up runs happen before the start.
+"""A profiling target: the 28-block int8 forward (or its GEMMs alone) between cudaProfilerStart and cudaProfilerStop, so
+that `ncu --profile-from-start off` captures exactly that work. Warm-up runs happen before the start.
 
     ncu --profile-from-start off --metrics gpu__time_duration.sum --clock-control none --csv \\
         python chess-transformer_b200/profile_target.py --batch 256 --forwards 1
     ncu --profile-from-start off --set full --clock-control none -k regex:gemm_kernel -c 1 -o gpurun_out/gemm \\
         python chess-transformer_b200/profile_target.py --gemm gate_up --batch 256
+    ncu --profile-from-start off --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \\
+        -k regex:gemm_kernel --csv python chess-transformer_b200/profile_target.py --gemm all --batch 256
 """
 import argparse
 import sys
@@ -12,15 +14,44 @@ from pathlib import Path
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
-# the int8 GEMMs of a block at M = batch x 70: (output columns N, depth K, gated)
-GEMMS = {"projection": (1152, 768, False), "gate_up": (992, 768, True), "down": (768, 1024, False)}
+# the GEMMs of a block at M = batch x 70: name -> (output columns N, depth K, kind), and how many of the 28 blocks run
+# each: the projection at dq 8/16/24, gate_up, down mixing the next block's input (the last block's adds its residual
+# only), and the attention-out fp16 linear
+GEMMS = {"projection864": (864, 768, "bias", 10), "projection1152": (1152, 768, "bias", 9), "projection1440": (1440, 768, "bias", 9),
+         "gate_up": (992, 768, "gated", 28), "down": (768, 1024, "mixing", 27), "down_last": (768, 1024, "residual", 1),
+         "combine": (768, 768, "fp16", 28)}
+
+
+def gemm_runner(torch, ops, name: str, M: int):
+    N, K, kind, _ = GEMMS[name]
+    generator = torch.Generator().manual_seed(0)
+    if kind == "fp16":
+        x = torch.randn(M, K, generator=generator).half().cuda()
+        weight = (torch.randn(N, K, generator=generator) / 16).half().cuda()  # [N, K]: the layout the library takes
+        bias = torch.randn(N, generator=generator).half().cuda()
+        residual = torch.randn(M, N, generator=generator).half().cuda()
+        out = torch.empty(M, N, dtype=torch.half, device="cuda")
+        from chess_transformer_b200 import library
+        return lambda: library().fry_linear(x.data_ptr(), weight.data_ptr(), bias.data_ptr(), residual.data_ptr(), out.data_ptr(), M, N,
+                                            K, 0, torch.cuda.current_stream().cuda_stream)
+    gated = kind == "gated"
+    x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
+    w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
+    xs, ws = (torch.rand(M, generator=generator) / 100).cuda(), (torch.rand(len(w), generator=generator) / 100).cuda()
+    bias = torch.randn(N, generator=generator).half().cuda() if kind == "bias" else None
+    residual = torch.randn(M, N, generator=generator).half().cuda() if kind in ("residual", "mixing") else None
+    mix = ()
+    if kind == "mixing":
+        mix = (torch.randn(M, N, generator=generator).half().cuda(), torch.tensor([0.8]).half().cuda(), torch.tensor([0.5]).half().cuda())
+    return lambda: ops.int8_linear(x, xs, w, ws, bias, residual, gated, name, *mix)
 
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--batch", type=int, default=256)
     parser.add_argument("--forwards", type=int, default=1)
-    parser.add_argument("--gemm", choices=sorted(GEMMS), help="profile one int8 GEMM launch instead of the forward")
+    parser.add_argument("--gemm", choices=sorted(GEMMS) + ["all"], help="profile GEMM launches instead of the forward "
+                        "(all: one launch of each, in the order of GEMMS)")
     parser.add_argument("--warmup", type=int, default=2)
     args = parser.parse_args()
 
@@ -31,27 +62,23 @@ def main() -> None:
 
     torch.cuda.set_device(0)
     if args.gemm:
-        N, K, gated = GEMMS[args.gemm]
-        M = args.batch * 70
-        generator = torch.Generator().manual_seed(0)
-        x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
-        w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
-        xs, ws = torch.rand(M).cuda() / 100, torch.rand(len(w)).cuda() / 100
-        bias = torch.randn(N).half().cuda() if args.gemm == "projection" else None
-        residual = torch.randn(M, N).half().cuda() if args.gemm == "down" else None
-        run = lambda: ops.int8_linear(x, xs, w, ws, bias, residual, gated, args.gemm)
+        names = list(GEMMS) if args.gemm == "all" else [args.gemm]
+        runners = [gemm_runner(torch, ops, name, args.batch * 70) for name in names]
+        run_all = lambda: [run() for run in runners]
+        runs = 1
     else:
         state = synthetic_state_dict(FRY_SETTINGS, 0)
         network = Int8Network(state, FRY_SETTINGS, quantize(state, FRY_SETTINGS), "cuda:0")
         boards = torch.from_numpy(random_boards(args.batch, 0)).long().cuda()
-        run = lambda: network(boards)
+        run_all = lambda: network(boards)
+        runs = args.forwards
     with torch.no_grad():
         for _ in range(args.warmup):
-            run()
+            run_all()
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
-        for _ in range(args.forwards if not args.gemm else 1):
-            run()
+        for _ in range(runs):
+            run_all()
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
 
