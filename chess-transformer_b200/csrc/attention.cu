@@ -12,11 +12,13 @@
 // (i0, i1), A = the 8 heads' coefficients block-diagonally over (i0's 8 templates | i1's 8 templates) and B = the pair's
 // templates, paired per key as [square][key][template] (fry_pair_templates, as the reference pairs them,
 // model/attention_cuda.py:412-434), so one m16n8k16 gives 8 heads x 2 squares x 8 keys of bias. Each warp then takes
-// its head's 16 rows: scores over 10 key tiles, bias added from the slab, softmax in registers, P.V with the values'
-// B fragments read by ldmatrix.trans. 70 x 80 scores and 16 x 32 outputs per tile are too small for tcgen05's 128-row
-// tiles; the legacy mma.sync keeps them in registers.
+// its head's 16 rows: scores over 9 key tiles, bias added from the slab, softmax in registers (paired fp32 arithmetic,
+// f32x2), P.V with the values' B fragments read by ldmatrix.trans. The next slab is formed in the same buffer once every
+// warp has added the current one, while the exponentials run. 70 x 80 scores and 16 x 32 outputs per tile are too small
+// for tcgen05's 128-row tiles; the legacy mma.sync keeps them in registers.
 #include <cmath>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,6 +43,42 @@ FRY_DEVICE float quad_sum(float v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     return v + __shfl_xor_sync(0xffffffffu, v, 2);
 }
+// Two fp32 lanes in one 64-bit register, for the paired (f32x2) IEEE adds, multiplies and FMAs of sm_100: each lane
+// rounds exactly as the scalar instruction does.
+FRY_DEVICE uint64_t pair2(float lo, float hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+FRY_DEVICE float2 lanes(uint64_t v) {
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(v));
+    return f;
+}
+FRY_DEVICE float lane0(uint64_t v) { return lanes(v).x; }
+FRY_DEVICE float lane1(uint64_t v) { return lanes(v).y; }
+FRY_DEVICE uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+FRY_DEVICE uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+FRY_DEVICE uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// the fp16 pair (low, high) as two fp32 lanes
+FRY_DEVICE uint64_t widen2(uint32_t pair) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pair));
+    return pair2(f.x, f.y);
+}
+FRY_DEVICE uint32_t narrow2(uint64_t v) { return pack_half2(lane0(v), lane1(v)); }
+
 FRY_DEVICE float quad_max(float v) {
     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
     return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
@@ -96,9 +134,10 @@ FRY_DEVICE void load_queries(uint32_t (&raw)[KS][2][2], const uint16_t* board, i
             }
 }
 
-// DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values [kv][80][40], two bias slabs.
+// DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values [kv][80][40], one bias slab (at most
+// 70 KB, so three CTAs share an SM).
 template <int DQP>
-__global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
+__global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     attention_kernel(const uint16_t* __restrict__ projected, const uint16_t* __restrict__ paired, const uint16_t* __restrict__ q_gain,
                      const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out, int heads, int kv_heads, int dq, float eps, float scale) {
     constexpr int KROW = DQP + 8, KS = DQP / 16;
@@ -108,8 +147,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     const int kv_here = heads_here / group;
     uint16_t* keys = attn_smem;                                   // [kv_here][80][KROW]
     uint16_t* values = keys + kv_here * kAttnKeys * KROW;         // [kv_here][80][kValueRow]
-    uint16_t* bias = values + kv_here * kAttnKeys * kValueRow;    // [2][heads_here][16][kBiasRow]
-    const int slab_size = heads_here * kBiasHead;
+    uint16_t* bias = values + kv_here * kAttnKeys * kValueRow;    // [heads_here][16][kBiasRow]
 
     const int b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int width = (heads + kv_heads) * dq + kv_heads * kAttnDv + heads * kAttnTemplates;
@@ -181,15 +219,15 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     load_queries<KS>(raw_q, board, 0, width, head, dq, g, t);
     __syncthreads();
 
-    for (int phase = 0; phase < 5; ++phase) {
-        const bool squares_phase = phase < 4;
+    const uint64_t scale2 = pair2(scale, scale), log2e2 = pair2(1.4426950408889634f, 1.4426950408889634f);
+    // one phase: 16 query rows from `first`; SQUARES (phases 0-3) adds the slab's template bias, the metadata phase (4)
+    // has none and is the last
+    auto run_phase = [&](auto squares_tag, int phase) {
+        constexpr bool SQUARES = decltype(squares_tag)::value;
         const int first = phase * kSlab;
-        // the next slab's bias into the other buffer, and the next phase's queries, ahead of this phase's work
-        if (phase + 1 < 4)
-            make_bias_slab(bias + ((phase + 1) & 1) * slab_size, board, paired, phase + 1, width, c_offset, first_head, heads_here, warp,
-                           warps, g, t);
+        // the next phase's queries, ahead of this phase's work
         uint32_t next_q[KS][2][2];
-        if (phase + 1 < 5) load_queries<KS>(next_q, board, first + kSlab, width, head, dq, g, t);
+        if (SQUARES) load_queries<KS>(next_q, board, first + kSlab, width, head, dq, g, t);
 
         uint32_t a[KS][4];
 #pragma unroll
@@ -210,60 +248,70 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
                     a[ks][r + 2 * half] = pack_half2(__fmul_rn(__fmul_rn(low_half(raw_q[ks][r][half]), inverse), qg[ks][half][0]),
                                                      __fmul_rn(__fmul_rn(high_half(raw_q[ks][r][half]), inverse), qg[ks][half][1]));
         }
-        // scores over the 9 key tiles that hold real keys (keys 72-79 never exist: their probabilities are 0)
+        // scores over the 9 key tiles that hold real keys (keys 72-79 never exist: their probabilities are 0), as fp32
+        // pairs: s2[j][r] holds row g + 8 r, keys 8 j + 2 t and + 1
         constexpr int kTiles = 9;
-        float s[kTiles][4];
+        uint64_t s2[kTiles][2];
 #pragma unroll
         for (int j = 0; j < kTiles; ++j) {
-            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             const uint16_t* key_row = kv_keys + (j * 8 + g) * KROW + 2 * t;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
-                mma_f16(s[j], a[ks][0], a[ks][1], a[ks][2], a[ks][3], *reinterpret_cast<const uint32_t*>(key_row + ks * 16),
+                mma_f16(c, a[ks][0], a[ks][1], a[ks][2], a[ks][3], *reinterpret_cast<const uint32_t*>(key_row + ks * 16),
                         *reinterpret_cast<const uint32_t*>(key_row + ks * 16 + 8));
+            s2[j][0] = pair2(c[0], c[1]);
+            s2[j][1] = pair2(c[2], c[3]);
         }
         // s * scale + bias (the bias on the square block only), keys 70 and 71 masked
-        const uint16_t* head_bias = bias + (phase & 1) * slab_size + warp * kBiasHead;
-        float top[2] = {-INFINITY, -INFINITY};
+        const uint16_t* head_bias = bias + warp * kBiasHead;
+        const uint64_t masked = pair2(-INFINITY, -INFINITY);
+        uint64_t top2[2] = {masked, masked};
 #pragma unroll
         for (int j = 0; j < kTiles; ++j)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                uint32_t pair = 0u;
-                if (squares_phase && j < 8) pair = *reinterpret_cast<const uint32_t*>(head_bias + (g + 8 * r) * kBiasRow + j * 8 + 2 * t);
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    float value = __fmaf_rn(s[j][2 * r + e], scale, e ? high_half(pair) : low_half(pair));
-                    if (j == kTiles - 1 && 2 * t + e >= kAttnTokens - 64) value = -INFINITY;
-                    s[j][2 * r + e] = value;
-                    top[r] = fmaxf(top[r], value);
-                }
+                uint64_t b2 = 0;  // +0.0 in both lanes
+                if (SQUARES && j < 8) b2 = widen2(*reinterpret_cast<const uint32_t*>(head_bias + (g + 8 * r) * kBiasRow + j * 8 + 2 * t));
+                uint64_t v = fma2(s2[j][r], scale2, b2);
+                if (j == kTiles - 1 && t == 3) v = masked;  // keys 70, 71
+                s2[j][r] = v;
+                top2[r] = pair2(fmaxf(lane0(top2[r]), lane0(v)), fmaxf(lane1(top2[r]), lane1(v)));
             }
-        float total[2] = {0.0f, 0.0f}, shift[2];
+        // every warp has read this slab: the next one takes its place while the exponentials run
+        if (SQUARES && phase + 1 < 4) {
+            __syncthreads();
+            make_bias_slab(bias, board, paired, phase + 1, width, c_offset, first_head, heads_here, warp, warps, g, t);
+        }
+        uint64_t shift2[2];
+        float top[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            top[r] = quad_max(top[r]);
-            shift[r] = -top[r] * 1.4426950408889634f;
+            top[r] = quad_max(fmaxf(lane0(top2[r]), lane1(top2[r])));
+            const float shift = -top[r] * 1.4426950408889634f;
+            shift2[r] = pair2(shift, shift);
         }
+        uint64_t total2[2] = {0, 0};
 #pragma unroll
         for (int j = 0; j < kTiles; ++j)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p = ex2_approx(__fmaf_rn(s[j][e], 1.4426950408889634f, shift[e >> 1]));  // e^(s - top)
-                s[j][e] = p;
-                total[e >> 1] = __fadd_rn(total[e >> 1], p);
+            for (int r = 0; r < 2; ++r) {
+                const uint64_t x = fma2(s2[j][r], log2e2, shift2[r]);  // (s - top) log2 e
+                const uint64_t p = pair2(ex2_approx(lane0(x)), ex2_approx(lane1(x)));
+                s2[j][r] = p;
+                total2[r] = add2(total2[r], p);
             }
         float inverse[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) inverse[r] = __frcp_rn(quad_sum(total[r]));
+        for (int r = 0; r < 2; ++r) inverse[r] = __frcp_rn(quad_sum(__fadd_rn(lane0(total2[r]), lane1(total2[r]))));
         float o[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < 5; ++kk) {
-            const uint32_t p0 = pack_half2(s[2 * kk][0], s[2 * kk][1]), p1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
-            const uint32_t p2 = 2 * kk + 1 < kTiles ? pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]) : 0u;
-            const uint32_t p3 = 2 * kk + 1 < kTiles ? pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]) : 0u;
+            const uint32_t p0 = narrow2(s2[2 * kk][0]), p1 = narrow2(s2[2 * kk][1]);
+            const uint32_t p2 = 2 * kk + 1 < kTiles ? narrow2(s2[2 * kk + 1][0]) : 0u;
+            const uint32_t p3 = 2 * kk + 1 < kTiles ? narrow2(s2[2 * kk + 1][1]) : 0u;
 #pragma unroll
             for (int n = 0; n < 4; n += 2) {
                 const uint16_t* rows = kv_values + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kValueRow + n * 8 + (lane >> 4) * 8;
@@ -280,20 +328,23 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             const int row = first + g + 8 * r;
             if (row >= kAttnTokens) continue;
             uint16_t* to = out + (static_cast<size_t>(b) * kAttnTokens + row) * (heads * kAttnDv) + head * kAttnDv + 2 * t;
+            const uint64_t inverse2 = pair2(inverse[r], inverse[r]);
 #pragma unroll
             for (int n = 0; n < 4; ++n)
-                *reinterpret_cast<uint32_t*>(to + n * 8) = pack_half2(__fmul_rn(o[n][2 * r], inverse[r]), __fmul_rn(o[n][2 * r + 1], inverse[r]));
+                *reinterpret_cast<uint32_t*>(to + n * 8) = narrow2(mul2(pair2(o[n][2 * r], o[n][2 * r + 1]), inverse2));
         }
-        if (phase + 1 < 5) {
+        if (SQUARES) {
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
                     for (int half = 0; half < 2; ++half) raw_q[ks][r][half] = next_q[ks][r][half];
+            __syncthreads();
         }
-        __syncthreads();
-    }
+    };
+    for (int phase = 0; phase < 4; ++phase) run_phase(std::true_type{}, phase);
+    run_phase(std::false_type{}, 4);
 }
 
 cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream) {
@@ -321,7 +372,7 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     const dim3 grid(heads / per_cta, B);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
-                          2 * static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
+                          static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
     if (dqp == 16) {
         const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<16>), static_cast<int>(bytes));
         if (attribute != cudaSuccess) return attribute;
