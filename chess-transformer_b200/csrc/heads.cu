@@ -7,9 +7,10 @@
 //   logit[f, t] = a_f . y_t + s_f, gathered to the 1968 moves, promotions plus their piece's logit at the landing square;
 //   value = Linear(GELU(Linear(GELU(board-down) flattened))) ; score = softmax(value) . bin centres.
 //
-// Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel, policy_kernel (per board: the 64x64
-// logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay fp32-exact), eval_linear_kernel (the eval head's
-// two layers over all boards), expected_score_kernel (softmax times the bin centres). fp32 arithmetic throughout, where the
+// Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel (also the eval head's GELU'd inputs),
+// policy_kernel (per board: the 64x64 logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay
+// fp32-exact), the eval head's two layers as split-K partial products (linear_split_kernel) summed in a fixed order by
+// linear_sum_kernel, expected_score_kernel (softmax times the bin centres). fp32 arithmetic throughout, where the
 // reference uses tf32 matmuls.
 #include <string>
 
@@ -20,35 +21,66 @@
 namespace fry {
 
 constexpr int kHeadTokens = 70, kHeadSquares = 64, kNarrow = 21, kNarrowStride = 24, kDown = 16, kMoves = 1968;
+constexpr int kEvalInputs = kHeadTokens * kDown;  // the eval head's first layer takes 70 x 16 GELU'd board-down units
 constexpr float kLoScale = 2048.0f;
+constexpr int kSplitTile = 32;  // linear_split_kernel: 32 boards x 32 outputs a CTA, K in steps of 32
 
-size_t heads_workspace_bytes(int B, int D) {
-    const size_t M = static_cast<size_t>(B) * kHeadTokens;
-    auto up = [](size_t bytes) { return (bytes + 255) / 256 * 256; };
-    // y, a, narrow, then the eval head's hidden units [B, D] and value logits [B, up to 256 bins]
-    return up(M * D * 2) + up(M * D * 4) + up(M * kNarrowStride * 4) + up(static_cast<size_t>(B) * (D + 256) * 4);
+FRY_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+size_t heads_workspace_bytes(int B, int D) { return heads_workspace_bytes_of(B, D); }
+
+// The warp's 32 lanes each hold 32 partial sums v[0..31]; afterwards lane j holds the total of v[j] over the lanes
+// (halving exchanges: 31 shuffles where 32 separate reductions take 160).
+FRY_DEVICE float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+        const bool upper = (lane & width) != 0;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            // keep v[i] (lower lanes) or v[i + width] (upper lanes); send the other half to the partner
+            const float send = upper ? v[i] : v[i + width];
+            const float keep = upper ? v[i + width] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, width));
+        }
+    }
+    return v[0];
 }
 
-// narrow[m, 0..20] = y[m] . N^T + n_bias, 8 warps a CTA, the weights staged in shared memory.
+// narrow[m, 0..20] = y[m] . N^T + n_bias for two rows a warp at a time, 8 warps a CTA, the weights staged in shared
+// memory; eval_in[b, t * 16 + i] = GELU(narrow[b * 70 + t, 5 + i]), the eval head's inputs, once per board.
 __global__ void __launch_bounds__(256) narrow_kernel(const uint16_t* __restrict__ y, const float* __restrict__ weight,
-                                                     const float* __restrict__ bias, float* __restrict__ narrow, int M, int D) {
+                                                     const float* __restrict__ bias, float* __restrict__ narrow,
+                                                     float* __restrict__ eval_in, int M, int D) {
     extern __shared__ float narrow_weights[];  // [21][D]
     for (int i = threadIdx.x; i < kNarrow * D; i += blockDim.x) narrow_weights[i] = weight[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = blockIdx.x * 8 + warp; m < M; m += gridDim.x * 8) {
-        float acc[kNarrow];
+    for (int m = (blockIdx.x * 8 + warp) * 2; m < M; m += gridDim.x * 16) {
+        const bool second = m + 1 < M;
+        float acc[2][32];
 #pragma unroll
-        for (int j = 0; j < kNarrow; ++j) acc[j] = 0.0f;
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[r][j] = 0.0f;
         for (int k = lane; k < D; k += 32) {
-            const float v = h2f_bits(y[static_cast<size_t>(m) * D + k]);
+            const float v0 = h2f_bits(y[static_cast<size_t>(m) * D + k]);
+            const float v1 = second ? h2f_bits(y[static_cast<size_t>(m + 1) * D + k]) : 0.0f;
 #pragma unroll
-            for (int j = 0; j < kNarrow; ++j) acc[j] = __fmaf_rn(v, narrow_weights[j * D + k], acc[j]);
+            for (int j = 0; j < kNarrow; ++j) {
+                const float w = narrow_weights[j * D + k];
+                acc[0][j] = __fmaf_rn(v0, w, acc[0][j]);
+                acc[1][j] = __fmaf_rn(v1, w, acc[1][j]);
+            }
         }
 #pragma unroll
-        for (int j = 0; j < kNarrow; ++j) {
-            const float total = warp_sum(acc[j]);
-            if (lane == j) narrow[static_cast<size_t>(m) * kNarrowStride + j] = __fadd_rn(total, bias[j]);
+        for (int r = 0; r < 2; ++r) {
+            const int row = m + r;
+            const float total = reduce_scatter32(acc[r], lane);  // lane j: output j
+            if (row < M && lane < kNarrow) {
+                const float value = __fadd_rn(total, bias[lane]);
+                narrow[static_cast<size_t>(row) * kNarrowStride + lane] = value;
+                if (lane >= 5) eval_in[static_cast<size_t>(row / kHeadTokens) * kEvalInputs + (row % kHeadTokens) * kDown + lane - 5] = gelu(value);
+            }
         }
     }
 }
@@ -80,18 +112,33 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 #pragma unroll
         for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
     const float* a_rows[2] = {a + (board + m_tile * 16 + g) * D, a + (board + m_tile * 16 + g + 8) * D};
-    for (int k = 0; k < D; k += 16) {
-        uint32_t ah[4], al[4];
-        split_pair(*reinterpret_cast<const float2*>(a_rows[0] + k + 2 * t), ah[0], al[0]);
-        split_pair(*reinterpret_cast<const float2*>(a_rows[1] + k + 2 * t), ah[1], al[1]);
-        split_pair(*reinterpret_cast<const float2*>(a_rows[0] + k + 8 + 2 * t), ah[2], al[2]);
-        split_pair(*reinterpret_cast<const float2*>(a_rows[1] + k + 8 + 2 * t), ah[3], al[3]);
+    // the operands of step k + 16 load while step k's MMAs run
+    float2 a_next[4];
+    uint32_t y_next[4][2];
+    auto fetch = [&](int k) {
+        a_next[0] = *reinterpret_cast<const float2*>(a_rows[0] + k + 2 * t);
+        a_next[1] = *reinterpret_cast<const float2*>(a_rows[1] + k + 2 * t);
+        a_next[2] = *reinterpret_cast<const float2*>(a_rows[0] + k + 8 + 2 * t);
+        a_next[3] = *reinterpret_cast<const float2*>(a_rows[1] + k + 8 + 2 * t);
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
             const uint16_t* y_row = y + (board + (n_first + n) * 8 + g) * D + k + 2 * t;
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(y_row), b1 = *reinterpret_cast<const uint32_t*>(y_row + 8);
-            mma_f16_heads(hi[n], ah, b0, b1);
-            mma_f16_heads(lo[n], al, b0, b1);
+            y_next[n][0] = *reinterpret_cast<const uint32_t*>(y_row);
+            y_next[n][1] = *reinterpret_cast<const uint32_t*>(y_row + 8);
+        }
+    };
+    fetch(0);
+    for (int k = 0; k < D; k += 16) {
+        uint32_t ah[4], al[4], yb[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) split_pair(a_next[i], ah[i], al[i]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) yb[n][0] = y_next[n][0], yb[n][1] = y_next[n][1];
+        if (k + 16 < D) fetch(k + 16);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+            mma_f16_heads(hi[n], ah, yb[n][0], yb[n][1]);
+            mma_f16_heads(lo[n], al, yb[n][0], yb[n][1]);
         }
     }
 #pragma unroll
@@ -112,56 +159,56 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
     }
 }
 
-FRY_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-
-// The eval head's two layers as one tiled fp32 kernel over all boards, 32 boards x 32 outputs a CTA, 2 x 2 a thread:
-//   FROM_NARROW: out[b, u] = GELU(bias[u] + sum_i W[u, i] * GELU(narrow[b, i / 16, 5 + i % 16]))   (K = 70 x 16)
-//   otherwise:   out[b, u] = bias[u] + sum_i W[u, i] * x[b, i]                                    (K = d)
-template <bool FROM_NARROW>
-__global__ void __launch_bounds__(256) eval_linear_kernel(const float* __restrict__ x, const float* __restrict__ weight,
-                                                          const float* __restrict__ bias, float* __restrict__ out, int B, int K, int N) {
-    constexpr int TB = 32, TU = 32, TK = 32;
-    __shared__ float xs[TK][TB + 1];
-    __shared__ float ws[TK][TU + 1];
+// One split of an fp32 linear layer: partial[split, b, u] = sum over inputs i of split's K range of W[u, i] * x[b, i], for
+// x [B, K] and W [N, K] row-major; a CTA takes 32 boards x 32 outputs of one split, 2 x 2 a thread.
+__global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ x, const float* __restrict__ weight,
+                                                           float* __restrict__ partial, int B, int K, int N, int k_split) {
+    __shared__ float xs[kSplitTile][kSplitTile + 1];
+    __shared__ float ws[kSplitTile][kSplitTile + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int b0 = blockIdx.y * TB, u0 = blockIdx.x * TU;
+    const int b0 = blockIdx.y * kSplitTile, u0 = blockIdx.x * kSplitTile;
+    const int k_begin = blockIdx.z * k_split, k_end = min(K, k_begin + k_split);
     float acc[2][2] = {};
-    for (int k0 = 0; k0 < K; k0 += TK) {
-        for (int i = threadIdx.x; i < TK * TB; i += 256) {
-            const int kk = i % TK, bb = i / TK, input = k0 + kk, board = b0 + bb;
-            float v = 0.0f;
-            if (board < B && input < K) {
-                if constexpr (FROM_NARROW)
-                    v = gelu(x[(static_cast<size_t>(board) * kHeadTokens + input / kDown) * kNarrowStride + 5 + input % kDown]);
-                else
-                    v = x[static_cast<size_t>(board) * K + input];
-            }
-            xs[kk][bb] = v;
-        }
-        for (int i = threadIdx.x; i < TK * TU; i += 256) {
-            const int kk = i % TK, uu = i / TK, input = k0 + kk, unit = u0 + uu;
-            ws[kk][uu] = (unit < N && input < K) ? weight[static_cast<size_t>(unit) * K + input] : 0.0f;
+    for (int k0 = k_begin; k0 < k_end; k0 += kSplitTile) {
+        for (int i = threadIdx.x; i < kSplitTile * kSplitTile; i += 256) {
+            const int kk = i % kSplitTile, row = i / kSplitTile, input = k0 + kk;
+            const int board = b0 + row, unit = u0 + row;
+            xs[kk][row] = (board < B && input < k_end) ? x[static_cast<size_t>(board) * K + input] : 0.0f;
+            ws[kk][row] = (unit < N && input < k_end) ? weight[static_cast<size_t>(unit) * K + input] : 0.0f;
         }
         __syncthreads();
 #pragma unroll 8
-        for (int kk = 0; kk < TK; ++kk)
+        for (int kk = 0; kk < kSplitTile; ++kk)
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
                 for (int j = 0; j < 2; ++j) acc[i][j] = __fmaf_rn(xs[kk][ty * 2 + i], ws[kk][tx * 2 + j], acc[i][j]);
         __syncthreads();
     }
+    float* out = partial + static_cast<size_t>(blockIdx.z) * B * N;
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int board = b0 + ty * 2 + i, unit = u0 + tx * 2 + j;
-            if (board < B && unit < N) {
-                const float value = __fadd_rn(acc[i][j], bias[unit]);
-                out[static_cast<size_t>(board) * N + unit] = FROM_NARROW ? gelu(value) : value;
-            }
+            if (board < B && unit < N) out[static_cast<size_t>(board) * N + unit] = acc[i][j];
         }
 }
+
+// out[b, u] = act(bias[u] + sum over splits s = 0, 1, ... of partial[s, b, u]), GELU when GELU.
+template <bool GELU>
+__global__ void __launch_bounds__(256) linear_sum_kernel(const float* __restrict__ partial, const float* __restrict__ bias,
+                                                         float* __restrict__ out, int B, int N, int splits) {
+    const int index = blockIdx.x * blockDim.x + threadIdx.x;
+    if (index >= B * N) return;
+    float total = partial[index];
+    for (int split = 1; split < splits; ++split) total = __fadd_rn(total, partial[static_cast<size_t>(split) * B * N + index]);
+    const float value = __fadd_rn(total, bias[index % N]);
+    out[index] = GELU ? gelu(value) : value;
+}
+
+// Splits of K for the eval head's layers: about 160 inputs a CTA, whole 32-input steps.
+inline int split_size(int K) { return (K + kEvalSplitsMax - 1) / kEvalSplitsMax < 160 ? 160 : ((K + kEvalSplitsMax - 1) / kEvalSplitsMax + 31) / 32 * 32; }
 
 // One warp per board: the softmax of its value logits times the bin centres (2i + 1) / 2bins, into the row's last column.
 __global__ void __launch_bounds__(256) expected_score_kernel(const float* __restrict__ logits, float* __restrict__ rows, int B, int bins) {
@@ -194,12 +241,15 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
         return cudaErrorInvalidValue;
     }
     const int M = B * kHeadTokens;
-    auto up = [](size_t bytes) { return (bytes + 255) / 256 * 256; };
+    const HeadsWorkspace layout(B, D);
     uint8_t* base = static_cast<uint8_t*>(workspace);
-    uint16_t* y = reinterpret_cast<uint16_t*>(base);
-    float* a = reinterpret_cast<float*>(base + up(static_cast<size_t>(M) * D * 2));
-    float* narrow = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a) + up(static_cast<size_t>(M) * D * 4));
-    float* hidden = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(narrow) + up(static_cast<size_t>(M) * kNarrowStride * 4));
+    uint16_t* y = reinterpret_cast<uint16_t*>(base + layout.y);
+    float* a = reinterpret_cast<float*>(base + layout.a);
+    float* narrow = reinterpret_cast<float*>(base + layout.narrow);
+    float* eval_in = reinterpret_cast<float*>(base + layout.eval_in);
+    float* partial = reinterpret_cast<float*>(base + layout.partial);
+    float* hidden = reinterpret_cast<float*>(base + layout.hidden);
+    float* value_logits = reinterpret_cast<float*>(base + layout.logits);
 
     cudaError_t status = rms_norm_f16(stream_x, w.ln_gain, eps, y, M, D, stream);
     if (status != cudaSuccess) return status;
@@ -211,14 +261,18 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     const size_t narrow_smem = static_cast<size_t>(kNarrow) * D * sizeof(float);
     status = ensure_smem(reinterpret_cast<const void*>(narrow_kernel), static_cast<int>(narrow_smem));
     if (status != cudaSuccess) return status;
-    const int narrow_blocks = (M + 31) / 32 < 148 * 4 ? (M + 31) / 32 : 148 * 4;
-    narrow_kernel<<<narrow_blocks, 256, narrow_smem, stream>>>(y, w.narrow_weight, w.narrow_bias, narrow, M, D);
+    const int narrow_blocks = (M + 15) / 16 < 148 * 3 ? (M + 15) / 16 : 148 * 3;
+    narrow_kernel<<<narrow_blocks, 256, narrow_smem, stream>>>(y, w.narrow_weight, w.narrow_bias, narrow, eval_in, M, D);
     policy_kernel<<<B, 256, 0, stream>>>(a, y, narrow, rows, D);
-    float* value_logits = hidden + static_cast<size_t>(B) * D;
-    eval_linear_kernel<true><<<dim3((D + 31) / 32, (B + 31) / 32), 256, 0, stream>>>(narrow, w.hidden_weight, w.hidden_bias, hidden, B,
-                                                                                      kHeadTokens * kDown, D);
-    eval_linear_kernel<false><<<dim3((w.bins + 31) / 32, (B + 31) / 32), 256, 0, stream>>>(hidden, w.out_weight, w.out_bias, value_logits, B,
-                                                                                          D, w.bins);
+    // the eval head: hidden = GELU(W1 . eval_in + b1), logits = W2 . hidden + b2, each as split-K partial products
+    const int split1 = split_size(kEvalInputs), splits1 = (kEvalInputs + split1 - 1) / split1;
+    linear_split_kernel<<<dim3((D + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits1), 256, 0, stream>>>(
+        eval_in, w.hidden_weight, partial, B, kEvalInputs, D, split1);
+    linear_sum_kernel<true><<<(B * D + 255) / 256, 256, 0, stream>>>(partial, w.hidden_bias, hidden, B, D, splits1);
+    const int split2 = split_size(D), splits2 = (D + split2 - 1) / split2;
+    linear_split_kernel<<<dim3((w.bins + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits2), 256, 0, stream>>>(
+        hidden, w.out_weight, partial, B, D, w.bins, split2);
+    linear_sum_kernel<false><<<(B * w.bins + 255) / 256, 256, 0, stream>>>(partial, w.out_bias, value_logits, B, w.bins, splits2);
     expected_score_kernel<<<(B + 7) / 8, 256, 0, stream>>>(value_logits, rows, B, w.bins);
     return cudaGetLastError();
 }

@@ -64,6 +64,19 @@ struct HeadWeights {
     const float* out_bias;           // fp32 [bins]
     int bins;
 };
+// The heads' scratch, each region 256-byte aligned: y fp16 and a fp32 per token row, narrow (24 floats a token row), the
+// eval head's GELU'd inputs (70 x 16 a board), its split-K partial sums (up to kEvalSplitsMax splits of B x max(D, 256)),
+// its hidden units [B, D] and its value logits [B, up to 256 bins].
+constexpr int kEvalSplitsMax = 8;
+struct HeadsWorkspace {
+    size_t y, a, narrow, eval_in, partial, hidden, logits, total;
+    static constexpr size_t up(size_t bytes) { return (bytes + 255) / 256 * 256; }
+    constexpr HeadsWorkspace(size_t B, size_t D)
+        : y(0), a(up(B * 70 * D * 2)), narrow(a + up(B * 70 * D * 4)), eval_in(narrow + up(B * 70 * 24 * 4)),
+          partial(eval_in + up(B * 70 * 16 * 4)), hidden(partial + up(kEvalSplitsMax * B * (D > 256 ? D : 256) * 4)),
+          logits(hidden + up(B * D * 4)), total(logits + up(B * 256 * 4)) {}
+};
+constexpr size_t heads_workspace_bytes_of(size_t B, size_t D) { return HeadsWorkspace(B, D).total; }
 size_t heads_workspace_bytes(int B, int D);
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
                   int D, cudaStream_t stream, std::string* error);

@@ -27,13 +27,8 @@ namespace fry {
 constexpr int kNoAllocMaxBoards = FRY_HEADS_NOALLOC_MAX_BOARDS;
 constexpr int kNoAllocMaxWidth = FRY_HEADS_NOALLOC_MAX_D_MODEL;
 
-// heads_workspace_bytes(kNoAllocMaxBoards, kNoAllocMaxWidth), as a constant: y fp16 and a fp32 per token row, the narrow
-// outputs (24 floats a token row), the eval head's units and up to 256 value logits a board, each region 256-aligned
-constexpr size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
-constexpr size_t kNoAllocRows = static_cast<size_t>(kNoAllocMaxBoards) * 70;
-constexpr size_t kHeadsScratchBytes = round256(kNoAllocRows * kNoAllocMaxWidth * 2) + round256(kNoAllocRows * kNoAllocMaxWidth * 4) +
-                                      round256(kNoAllocRows * 24 * 4) +
-                                      round256(static_cast<size_t>(kNoAllocMaxBoards) * (kNoAllocMaxWidth + 256) * 4);
+// heads_workspace_bytes(kNoAllocMaxBoards, kNoAllocMaxWidth), as a constant
+constexpr size_t kHeadsScratchBytes = heads_workspace_bytes_of(kNoAllocMaxBoards, kNoAllocMaxWidth);
 
 static __device__ __align__(256) uint8_t g_heads_scratch[kHeadsScratchBytes];
 

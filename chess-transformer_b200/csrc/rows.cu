@@ -311,9 +311,14 @@ __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restric
         unpack8(*reinterpret_cast<const uint4*>(position + static_cast<size_t>(t) * D + col), p);
         float features[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (t < kSquares) {
+            // all 23 rows in flight before the first add; the adds keep the feature order
+            uint4 raw[kFeatures];
+#pragma unroll
+            for (int f = 0; f < kFeatures; ++f) raw[f] = *reinterpret_cast<const uint4*>(table + static_cast<size_t>(rows[t][f]) * D + col);
+#pragma unroll
             for (int f = 0; f < kFeatures; ++f) {
                 float row[8];
-                unpack8(*reinterpret_cast<const uint4*>(table + static_cast<size_t>(rows[t][f]) * D + col), row);
+                unpack8(raw[f], row);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) features[i] = __fadd_rn(features[i], row[i]);
             }

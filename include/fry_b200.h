@@ -116,7 +116,7 @@ int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float*
  * thread in the middle of a stream capture, where cudaMalloc is not allowed; a latency-bound search loop that must not
  * risk the device-wide synchronisation an allocation can cause; a host in another language with no device allocator).
  * No counterpart in the reference: its heads always allocate through torch.
- * The scratch is a fixed array inside the library (about 5.1 MiB, held by every GPU that loads the library until
+ * The scratch is a fixed array inside the library (about 5.5 MiB, held by every GPU that loads the library until
  * exit), so a call takes at most FRY_HEADS_NOALLOC_MAX_BOARDS boards of d_model up to FRY_HEADS_NOALLOC_MAX_D_MODEL;
  * larger calls return FRY_ERROR_SHAPE before anything is enqueued. All calls on a device share the array, which keeps
  * the last call's contents: calls whose work overlaps on the GPU race and must be ordered by the caller. The first call
