@@ -202,6 +202,34 @@ __host__ __device__ constexpr uint32_t instr_desc(int n) {
 
 // ---- small numeric helpers -----------------------------------------------------------------------------
 
+// Two fp32 lanes in one 64-bit register, for the paired (f32x2) IEEE adds, multiplies and FMAs of sm_100: each lane
+// rounds exactly as the scalar instruction does.
+FRY_DEVICE uint64_t pair2(float lo, float hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+FRY_DEVICE float2 lanes(uint64_t v) {
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(v));
+    return f;
+}
+FRY_DEVICE uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+FRY_DEVICE uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+FRY_DEVICE uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 FRY_DEVICE float ex2_approx(float x) {
     float y;
     asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -10,105 +10,57 @@
 //                       feature rows of `SquareFeatures.indices` (model/model.py:147-169), found in-kernel from the board.
 #include "common.cuh"
 #include "kernels.h"
+#include "rowops.cuh"
 
 namespace fry {
 
 constexpr int kRowWarps = 8;
-
-FRY_DEVICE void unpack8(const uint4& u, float (&v)[8]) {
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(&u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = h2f_bits(h[i]);
-}
+constexpr int kRowCtasPerSm = 3;  // persistent row kernels: CTAs of kRowWarps warps an SM
 
 // x [M, D] fp16 -> q [M, D] int8, scale [M]; with MIX, x is first mixed with original and the mix stored to mixed.
-// A warp takes ROWS consecutive rows and issues all their loads (and the gain's) before working on any, so the row
-// latencies overlap; each row's arithmetic is the single-row order: per lane over its chunks, then the warp's tree.
-template <int CHUNKS, bool MIX, int ROWS>
-__global__ void __launch_bounds__(kRowWarps * 32) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
+// Persistent warps: warp w of W takes rows w, w + W, ..., loading the next row while it works on this one. A row's
+// arithmetic is the single-row order: per lane over its chunks, then the warp's tree.
+template <int CHUNKS, bool MIX>
+__global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
                                                                     const uint16_t* residual_scale, const uint16_t* input_scale,
                                                                     const uint16_t* __restrict__ gain, float eps, uint16_t* mixed,
                                                                     int8_t* __restrict__ q, float* __restrict__ scale, int M, int D) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int first_row = (blockIdx.x * kRowWarps + warp) * ROWS;
-    if (first_row >= M) return;
+    const int lane = threadIdx.x & 31;
+    const int stride = gridDim.x * kRowWarps;
+    int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    if (row >= M) return;
     float rs = 0.0f, is = 0.0f;
     if constexpr (MIX) {
         rs = h2f_bits(*residual_scale);
         is = h2f_bits(*input_scale);
     }
-    uint4 raw[ROWS][CHUNKS], raw_original[MIX ? ROWS : 1][CHUNKS], raw_gain[CHUNKS];
+    const uint64_t rs2 = pair2(rs, rs), is2 = pair2(is, is);
+    uint4 raw_gain[CHUNKS], raw[CHUNKS], raw_original[MIX ? CHUNKS : 1];
+    auto load_row = [&](int r, uint4 (&to)[CHUNKS], uint4 (&to_original)[MIX ? CHUNKS : 1]) {
+#pragma unroll
+        for (int c = 0; c < CHUNKS; ++c) {
+            const int col = (c * 32 + lane) * 8;
+            const size_t at = static_cast<size_t>(r) * D + col;
+            to[c] = col < D ? *reinterpret_cast<const uint4*>(x + at) : make_uint4(0, 0, 0, 0);
+            if constexpr (MIX) to_original[c] = col < D ? *reinterpret_cast<const uint4*>(original + at) : make_uint4(0, 0, 0, 0);
+        }
+    };
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
         raw_gain[c] = col < D ? *reinterpret_cast<const uint4*>(gain + col) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-            const bool ok = col < D && first_row + r < M;
-            const size_t at = static_cast<size_t>(first_row + r) * D + col;
-            raw[r][c] = ok ? *reinterpret_cast<const uint4*>(x + at) : make_uint4(0, 0, 0, 0);
-            if constexpr (MIX) raw_original[r][c] = ok ? *reinterpret_cast<const uint4*>(original + at) : make_uint4(0, 0, 0, 0);
-        }
     }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        const int row = first_row + r;
-        if (row >= M) break;  // uniform across the warp
+    load_row(row, raw, raw_original);
+    for (; row < M; row += stride) {  // uniform across the warp
+        uint4 next[CHUNKS], next_original[MIX ? CHUNKS : 1];
+        if (row + stride < M) load_row(row + stride, next, next_original);
         const size_t base = static_cast<size_t>(row) * D;
-        float v[CHUNKS][8];
-        float squares = 0.0f;
+        norm_quant_row<CHUNKS, MIX>(raw, raw_original, raw_gain, rs2, is2, eps, D, lane, mixed + base, q + base, scale + row);
 #pragma unroll
         for (int c = 0; c < CHUNKS; ++c) {
-            const int col = (c * 32 + lane) * 8;
-            unpack8(raw[r][c], v[c]);
-            if (col < D) {
-                if constexpr (MIX) {
-                    float o[8];
-                    unpack8(raw_original[r][c], o);
-                    uint16_t packed[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        packed[i] = f2h_bits(__fmaf_rn(rs, v[c][i], __fmul_rn(is, o[i])));
-                        v[c][i] = h2f_bits(packed[i]);
-                    }
-                    *reinterpret_cast<uint4*>(mixed + base + col) = *reinterpret_cast<const uint4*>(packed);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) squares = __fmaf_rn(v[c][i], v[c][i], squares);
-            }
+            raw[c] = next[c];
+            if constexpr (MIX) raw_original[c] = next_original[c];
         }
-        squares = warp_sum(squares);
-        const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(D)), eps));
-        float absmax = 0.0f;
-#pragma unroll
-        for (int c = 0; c < CHUNKS; ++c) {
-            const int col = (c * 32 + lane) * 8;
-            if (col < D) {
-                float g[8];
-                unpack8(raw_gain[c], g);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    v[c][i] = __fmul_rn(__fmul_rn(v[c][i], inverse), g[i]);
-                    absmax = fmaxf(absmax, fabsf(v[c][i]));
-                }
-            }
-        }
-        absmax = fmaxf(warp_max(absmax), 1e-20f);
-        const float step_inverse = __fdiv_rn(127.0f, absmax);
-#pragma unroll
-        for (int c = 0; c < CHUNKS; ++c) {
-            const int col = (c * 32 + lane) * 8;
-            if (col < D) {
-                uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int value = __float2int_rn(__fmul_rn(v[c][i], step_inverse));
-                    packed[i / 4] |= (static_cast<uint32_t>(value) & 0xffu) << (8 * (i % 4));
-                }
-                *reinterpret_cast<uint2*>(q + base + col) = make_uint2(packed[0], packed[1]);
-            }
-        }
-        if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
     }
 }
 
@@ -145,12 +97,8 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
     }
 }
 
-// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M]. Lane l of part p owns the
-// 8-element chunk c = 32 p + l (coalesced 16-byte loads and 8-byte stores); a Hadamard block of 32 is the chunks of
-// 4 consecutive lanes. With i = 8 q + r (q the chunk within the block, r the element within the chunk),
-// H32[i][j] = (-1)^popcount(i & j) = H4[q_i][q_j] H8[r_i][r_j]: the butterflies over r run in registers, those over q
-// across the quad by shuffles, in the same order over the index bits as a 32-element butterfly.
-// A warp takes kRotateRows consecutive rows, their loads all issued first.
+// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M], by rotate_quant_row. A warp
+// takes kRotateRows consecutive rows, their loads all issued first.
 constexpr int kRotateRows = 2;
 __global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
                                                                       float* __restrict__ scale, int M, int hidden, int width) {
@@ -159,60 +107,14 @@ __global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint
     if (first_row >= M) return;
     uint4 raw[kRotateRows][4];
 #pragma unroll
-    for (int r = 0; r < kRotateRows; ++r)
-#pragma unroll
-        for (int part = 0; part < 4; ++part) {
-            const int col = (part * 32 + lane) * 8;
-            raw[r][part] = (col < hidden && first_row + r < M)
-                               ? *reinterpret_cast<const uint4*>(h + static_cast<size_t>(first_row + r) * hidden + col)
-                               : make_uint4(0, 0, 0, 0);
-        }
+    for (int r = 0; r < kRotateRows; ++r) {
+        if (first_row + r < M) load_row_chunks<4>(h + static_cast<size_t>(first_row + r) * hidden, hidden, lane, raw[r]);
+    }
 #pragma unroll
     for (int r = 0; r < kRotateRows; ++r) {
         const int row = first_row + r;
         if (row >= M) break;  // uniform across the warp
-        float v[4][8];
-#pragma unroll
-        for (int part = 0; part < 4; ++part) unpack8(raw[r][part], v[part]);
-        // (a, b) -> (a + b, a - b) over the element bits (registers), then over the chunk bits (the quad's lanes)
-#pragma unroll
-        for (int part = 0; part < 4; ++part) {
-#pragma unroll
-            for (int span = 1; span < 8; span <<= 1)
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    if ((i & span) == 0) {
-                        const float a = v[part][i], b = v[part][i + span];
-                        v[part][i] = __fadd_rn(a, b);
-                        v[part][i + span] = __fsub_rn(a, b);
-                    }
-#pragma unroll
-            for (int span = 1; span < 4; span <<= 1)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float partner = __shfl_xor_sync(0xffffffffu, v[part][i], span);
-                    v[part][i] = (lane & span) ? __fsub_rn(partner, v[part][i]) : __fadd_rn(v[part][i], partner);
-                }
-        }
-        float absmax = 0.0f;
-#pragma unroll
-        for (int part = 0; part < 4; ++part)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) absmax = fmaxf(absmax, fabsf(v[part][i]));
-        absmax = fmaxf(warp_max(absmax), 1e-20f);
-        const float step_inverse = __fdiv_rn(127.0f, absmax);
-#pragma unroll
-        for (int part = 0; part < 4; ++part) {
-            const int col = (part * 32 + lane) * 8;
-            if (col < width) {
-                uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    packed[i / 4] |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[part][i], step_inverse))) & 0xffu) << (8 * (i % 4));
-                *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * width + col) = make_uint2(packed[0], packed[1]);
-            }
-        }
-        if (lane == 0) scale[row] = __fdiv_rn(absmax, 127.0f);
+        rotate_quant_row(raw[r], width, lane, q + static_cast<size_t>(row) * width, scale + row);
     }
 }
 
@@ -337,15 +239,20 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
                        const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
-    constexpr int kRows = 4, kMixRows = 2;  // rows a warp
     const bool mix = original != nullptr;
-    const dim3 grid((M + kRowWarps * (mix ? kMixRows : kRows) - 1) / (kRowWarps * (mix ? kMixRows : kRows)));
+    // persistent warps: up to kRowCtasPerSm CTAs an SM, each warp looping over rows
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const int wanted = (M + kRowWarps - 1) / kRowWarps, most = multiprocessors * kRowCtasPerSm;
+    const dim3 grid(wanted < most ? wanted : most);
     const int chunks = (D + 255) / 256;
-#define FRY_NQ(C)                                                                                                                       \
-    (mix ? (norm_quant_kernel<C, true, kMixRows><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, \
-                                                                                       eps, mixed, q, scale, M, D), 0)                  \
-         : (norm_quant_kernel<C, false, kRows><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, \
-                                                                                     mixed, q, scale, M, D), 0))
+#define FRY_NQ(C)                                                                                                                   \
+    (mix ? (norm_quant_kernel<C, true><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, mixed, \
+                                                                             q, scale, M, D), 0)                                    \
+         : (norm_quant_kernel<C, false><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, mixed, \
+                                                                              q, scale, M, D), 0))
     switch (chunks) {
         case 1: FRY_NQ(1); break;
         case 2: FRY_NQ(2); break;
