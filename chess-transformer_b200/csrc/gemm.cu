@@ -13,12 +13,12 @@
 // tcgen05.ld, and applies the epilogue in the reference's op order (model/int8_cuda.py:163-178) while the MMAs of the
 // next tile fill the other accumulator.
 //
-// fp16 outputs leave through shared memory: a tile is staged as 64-column boxes of 128 rows x 128 bytes in the 128-byte
-// swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread over all banks), which warp
-// 18 writes to global memory with TMA stores; no thread stores a row of its own. The row operands (residual, original)
-// arrive the same way, as TMA loads of the same boxes that warp 18 issues a tile ahead into the other of two slots, and
-// each output overwrites its residual in the slot. A tile's column operands (weight scales, bias) are staged one tile ahead in
-// shared memory too, so one barrier a tile suffices.
+// fp16 outputs leave through shared memory, a sub-tile of SUB columns at a time: staged as 64-column boxes of 128 rows x
+// 128 bytes in the 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread
+// over all banks), which warp 18 writes to global memory with TMA stores; no thread stores a row of its own. The row
+// operands (residual, original) arrive the same way, as TMA loads of the same boxes that warp 18 issues a sub-tile ahead
+// into the other of two slots, and each output overwrites its residual in the slot. A tile's column operands (weight
+// scales, bias) are staged one tile ahead in shared memory too, so one barrier a sub-tile suffices.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
@@ -45,7 +45,9 @@ constexpr int kBoxBytes = kBlockM * kBoxCols * 2;  // a staged fp16 box: 128 row
 constexpr int kBarrierBytes = 256;
 constexpr int kSmemBudget = 227 * 1024 - kBarrierBytes;
 
-template <int KIND, int BN, bool GATED, int EPI>
+// SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
+// up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
+template <int KIND, int BN, bool GATED, int EPI, int SUB>
 struct GemmShape {
     static constexpr int kElem = KIND == 0 ? 1 : 2;
     static constexpr int kBoxK = kTileKBytes / kElem;
@@ -56,10 +58,12 @@ struct GemmShape {
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
     // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
     static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
-    static constexpr int kBoxes = BN / kBoxCols;
-    static_assert(!kStaged || BN % kBoxCols == 0, "a staged tile is whole 64-column boxes");
-    // one slot holds a tile's row operands (the output overwrites the first) or, without row operands, its output; there
-    // are two, so the next tile's operands load, and the last tile's stores drain, while this tile is worked on
+    static constexpr int kSubs = BN / SUB;       // sub-tiles a tile
+    static constexpr int kBoxes = SUB / kBoxCols;  // staged boxes a sub-tile (per row tensor)
+    static_assert(!kStaged || (SUB % kBoxCols == 0 && BN % SUB == 0), "a staged sub-tile is whole 64-column boxes");
+    static_assert(kStaged || SUB == BN, "unstaged epilogues take the tile whole");
+    // one slot holds a sub-tile's row operands (the output overwrites the first) or, without row operands, its output;
+    // there are two, so the next sub-tile's operands load, and the last one's stores drain, while one is worked on
     static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kBoxes * kBoxBytes : 0;
     static constexpr int kSlots = 2;
     static constexpr int kIoBytes = kSlots * kSlotBytes;
@@ -95,12 +99,13 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
     }
 }
 
-// Issues the TMA loads of one tile's row operands (the boxes of its columns below N) into a slot, completing on bar.
-template <int EPI, int BN>
-FRY_DEVICE void load_tile_rows(const CUtensorMap* map_residual, const CUtensorMap* map_original, uint8_t* slot, uint64_t* bar, int m0,
-                               int n0, int N) {
-    constexpr int kBoxes = BN / kBoxCols, kTensors = EPI == kEpiMix ? 2 : 1;
-    const int in_range = (N - n0 + kBoxCols - 1) / kBoxCols;
+// Issues the TMA loads of one sub-tile's row operands (the boxes of its columns below N, none past it) into a slot,
+// completing on bar.
+template <int EPI, int SUB>
+FRY_DEVICE void load_sub_rows(const CUtensorMap* map_residual, const CUtensorMap* map_original, uint8_t* slot, uint64_t* bar, int m0,
+                              int n0, int N) {
+    constexpr int kBoxes = SUB / kBoxCols, kTensors = EPI == kEpiMix ? 2 : 1;
+    const int in_range = n0 < N ? (N - n0 + kBoxCols - 1) / kBoxCols : 0;
     const int boxes = in_range < kBoxes ? in_range : kBoxes;
     mbar_arrive_expect_tx(bar, boxes * kTensors * kBoxBytes);
     for (int b = 0; b < boxes; ++b) {
@@ -202,12 +207,12 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
     }
 }
 
-template <int KIND, int BN, bool GATED, int EPI>
+template <int KIND, int BN, bool GATED, int EPI, int SUB>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_residual,
                 const __grid_constant__ CUtensorMap map_original, const GemmArgs args, int M, int N, int K) {
-    using S = GemmShape<KIND, BN, GATED, EPI>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB>;
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023u) {  // uniform across the CTA: every thread leaves before any barrier
         if (threadIdx.x == 0) record_error(kMisaligned, 20);
@@ -215,6 +220,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     uint8_t* stages = smem;                                              // [kStages][A box | B box(es)]
     uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kBoxes][128 rows][128 bytes, swizzled]
+    // sub-tiles in the order this CTA takes them: (tile, s) -> (tile, s + 1), or the next tile's first
+    auto advance = [&](int& tile, int& sub) {
+        if (++sub == S::kSubs) {
+            sub = 0;
+            tile += static_cast<int>(gridDim.x);
+        }
+    };
     float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][2 * BN]
     uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes);
     uint64_t* empty = full + S::kStages;
@@ -309,34 +321,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     } else if (warp == kStoreWarp) {
-        // the staged tiles' TMA traffic: after tile k's barrier, its stores from slot k % 2; once they have read the slot,
-        // the row operands of tile k + 2 into it (those of tiles 0 and 1 first). Waiting for the reads before the next
-        // barrier also frees the slot for tile k + 2's outputs.
+        // the staged sub-tiles' TMA traffic: after sub-tile j's barrier, its stores from slot j % 2; once they have read
+        // the slot, the row operands of sub-tile j + 2 into it (those of sub-tiles 0 and 1 first). Waiting for the reads
+        // before the next barrier also frees the slot for sub-tile j + 2's outputs.
         if constexpr (S::kStaged) {
             const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
             const bool issuer = lane == 0;
-            auto load_rows = [&](int tile, int slot) {
+            auto load_rows = [&](int tile, int sub, int slot) {
                 if (!issuer || !has_rows || tile >= tiles) return;
-                load_tile_rows<EPI, BN>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
-                                        (tile / n_blocks) * kBlockM, (tile % n_blocks) * BN, N);
+                load_sub_rows<EPI, SUB>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
+                                        (tile / n_blocks) * kBlockM, (tile % n_blocks) * BN + sub * SUB, N);
             };
-            load_rows(blockIdx.x, 0);
-            load_rows(blockIdx.x + gridDim.x, 1);
+            int ahead_tile = blockIdx.x, ahead_sub = 0;  // the sub-tile two ahead of the one being stored
+            load_rows(ahead_tile, ahead_sub, 0);
+            advance(ahead_tile, ahead_sub);
+            load_rows(ahead_tile, ahead_sub, 1);
+            advance(ahead_tile, ahead_sub);
             epilogue_sync();  // the first tile's column operands are staged
-            int local = 0;
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-                const int slot = local & 1;
-                __syncwarp();
-                epilogue_sync();  // tile k is staged
-                if (issuer) {
-                    const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
-                    uint8_t* staged_tile = io + slot * S::kSlotBytes;
-                    for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
-                        tma_store_2d(&map_out, staged_tile + b * kBoxBytes, n0 + b * kBoxCols, m0);
-                    bulk_commit();
-                    bulk_wait_read_all();
+            int j = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
+                    const int slot = j & 1;
+                    __syncwarp();
+                    epilogue_sync();  // sub-tile j is staged
+                    if (issuer) {
+                        const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN + sub * SUB;
+                        uint8_t* staged = io + slot * S::kSlotBytes;
+                        for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
+                            tma_store_2d(&map_out, staged + b * kBoxBytes, n0 + b * kBoxCols, m0);
+                        bulk_commit();
+                        bulk_wait_read_all();
+                    }
+                    load_rows(ahead_tile, ahead_sub, slot);
+                    advance(ahead_tile, ahead_sub);
                 }
-                load_rows(tile + 2 * gridDim.x, slot);
             }
             if (issuer) bulk_wait_all();
         } else {
@@ -373,46 +391,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epilogue_sync();
         // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
         // epilogue warps never wait at the barrier for it
-        int local = 0;
+        int local = 0, j = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
-            // tile k stages into slot k % 2, which the stores of tile k - 2 had read before the barrier that ended tile k - 1
-            const int buffer = local & 1, slot = local & 1;
+            const int buffer = local & 1;
             const int next = tile + static_cast<int>(gridDim.x);
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
-            const int c0 = part * kChunkCols;
             const float xs = xs_next;
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
-            // every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
-            if (has_rows && !mbar_wait(&rows_full[slot], (local >> 1) & 1, 14)) alive = false;
-            uint8_t* staged_tile = io + slot * S::kSlotBytes;
             const float* columns = column_buffers + buffer * 2 * BN;
-            if (alive) {
-                tc_fence_after();
-                const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-                for (int c = c0; c < BN && n0 + c < N; c += kChunkCols * kChunkParts) {  // uniform across the warp
-                    uint32_t acc[16], up[16];
-                    tmem_load16(lane_base + c, acc);
-                    if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
-                    tmem_load_wait();
-                    const int box = c / kBoxCols, unit = 2 * ((c % kBoxCols) / kChunkCols), swizzle = row_in_tile & 7;
-                    const StagedChunk staged{staged_tile + box * kBoxBytes + row_in_tile * 128, unit, swizzle};
-                    const StagedChunk original{staged_tile + (S::kBoxes + box) * kBoxBytes + row_in_tile * 128, unit, swizzle};
-                    const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
-                    if (S::kStaged || m < M)
-                        epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original,
-                                        static_cast<size_t>(m) * N + n0 + c, valid);
+            const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
+                // sub-tile j stages into slot j % 2, which the stores of sub-tile j - 2 had read before the barrier that ended
+                // sub-tile j - 1; every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
+                const int slot = j & 1;
+                if (has_rows && !mbar_wait(&rows_full[slot], (j >> 1) & 1, 14)) alive = false;
+                uint8_t* staged_sub = io + slot * S::kSlotBytes;
+                if (alive) {
+                    tc_fence_after();
+                    for (int c = sub * SUB + part * kChunkCols; c < (sub + 1) * SUB && n0 + c < N; c += kChunkCols * kChunkParts) {  // uniform
+                        uint32_t acc[16], up[16];
+                        tmem_load16(lane_base + c, acc);
+                        if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
+                        tmem_load_wait();
+                        const int c_sub = c - sub * SUB;
+                        const int box = c_sub / kBoxCols, unit = 2 * ((c_sub % kBoxCols) / kChunkCols), swizzle = row_in_tile & 7;
+                        const StagedChunk staged{staged_sub + box * kBoxBytes + row_in_tile * 128, unit, swizzle};
+                        const StagedChunk original{staged_sub + (S::kBoxes + box) * kBoxBytes + row_in_tile * 128, unit, swizzle};
+                        const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
+                        if (S::kStaged || m < M)
+                            epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original,
+                                            static_cast<size_t>(m) * N + n0 + c, valid);
+                    }
                 }
+                if (sub == S::kSubs - 1) {
+                    // this warp's reads of the accumulator are complete: the MMA warp may fill it again
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
+                    if (next < tiles) fetch_operands(next, buffer ^ 1);
+                }
+                // this thread's staged writes, visible to the async proxy before the stores read them
+                if constexpr (S::kStaged) fence_proxy_async_shared();
+                epilogue_sync();
             }
-            // this warp's reads of the accumulator are complete: the MMA warp may fill it again
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
-            if (next < tiles) fetch_operands(next, buffer ^ 1);
-            // this thread's staged writes, visible to the async proxy before the stores read them
-            if constexpr (S::kStaged) fence_proxy_async_shared();
-            epilogue_sync();
         }
     }
     tc_fence_before();
@@ -483,10 +506,10 @@ bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::s
     return true;
 }
 
-template <int KIND, int BN, bool GATED, int EPI>
+template <int KIND, int BN, bool GATED, int EPI, int SUB = BN>
 cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
-    using S = GemmShape<KIND, BN, GATED, EPI>;
-    auto kernel = gemm_kernel<KIND, BN, GATED, EPI>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB>;
+    auto kernel = gemm_kernel<KIND, BN, GATED, EPI, SUB>;
     const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
     if (attribute != cudaSuccess) return attribute;
     CUtensorMap map_a, map_b, map_out, map_residual, map_original;
@@ -512,23 +535,23 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 
 }  // namespace
 
-// Tile widths: whole 64-column staging boxes; gate_up's 128 columns hold 256 accumulators (its gate and its up); mixing's
-// 64 keep two staged row operands in two slots beside six stages; 128 elsewhere. An fp16 output needs N a multiple of 8
-// (its rows 16-byte aligned for the TMA maps).
+// Tile widths: one N = 256 MMA a K step where N allows (gate_up's 128 columns hold 256 accumulators, its gate and its
+// up), staged in 128-column sub-tiles, mixing's in 64-column ones (two row operands a slot); 128 elsewhere. An fp16
+// output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
     if (kind == 0) {
         switch (epilogue) {
-            case kEpiBias: return launch<0, 128, false, kEpiBias>(a, b, args, M, N, K, stream, error);
+            case kEpiBias: return launch<0, 256, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
             case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
-            case kEpiResidual: return launch<0, 128, false, kEpiResidual>(a, b, args, M, N, K, stream, error);
-            case kEpiMix: return launch<0, 64, false, kEpiMix>(a, b, args, M, N, K, stream, error);
+            case kEpiResidual: return launch<0, 256, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
+            case kEpiMix: return launch<0, 256, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {
         switch (epilogue) {
-            case kEpiLinearF16: return launch<1, 128, false, kEpiLinearF16>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF16: return launch<1, 256, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
