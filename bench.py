@@ -183,6 +183,38 @@ def gemm_roofline(torch, stream) -> dict:
     return {"ops_per_forward": total_ops, "seconds_per_forward": total_seconds, "tops_by_shape": per_shape}
 
 
+SWEEP_BATCHES = (1, 16, 64, 256, 1024)
+
+
+def batch_sweep(torch, network, device, stream, flush, steps: int) -> dict:
+    """Positions/s and ms per forward at each of SWEEP_BATCHES (a CUDA graph per batch, inputs resident, L2 flushed
+    before each timed replay, CUDA events on the graph's stream)."""
+    from chess_transformer_b200.boards import random_boards
+    results = {}
+    for batch in SWEEP_BATCHES:
+        boards = torch.from_numpy(random_boards(batch, 500 + batch)).long().to(device)
+        with torch.cuda.stream(stream), torch.no_grad():
+            network(boards)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                network(boards)
+            for _ in range(3):
+                graph.replay()
+            times = []
+            for _ in range(steps):
+                flush.fill_(1)
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                graph.replay()
+                end.record(stream)
+                end.synchronize()
+                times.append(start.elapsed_time(end))
+        ms = statistics.median(times)
+        results[str(batch)] = {"ms_per_forward": round(ms, 4), "positions_per_s": round(batch / ms * 1000, 1)}
+        del graph
+    return results
+
+
 def main() -> None:
     args = arguments()
     rank = int(os.environ.get("RANK", "0"))
@@ -274,6 +306,8 @@ def main() -> None:
             latencies.append(time.perf_counter() - t0)
         extra["latency_p50_ms_batch64"] = round(1000 * statistics.median(latencies[10:]), 3)
     del batches
+    if rank == 0 and not args.no_sweep:
+        extra["batch_sweep"] = batch_sweep(torch, network, device, stream, flush, max(5, args.steps))
 
     if rank == 0:
         gemm = gemm_roofline(torch, stream)

@@ -536,22 +536,45 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 }  // namespace
 
 // Tile widths: one N = 256 MMA a K step where N allows (gate_up's 128 columns hold 256 accumulators, its gate and its
-// up), staged in 128-column sub-tiles, mixing's in 64-column ones (two row operands a slot); 128 elsewhere. An fp16
-// output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
+// up), staged in 128-column sub-tiles, mixing's in 64-column ones (two row operands a slot). When that leaves fewer tiles
+// than SMs (small batches), narrower tiles (128, then 64 columns: more CTAs streaming the weights, deeper pipelines)
+// take their place. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const int row_blocks = (M + kBlockM - 1) / kBlockM;
+    auto tiles = [&](int bn) { return row_blocks * ((N + bn - 1) / bn); };
+    // the widest tile whose count fills the SMs (or the narrowest)
+    const int width = tiles(256) >= multiprocessors ? 256 : tiles(128) >= multiprocessors ? 128 : 64;
     if (kind == 0) {
         switch (epilogue) {
-            case kEpiBias: return launch<0, 256, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
-            case kEpiGated: return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
-            case kEpiResidual: return launch<0, 256, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
-            case kEpiMix: return launch<0, 256, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
+            case kEpiBias:
+                if (width == 256) return launch<0, 256, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
+            case kEpiGated:
+                if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);
+            case kEpiResidual:
+                if (width == 256) return launch<0, 256, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
+            case kEpiMix:
+                if (width == 256) return launch<0, 256, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {
         switch (epilogue) {
-            case kEpiLinearF16: return launch<1, 256, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF16:
+                if (width == 256) return launch<1, 256, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<1, 128, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
+                return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             default: break;
         }
