@@ -7,7 +7,7 @@
 // whose fp32 sums are divided by the unrounded total. Grouped-query: head h reads key/value head h / (heads / kv_heads).
 //
 // One CTA per (position, group of up to 8 query heads), one warp per query head, in 5 phases: the 4 slabs of 16 square
-// rows, then the metadata rows. The CTA stages its key/value heads' normalised keys and raw values in shared memory.
+// rows, then the metadata rows (at small batches one CTA per phase, so more SMs share a position). The CTA stages its key/value heads' normalised keys and raw values in shared memory.
 // Before a square slab, the warps form its template bias for all the CTA's heads with mma.sync: for a pair of squares
 // (i0, i1), A = the 8 heads' coefficients block-diagonally over (i0's 8 templates | i1's 8 templates) and B = the pair's
 // templates, paired per key as [square][key][template] (fry_pair_templates, as the reference pairs them,
@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
         if (key < kAttnTokens) raw = *reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8);
         *reinterpret_cast<uint4*>(values + (kv * kAttnKeys + key) * kValueRow + part * 8) = raw;
     }
-    make_bias_slab(bias, board, paired, 0, width, c_offset, first_head, heads_here, warp, warps, g, t);
+    // this CTA's phases: all five, or with a phase split (blockIdx.z, small batches), a share of them
+    const int phases = (5 + gridDim.z - 1) / gridDim.z;
+    const int phase_begin = blockIdx.z * phases, phase_end = min(5, phase_begin + phases);
+    if (phase_begin < 4) make_bias_slab(bias, board, paired, phase_begin, width, c_offset, first_head, heads_here, warp, warps, g, t);
 
     const int head = first_head + warp;
     const uint16_t* kv_keys = keys + (warp / group) * kAttnKeys * KROW;
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
                 qg[ks][half][e] = col < dq ? h2f_bits(q_gain[col]) : 0.0f;
             }
     uint32_t raw_q[KS][2][2];
-    load_queries<KS>(raw_q, board, 0, width, head, dq, g, t);
+    load_queries<KS>(raw_q, board, phase_begin * kSlab, width, head, dq, g, t);
     __syncthreads();
 
     const uint64_t scale2 = pair2(scale, scale), log2e2 = pair2(1.4426950408889634f, 1.4426950408889634f);
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
         const int first = phase * kSlab;
         // the next phase's queries, ahead of this phase's work
         uint32_t next_q[KS][2][2];
-        if (SQUARES) load_queries<KS>(next_q, board, first + kSlab, width, head, dq, g, t);
+        if (SQUARES && phase + 1 < phase_end) load_queries<KS>(next_q, board, first + kSlab, width, head, dq, g, t);
 
         uint32_t a[KS][4];
 #pragma unroll
@@ -252,7 +255,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
                 top2[r] = pair2(fmaxf(lane0(top2[r]), lane0(v)), fmaxf(lane1(top2[r]), lane1(v)));
             }
         // every warp has read this slab: the next one takes its place while the exponentials run
-        if (SQUARES && phase + 1 < 4) {
+        if (SQUARES && phase + 1 < 4 && phase + 1 < phase_end) {
             __syncthreads();
             make_bias_slab(bias, board, paired, phase + 1, width, c_offset, first_head, heads_here, warp, warps, g, t);
         }
@@ -316,8 +319,8 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
             __syncthreads();
         }
     };
-    for (int phase = 0; phase < 4; ++phase) run_phase(std::true_type{}, phase);
-    run_phase(std::false_type{}, 4);
+    for (int phase = phase_begin; phase < 4 && phase < phase_end; ++phase) run_phase(std::true_type{}, phase);
+    if (phase_end == 5) run_phase(std::false_type{}, 4);
 }
 
 cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream) {
@@ -342,7 +345,13 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     }
     const int kv_per_cta = per_cta / group;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dq)));  // 1 / math.sqrt(dq), rounded once to fp32
-    const dim3 grid(heads / per_cta, B);
+    // small batches: each phase its own CTA (every CTA stages the keys and values again), so more SMs share a board
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const int ctas = heads / per_cta * B;
+    const dim3 grid(heads / per_cta, B, ctas < 2 * multiprocessors ? 5 : 1);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
