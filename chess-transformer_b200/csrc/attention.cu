@@ -127,6 +127,10 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     const int k_offset = heads * dq, v_offset = (heads + kv_heads) * dq, c_offset = v_offset + kv_heads * kAttnDv;
     const int first_head = blockIdx.x * heads_here, first_kv = blockIdx.x * kv_here;
     const uint16_t* board = projected + static_cast<size_t>(b) * kAttnTokens * width;
+    // the mean of dq squares: for a power-of-two dq, the multiply by its reciprocal rounds exactly as the division
+    const bool dq_pow2 = (dq & (dq - 1)) == 0;
+    const float dq_reciprocal = 1.0f / static_cast<float>(dq);
+    auto mean_of = [&](float sum) { return dq_pow2 ? __fmul_rn(sum, dq_reciprocal) : __fdiv_rn(sum, static_cast<float>(dq)); };
 
     // normalised keys (zero past dq and past the 70th key), 16-byte loads and stores
     for (int item = tid; item < kv_here * kAttnKeys; item += blockDim.x) {
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
             for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
         }
-        const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(squares, static_cast<float>(dq)), eps));
+        const float inverse = rsqrtf(__fadd_rn(mean_of(squares), eps));
         uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
 #pragma unroll
         for (int part = 0; part < DQP / 8; ++part) {
@@ -196,6 +200,8 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     __syncthreads();
 
     const uint64_t scale2 = pair2(scale, scale), log2e2 = pair2(1.4426950408889634f, 1.4426950408889634f);
+    // the metadata phase's rows g + 8 (72-79) do not exist: its r = 1 half is skipped
+    constexpr int kRowHalves = 2;
     // one phase: 16 query rows from `first`; SQUARES (phases 0-3) adds the slab's template bias, the metadata phase (4)
     // has none and is the last
     auto run_phase = [&](auto squares_tag, int phase) {
@@ -207,7 +213,12 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 
         uint32_t a[KS][4];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < kRowHalves; ++r) {
+            if (!SQUARES && r == 1) {
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) a[ks][1] = a[ks][3] = 0u;
+                continue;
+            }
             float squares = 0.0f;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
@@ -216,7 +227,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
                     const float x0 = low_half(raw_q[ks][r][half]), x1 = high_half(raw_q[ks][r][half]);
                     squares = __fmaf_rn(x1, x1, __fmaf_rn(x0, x0, squares));
                 }
-            const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(quad_sum(squares), static_cast<float>(dq)), eps));
+            const float inverse = rsqrtf(__fadd_rn(mean_of(quad_sum(squares)), eps));
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
@@ -246,7 +257,11 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
         for (int j = 0; j < kTiles; ++j)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
+            for (int r = 0; r < kRowHalves; ++r) {
+                if (!SQUARES && r == 1) {
+                    s2[j][1] = 0;  // probability 0 for the rows that do not exist
+                    continue;
+                }
                 uint64_t b2 = 0;  // +0.0 in both lanes
                 if (SQUARES && j < 8) b2 = widen2(*reinterpret_cast<const uint32_t*>(head_bias + (g + 8 * r) * kBiasRow + j * 8 + 2 * t));
                 uint64_t v = fma2(s2[j][r], scale2, b2);
@@ -262,7 +277,8 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
         uint64_t shift2[2];
         float top[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < kRowHalves; ++r) {
+            if (!SQUARES && r == 1) continue;
             top[r] = quad_max(fmaxf(lane0(top2[r]), lane1(top2[r])));
             const float shift = -top[r] * 1.4426950408889634f;
             shift2[r] = pair2(shift, shift);
@@ -271,7 +287,8 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
         for (int j = 0; j < kTiles; ++j)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
+            for (int r = 0; r < kRowHalves; ++r) {
+                if (!SQUARES && r == 1) continue;
                 const uint64_t x = fma2(s2[j][r], log2e2, shift2[r]);  // (s - top) log2 e
                 const uint64_t p = pair2(ex2_approx(lane0(x)), ex2_approx(lane1(x)));
                 s2[j][r] = p;
@@ -279,7 +296,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
             }
         float inverse[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) inverse[r] = __frcp_rn(quad_sum(__fadd_rn(lane0(total2[r]), lane1(total2[r]))));
+        for (int r = 0; r < kRowHalves; ++r) inverse[r] = (!SQUARES && r == 1) ? 0.0f : __frcp_rn(quad_sum(__fadd_rn(lane0(total2[r]), lane1(total2[r]))));
         float o[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
@@ -345,13 +362,14 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     }
     const int kv_per_cta = per_cta / group;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dq)));  // 1 / math.sqrt(dq), rounded once to fp32
-    // small batches: each phase its own CTA (every CTA stages the keys and values again), so more SMs share a board
+    // small batches: the phases shared among up to 5 CTAs (each stages the keys and values again), as many as still fit
+    // the SMs at once (3 CTAs an SM), so more SMs share a board
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    const int ctas = heads / per_cta * B;
-    const dim3 grid(heads / per_cta, B, ctas < 2 * multiprocessors ? 5 : 1);
+    const int ctas = heads / per_cta * B, fit = 3 * multiprocessors / ctas;
+    const dim3 grid(heads / per_cta, B, fit < 1 ? 1 : fit > 5 ? 5 : fit);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
