@@ -59,6 +59,7 @@ FRY_DEVICE float quad_max(float v) {
 
 // paired[i][j][t] = templates[t][i][j]: a key's 8 templates side by side, the B operand of the bias MMA.
 __global__ void pair_templates_kernel(const uint16_t* __restrict__ templates, uint16_t* __restrict__ paired) {
+    grid_dependency_start();
     const int index = blockIdx.x * blockDim.x + threadIdx.x;  // over 64 x 64 (i, j)
     if (index >= kAttnSquares * kAttnSquares) return;
     uint16_t row[kAttnTemplates];
@@ -113,6 +114,7 @@ template <int DQP>
 __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     attention_kernel(const uint16_t* __restrict__ projected, const uint16_t* __restrict__ paired, const uint16_t* __restrict__ q_gain,
                      const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out, int heads, int kv_heads, int dq, float eps, float scale) {
+    grid_dependency_start();
     constexpr int KROW = DQP + 8, KS = DQP / 16;
     extern __shared__ __align__(16) uint16_t attn_smem[];
     const int heads_here = blockDim.x / 32, warps = heads_here;
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     // this CTA's phases: all five, or with a phase split (blockIdx.z, small batches), a share of them
     const int phases = (5 + gridDim.z - 1) / gridDim.z;
     const int phase_begin = blockIdx.z * phases, phase_end = min(5, phase_begin + phases);
+    if (phase_begin >= 5) return;  // uniform across the CTA; the launcher gives every group a phase
     if (phase_begin < 4) make_bias_slab(bias, board, paired, phase_begin, width, c_offset, first_head, heads_here, warp, warps, g, t);
 
     const int head = first_head + warp;
@@ -341,8 +344,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 }
 
 cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream) {
-    pair_templates_kernel<<<(kAttnSquares * kAttnSquares + 255) / 256, 256, 0, stream>>>(templates, paired);
-    return cudaGetLastError();
+    return launch_dependent(pair_templates_kernel, dim3((kAttnSquares * kAttnSquares + 255) / 256), dim3(256), 0, stream, templates, paired);
 }
 
 cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
@@ -368,19 +370,22 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
+    // 1, 2, 3 or 5 groups: each has a phase (4 groups of 2 phases would leave the last without one)
     const int ctas = heads / per_cta * B, fit = 3 * multiprocessors / ctas;
-    const dim3 grid(heads / per_cta, B, fit < 1 ? 1 : fit > 5 ? 5 : fit);
+    const dim3 grid(heads / per_cta, B, fit >= 5 ? 5 : fit >= 3 ? 3 : fit >= 2 ? 2 : 1);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
     if (dqp == 16) {
         const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<16>), static_cast<int>(bytes));
         if (attribute != cudaSuccess) return attribute;
-        attention_kernel<16><<<grid, per_cta * 32, bytes, stream>>>(projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps, scale);
+        return launch_dependent(attention_kernel<16>, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads,
+                                kv_heads, dq, eps, scale);
     } else {
         const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<32>), static_cast<int>(bytes));
         if (attribute != cudaSuccess) return attribute;
-        attention_kernel<32><<<grid, per_cta * 32, bytes, stream>>>(projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps, scale);
+        return launch_dependent(attention_kernel<32>, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads,
+                                kv_heads, dq, eps, scale);
     }
     return cudaGetLastError();
 }

@@ -200,6 +200,33 @@ __host__ __device__ constexpr uint32_t instr_desc(int n) {
            (static_cast<uint32_t>(128 >> 4) << 24);
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------------------------
+//
+// Every kernel of the library is launched with programmatic stream serialization, so it may start (launch, take its
+// shared memory, set up) while the kernel before it in the stream finishes. Each kernel calls grid_dependency_start()
+// before it reads or writes anything an earlier kernel touches, in every CTA: that waits until the previous grid has
+// completed with its memory visible, so a kernel's completion still implies every earlier one's, then lets the next
+// kernel be scheduled.
+FRY_DEVICE void grid_dependency_start() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
 // ---- small numeric helpers -----------------------------------------------------------------------------
 
 // Two fp32 lanes in one 64-bit register, for the paired (f32x2) IEEE adds, multiplies and FMAs of sm_100: each lane

@@ -264,6 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dependency_start();  // setup done: now the operands of earlier kernels
 
     if (warp == kProducerWarp) {
         if (elect_one()) {
@@ -528,9 +529,8 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    kernel<<<tiles < multiprocessors ? tiles : multiprocessors, kGemmThreads, S::kSmemBytes, stream>>>(map_a, map_b, map_out, map_residual,
-                                                                                                         map_original, args, M, N, K);
-    return cudaGetLastError();
+    return launch_dependent(kernel, dim3(tiles < multiprocessors ? tiles : multiprocessors), dim3(kGemmThreads), S::kSmemBytes, stream, map_a,
+                            map_b, map_out, map_residual, map_original, args, M, N, K);
 }
 
 }  // namespace

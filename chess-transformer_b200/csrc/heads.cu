@@ -51,6 +51,7 @@ FRY_DEVICE float reduce_scatter32(float (&v)[32], int lane) {
 __global__ void __launch_bounds__(256) narrow_kernel(const uint16_t* __restrict__ y, const float* __restrict__ weight,
                                                      const float* __restrict__ bias, float* __restrict__ narrow,
                                                      float* __restrict__ eval_in, int M, int D) {
+    grid_dependency_start();
     extern __shared__ float narrow_weights[];  // [21][D]
     for (int i = threadIdx.x; i < kNarrow * D; i += blockDim.x) narrow_weights[i] = weight[i];
     __syncthreads();
@@ -102,6 +103,7 @@ FRY_DEVICE void split_pair(float2 v, uint32_t& hi, uint32_t& lo) {
 // One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits.
 __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a, const uint16_t* __restrict__ y,
                                                      const float* __restrict__ narrow, float* __restrict__ rows, int D) {
+    grid_dependency_start();
     __shared__ float logits[kHeadSquares][kHeadSquares + 1];
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int m_tile = warp >> 1, n_first = (warp & 1) * 4;
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 // x [B, K] and W [N, K] row-major; a CTA takes 32 boards x 32 outputs of one split, 2 x 2 a thread.
 __global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ x, const float* __restrict__ weight,
                                                            float* __restrict__ partial, int B, int K, int N, int k_split) {
+    grid_dependency_start();
     __shared__ float xs[kSplitTile][kSplitTile + 1];
     __shared__ float ws[kSplitTile][kSplitTile + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -199,6 +202,7 @@ __global__ void __launch_bounds__(256) linear_split_kernel(const float* __restri
 template <bool GELU>
 __global__ void __launch_bounds__(256) linear_sum_kernel(const float* __restrict__ partial, const float* __restrict__ bias,
                                                          float* __restrict__ out, int B, int N, int splits) {
+    grid_dependency_start();
     const int index = blockIdx.x * blockDim.x + threadIdx.x;
     if (index >= B * N) return;
     float total = partial[index];
@@ -212,6 +216,7 @@ inline int split_size(int K) { return (K + kEvalSplitsMax - 1) / kEvalSplitsMax 
 
 // One warp per board: the softmax of its value logits times the bin centres (2i + 1) / 2bins, into the row's last column.
 __global__ void __launch_bounds__(256) expected_score_kernel(const float* __restrict__ logits, float* __restrict__ rows, int B, int bins) {
+    grid_dependency_start();
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     const float* row = logits + static_cast<size_t>(b) * bins;
@@ -262,19 +267,27 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     status = ensure_smem(reinterpret_cast<const void*>(narrow_kernel), static_cast<int>(narrow_smem));
     if (status != cudaSuccess) return status;
     const int narrow_blocks = (M + 15) / 16 < 148 * 3 ? (M + 15) / 16 : 148 * 3;
-    narrow_kernel<<<narrow_blocks, 256, narrow_smem, stream>>>(y, w.narrow_weight, w.narrow_bias, narrow, eval_in, M, D);
-    policy_kernel<<<B, 256, 0, stream>>>(a, y, narrow, rows, D);
+    status = launch_dependent(narrow_kernel, dim3(narrow_blocks), dim3(256), narrow_smem, stream, y, w.narrow_weight, w.narrow_bias, narrow,
+                              eval_in, M, D);
+    if (status != cudaSuccess) return status;
+    status = launch_dependent(policy_kernel, dim3(B), dim3(256), 0, stream, a, y, narrow, rows, D);
+    if (status != cudaSuccess) return status;
     // the eval head: hidden = GELU(W1 . eval_in + b1), logits = W2 . hidden + b2, each as split-K partial products
     const int split1 = split_size(kEvalInputs), splits1 = (kEvalInputs + split1 - 1) / split1;
-    linear_split_kernel<<<dim3((D + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits1), 256, 0, stream>>>(
-        eval_in, w.hidden_weight, partial, B, kEvalInputs, D, split1);
-    linear_sum_kernel<true><<<(B * D + 255) / 256, 256, 0, stream>>>(partial, w.hidden_bias, hidden, B, D, splits1);
+    status = launch_dependent(linear_split_kernel, dim3((D + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits1),
+                              dim3(256), 0, stream, eval_in, w.hidden_weight, partial, B, kEvalInputs, D, split1);
+    if (status != cudaSuccess) return status;
+    status = launch_dependent(linear_sum_kernel<true>, dim3((B * D + 255) / 256), dim3(256), 0, stream, partial, w.hidden_bias, hidden, B, D,
+                              splits1);
+    if (status != cudaSuccess) return status;
     const int split2 = split_size(D), splits2 = (D + split2 - 1) / split2;
-    linear_split_kernel<<<dim3((w.bins + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits2), 256, 0, stream>>>(
-        hidden, w.out_weight, partial, B, D, w.bins, split2);
-    linear_sum_kernel<false><<<(B * w.bins + 255) / 256, 256, 0, stream>>>(partial, w.out_bias, value_logits, B, w.bins, splits2);
-    expected_score_kernel<<<(B + 7) / 8, 256, 0, stream>>>(value_logits, rows, B, w.bins);
-    return cudaGetLastError();
+    status = launch_dependent(linear_split_kernel, dim3((w.bins + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits2),
+                              dim3(256), 0, stream, hidden, w.out_weight, partial, B, D, w.bins, split2);
+    if (status != cudaSuccess) return status;
+    status = launch_dependent(linear_sum_kernel<false>, dim3((B * w.bins + 255) / 256), dim3(256), 0, stream, partial, w.out_bias, value_logits,
+                              B, w.bins, splits2);
+    if (status != cudaSuccess) return status;
+    return launch_dependent(expected_score_kernel, dim3((B + 7) / 8), dim3(256), 0, stream, value_logits, rows, B, w.bins);
 }
 
 }  // namespace fry

@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) norm_quant_kern
                                                                     const uint16_t* residual_scale, const uint16_t* input_scale,
                                                                     const uint16_t* __restrict__ gain, float eps, uint16_t* mixed,
                                                                     int8_t* __restrict__ q, float* __restrict__ scale, int M, int D) {
+    grid_dependency_start();
     const int lane = threadIdx.x & 31;
     const int stride = gridDim.x * kRowWarps;
     int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) norm_quant_kern
 template <int CHUNKS>
 __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gain, float eps,
                                                                   uint16_t* __restrict__ y, int M, int D) {
+    grid_dependency_start();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowWarps + warp;
     if (row >= M) return;
@@ -102,6 +104,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
 constexpr int kRotateRows = 2;
 __global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
                                                                       float* __restrict__ scale, int M, int hidden, int width) {
+    grid_dependency_start();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int first_row = (blockIdx.x * kRowWarps + warp) * kRotateRows;
     if (first_row >= M) return;
@@ -135,6 +138,7 @@ FRY_DEVICE int code_at(const int* codes, int file, int rank) {
 __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ boards, const uint16_t* __restrict__ embed,
                                                         const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
                                                         uint16_t* __restrict__ out, int D) {
+    grid_dependency_start();
     __shared__ int codes[kTokens];
     __shared__ int firsts[4];
     __shared__ int rows[kSquares][kFeatures];
@@ -248,11 +252,11 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
     const int wanted = (M + kRowWarps - 1) / kRowWarps, most = multiprocessors * kRowCtasPerSm;
     const dim3 grid(wanted < most ? wanted : most);
     const int chunks = (D + 255) / 256;
-#define FRY_NQ(C)                                                                                                                   \
-    (mix ? (norm_quant_kernel<C, true><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, mixed, \
-                                                                             q, scale, M, D), 0)                                    \
-         : (norm_quant_kernel<C, false><<<grid, kRowWarps * 32, 0, stream>>>(x, original, residual_scale, input_scale, gain, eps, mixed, \
-                                                                              q, scale, M, D), 0))
+#define FRY_NQ(C)                                                                                                                  \
+    status = mix ? launch_dependent(norm_quant_kernel<C, true>, grid, dim3(kRowWarps * 32), 0, stream, x, original, residual_scale,   \
+                                    input_scale, gain, eps, mixed, q, scale, M, D)                                                  \
+                 : launch_dependent(norm_quant_kernel<C, false>, grid, dim3(kRowWarps * 32), 0, stream, x, original, residual_scale,  \
+                                    input_scale, gain, eps, mixed, q, scale, M, D)
     switch (chunks) {
         case 1: FRY_NQ(1); break;
         case 2: FRY_NQ(2); break;
@@ -260,7 +264,7 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
         default: FRY_NQ(4); break;
     }
 #undef FRY_NQ
-    return cudaGetLastError();
+    return status;
 }
 
 cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream) {
@@ -268,28 +272,26 @@ cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uin
     if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
     const dim3 grid((M + kRowWarps - 1) / kRowWarps);
     switch ((D + 255) / 256) {
-        case 1: rms_norm_kernel<1><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
-        case 2: rms_norm_kernel<2><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
-        case 3: rms_norm_kernel<3><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
-        default: rms_norm_kernel<4><<<grid, kRowWarps * 32, 0, stream>>>(x, gain, eps, y, M, D); break;
+        case 1: return launch_dependent(rms_norm_kernel<1>, grid, dim3(kRowWarps * 32), 0, stream, x, gain, eps, y, M, D);
+        case 2: return launch_dependent(rms_norm_kernel<2>, grid, dim3(kRowWarps * 32), 0, stream, x, gain, eps, y, M, D);
+        case 3: return launch_dependent(rms_norm_kernel<3>, grid, dim3(kRowWarps * 32), 0, stream, x, gain, eps, y, M, D);
+        default: return launch_dependent(rms_norm_kernel<4>, grid, dim3(kRowWarps * 32), 0, stream, x, gain, eps, y, M, D);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (hidden % 8 != 0 || width % 32 != 0 || width > 1024 || hidden > width) return cudaErrorInvalidValue;
     const int rows_a_block = kRowWarps * kRotateRows;
-    rotate_quant_kernel<<<(M + rows_a_block - 1) / rows_a_block, kRowWarps * 32, 0, stream>>>(h, q, scale, M, hidden, width);
-    return cudaGetLastError();
+    return launch_dependent(rotate_quant_kernel, dim3((M + rows_a_block - 1) / rows_a_block), dim3(kRowWarps * 32), 0, stream, h, q, scale, M,
+                            hidden, width);
 }
 
 cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
                             uint16_t* out, int B, int D, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
     if (D % 8 != 0) return cudaErrorInvalidValue;
-    embedding_kernel<<<dim3(B, (D + 255) / 256), 256, 0, stream>>>(boards, embed, position, table, out, D);
-    return cudaGetLastError();
+    return launch_dependent(embedding_kernel, dim3(B, (D + 255) / 256), dim3(256), 0, stream, boards, embed, position, table, out, D);
 }
 
 }  // namespace fry
