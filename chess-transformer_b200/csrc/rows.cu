@@ -99,25 +99,23 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
     }
 }
 
-// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M], by rotate_quant_row. A warp
-// takes kRotateRows consecutive rows, their loads all issued first.
-constexpr int kRotateRows = 2;
-__global__ void __launch_bounds__(kRowWarps * 32) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
-                                                                      float* __restrict__ scale, int M, int hidden, int width) {
+// h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M], by rotate_quant_row.
+// Persistent warps, as norm_quant: warp w of W takes rows w, w + W, ..., loading the next row while it works on one.
+__global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
+                                                                                     float* __restrict__ scale, int M, int hidden, int width) {
     grid_dependency_start();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int first_row = (blockIdx.x * kRowWarps + warp) * kRotateRows;
-    if (first_row >= M) return;
-    uint4 raw[kRotateRows][4];
+    const int lane = threadIdx.x & 31;
+    const int stride = gridDim.x * kRowWarps;
+    int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    if (row >= M) return;
+    uint4 raw[4];
+    load_row_chunks<4>(h + static_cast<size_t>(row) * hidden, hidden, lane, raw);
+    for (; row < M; row += stride) {  // uniform across the warp
+        uint4 next[4];
+        if (row + stride < M) load_row_chunks<4>(h + static_cast<size_t>(row + stride) * hidden, hidden, lane, next);
+        rotate_quant_row(raw, width, lane, q + static_cast<size_t>(row) * width, scale + row);
 #pragma unroll
-    for (int r = 0; r < kRotateRows; ++r) {
-        if (first_row + r < M) load_row_chunks<4>(h + static_cast<size_t>(first_row + r) * hidden, hidden, lane, raw[r]);
-    }
-#pragma unroll
-    for (int r = 0; r < kRotateRows; ++r) {
-        const int row = first_row + r;
-        if (row >= M) break;  // uniform across the warp
-        rotate_quant_row(raw[r], width, lane, q + static_cast<size_t>(row) * width, scale + row);
+        for (int c = 0; c < 4; ++c) raw[c] = next[c];
     }
 }
 
@@ -282,9 +280,13 @@ cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uin
 cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (hidden % 8 != 0 || width % 32 != 0 || width > 1024 || hidden > width) return cudaErrorInvalidValue;
-    const int rows_a_block = kRowWarps * kRotateRows;
-    return launch_dependent(rotate_quant_kernel, dim3((M + rows_a_block - 1) / rows_a_block), dim3(kRowWarps * 32), 0, stream, h, q, scale, M,
-                            hidden, width);
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const int wanted = (M + kRowWarps - 1) / kRowWarps, most = multiprocessors * kRowCtasPerSm;
+    return launch_dependent(rotate_quant_kernel, dim3(wanted < most ? wanted : most), dim3(kRowWarps * 32), 0, stream, h, q, scale, M, hidden,
+                            width);
 }
 
 cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
