@@ -50,45 +50,82 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def workload_config(world: int) -> dict:
+    """The workload both arms measure (the reference arm on a bounded sample of it)."""
+    return {"workload": "fry-28L-int8-forward-b256", "model": "fry d768, 28 blocks, 24q/12kv heads, dq 8/16/24, SwiGLU 992",
+            "global_batch": BATCH * world, "seq_len": 70, "l2": "flushed between steps (256 MiB write outside the timed events)",
+            "weights": "random-init N(0,0.02), round-to-nearest int8"}
+
+
 class ClockSampler:
-    """nvidia-smi clock and throttle-reason samples every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons sampled every 5 ms through NVML while the timed region runs (a
+    reader only: it changes no setting); nvidia-smi every 200 ms where NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
         self.device_index = device_index
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.process = None
+        self.samples, self.max_mhz, self.source = [], None, None
+        self.stop = threading.Event()
+        self.thread = self.process = self.file = None
+
+    def _poll(self, nvml, handle):
+        reasons = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown, "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                   "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown, "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+        while not self.stop.is_set():
+            try:
+                mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.samples.append((float(mhz), sorted(name for name, bit in reasons.items() if mask & bit)))
+            except Exception:
+                pass
+            self.stop.wait(0.005)
 
     def __enter__(self):
         try:
-            self.process = subprocess.Popen(["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                             "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.process = None
+            import pynvml as nvml
+            nvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.device_index]) if visible and visible.split(",")[0].isdigit() else self.device_index
+            handle = nvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, args=(nvml, handle), daemon=True)
+            self.thread.start()
+            self.source = "nvml, every 5 ms"
+        except Exception:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            try:
+                self.process = subprocess.Popen(["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                                                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+                self.source = "nvidia-smi, every 200 ms"
+            except OSError:
+                self.process = None
         return self
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
         if self.process is not None:
             self.process.terminate()
             self.process.wait(timeout=10)
 
     def summary(self) -> dict:
-        self.file.flush()
-        self.file.seek(0)
-        rows = [line.split(",") for line in self.file.read().splitlines() if line.strip()]
-        Path(self.file.name).unlink(missing_ok=True)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        reasons = set()
-        for r in rows:
-            for name, value in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
-                if value.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip() else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        if self.file is not None:
+            self.file.flush()
+            self.file.seek(0)
+            for row in (line.split(",") for line in self.file.read().splitlines() if line.strip()):
+                if row[1].strip().replace(".", "").isdigit():
+                    names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+                    self.samples.append((float(row[1]), sorted(n for n, v in zip(names, row[5:9]) if v.strip().lower() == "active")))
+                    self.max_mhz = float(row[2]) if row[2].strip() else self.max_mhz
+            Path(self.file.name).unlink(missing_ok=True)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no clock samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(mhz for mhz, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted({name for _, names in self.samples for name in names}), "samples": len(self.samples),
+                "source": self.source}
 
 
 def reference_arm(args, rank: int) -> None:
@@ -115,8 +152,8 @@ def reference_arm(args, rank: int) -> None:
     line = {"metric": "positions/sec (28L int8 fwd, batch 256)", "value": value, "unit": "positions/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "fry-28L-forward-b256", "sample": f"{sample} boards a step (bounded CPU sample of the batch of 256)",
-                       "seq_len": 70, "parallelism": "host cores"},
+            "config": {**workload_config(1), "parallelism": "host cores",
+                       "sample": f"{sample} boards a step (bounded CPU sample of the batch of 256)"},
             "cpu_baseline": {"value": value, "unit": "positions/s", "cores": cores, "kind": "port",
                              "sample": f"{sample} boards x {args.steps} steps, fp32 ChessTransformer forward (oracle/model.py) "
                                        f"on {cores} threads, {os.cpu_count()} host cores"},
@@ -326,9 +363,7 @@ def main() -> None:
         line = {"metric": "positions/sec (28L int8 fwd, batch 256)", "value": BATCH * args.steps * world / seconds, "unit": "positions/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * seconds / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-                "config": {"workload": "fry-28L-int8-forward-b256", "model": "fry d768, 28 int8 blocks, 24q/12kv heads, dq 8/16/24, SwiGLU 992",
-                           "global_batch": BATCH * world, "seq_len": 70, "parallelism": f"replicas x{world}",
-                           "l2": "flushed between steps (256 MiB write outside the timed events)", "weights": "random-init N(0,0.02), round-to-nearest int8"},
+                "config": {**workload_config(world), "parallelism": f"replicas x{world}"},
                 "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
                         "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4},
                 "gpu_launches": 231 * args.steps,
