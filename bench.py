@@ -198,7 +198,7 @@ def gemm_roofline(torch, stream) -> dict:
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     with torch.cuda.stream(stream):
         for name, (N, K, kind, count) in GEMMS.items():
-            if kind == "fp16":
+            if kind == "fp16" or count == 0:
                 continue
             run = gemm_runner(torch, ops, name, M)
             for _ in range(3):
@@ -213,7 +213,7 @@ def gemm_roofline(torch, stream) -> dict:
                 end.synchronize()
                 times.append(start.elapsed_time(end) / 1000)
             seconds = statistics.mean(times)
-            ops_per_launch = 2.0 * M * K * N * (2 if kind == "gated" else 1)
+            ops_per_launch = 2.0 * M * K * N * (2 if kind.startswith("gated") else 1)
             per_shape[f"{name}_{N}x{K}"] = round(ops_per_launch / seconds / 1e12, 1)
             total_ops += ops_per_launch * count
             total_seconds += seconds * count

@@ -82,6 +82,26 @@ int fry_int8_linear(const int8_t* x, const float* x_scale, const int8_t* weight,
     return check(fry::gemm(0, epilogue, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_linear", detail);
 }
 
+int fry_int8_linear_normed(const uint16_t* x, const uint16_t* gain, float eps, const int8_t* weight, const float* weight_scale,
+                           const uint16_t* bias, uint16_t* out, int M, int N, int K, int gated, void* stream) {
+    if (M < 0 || N <= 0 || N % 8 != 0 || K != 768)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear_normed takes K = 768 and N a multiple of 8, got N " + std::to_string(N) + ", K " +
+                                         std::to_string(K));
+    if (!aligned16(x) || !aligned16(gain) || !aligned16(weight) || !aligned16(out))
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear_normed reads and writes 16-byte vectors: x, gain, weight and out must be 16-byte aligned");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.w_scale = weight_scale;
+    args.bias = bias;
+    args.out = out;
+    args.norm_x = x;
+    args.norm_gain = gain;
+    args.norm_eps = eps;
+    std::string detail;
+    return check(fry::gemm(0, gated ? fry::kEpiGated : fry::kEpiBias, nullptr, weight, args, M, N, K, as_stream(stream), &detail),
+                 "fry_int8_linear_normed", detail);
+}
+
 int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int M, int N, int K, void* stream) {
     if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0)
         return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_i32 takes N a multiple of 8 and K a multiple of 16");
@@ -216,6 +236,8 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
     const size_t heads_bytes = fry::heads_workspace_bytes(B, D);
     void* heads_workspace = take(heads_bytes);
 
+    // ln1 and ln2 run as their own kernels: the GEMMs with the norm in their prologue (fry_int8_linear_normed) measured
+    // no faster at 256 boards and slower at small batches, where each CTA of a row block repeats the block's norm
     std::string detail;
     cudaError_t status = fry::board_embedding(boards, n->embed, n->position, n->table, original, B, D, s);
     if (status != cudaSuccess) return check(status, "fry_forward: embedding");

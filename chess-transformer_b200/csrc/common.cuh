@@ -277,6 +277,12 @@ FRY_DEVICE float warp_max(float v) {
     for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
     return v;
 }
+// The warp's maximum of v in one instruction (sm_100's f32 redux.sync); NaN lanes are ignored, as fmaxf ignores them.
+FRY_DEVICE float warp_max_redux(float v) {
+    float m;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+    return m;
+}
 FRY_DEVICE float h2f(__half h) { return __half2float(h); }
 FRY_DEVICE float h2f_bits(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
 FRY_DEVICE uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }

@@ -19,12 +19,18 @@
 // operands (residual, original) arrive the same way, as TMA loads of the same boxes that warp 18 issues a sub-tile ahead
 // into the other of two slots, and each output overwrites its residual in the slot. A tile's column operands (weight
 // scales, bias) are staged one tile ahead in shared memory too, so one barrier a sub-tile suffices.
+//
+// Normed A (NKS > 0): the int8 A operand is not loaded but made in the prologue of each 128-row block: the epilogue warps
+// run norm_quant (rowops.cuh) on the block's fp16 rows straight into NKS resident 128-byte K slices of shared memory,
+// in the layout the MMA reads, and the row scales beside them; the CTA then takes every column tile of the block in turn
+// while only B streams. The norm's output never reaches global memory.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "rowops.cuh"
 
 namespace fry {
 
@@ -44,16 +50,21 @@ constexpr int kBoxBytes = kBlockM * kBoxCols * 2;  // a staged fp16 box: 128 row
 // reserved shared memory), as the 128-byte swizzle atoms need; a kernel checks and records kMisaligned otherwise.
 constexpr int kBarrierBytes = 256;
 constexpr int kSmemBudget = 227 * 1024 - kBarrierBytes;
+constexpr int kNormedK = 768, kNormedSlices = kNormedK / kTileKBytes;  // the one width a normed A is built for
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
-template <int KIND, int BN, bool GATED, int EPI, int SUB>
+template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS>
 struct GemmShape {
     static constexpr int kElem = KIND == 0 ? 1 : 2;
     static constexpr int kBoxK = kTileKBytes / kElem;
     static constexpr int kABytes = kBlockM * kTileKBytes;
     static constexpr int kBBytes = BN * kTileKBytes;
-    static constexpr int kStageBytes = kABytes + kBBytes * (GATED ? 2 : 1);
+    // a normed A is resident (NKS slices), so a stage holds B alone
+    static constexpr int kResidentBytes = NKS * kABytes;
+    static constexpr int kRowScaleBytes = NKS > 0 ? kBlockM * 4 : 0;
+    static constexpr int kStageBytes = (NKS > 0 ? 0 : kABytes) + kBBytes * (GATED ? 2 : 1);
+    static_assert(NKS == 0 || (KIND == 0 && NKS * kTileKBytes <= 1024 && NKS % 2 == 0), "a normed A is int8, 256 to 1024 columns");
     // fp16 outputs are staged for TMA stores; int32 and fp32 outputs are stored by their threads
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
     // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
@@ -69,13 +80,13 @@ struct GemmShape {
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
     static constexpr int kColumnBytes = 2 * 2 * BN * 4;
-    static constexpr int kStagesFit = (kSmemBudget - kIoBytes - kColumnBytes) / kStageBytes;
+    static constexpr int kStagesFit = (kSmemBudget - kResidentBytes - kRowScaleBytes - kIoBytes - kColumnBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kIoBytes + kStages * kStageBytes + kColumnBytes + kBarrierBytes;
+    static constexpr int kSmemBytes = kResidentBytes + kIoBytes + kStages * kStageBytes + kColumnBytes + kRowScaleBytes + kBarrierBytes;
     static_assert(kAccCols % 16 == 0 && kAccCols >= 16 && kAccCols <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
@@ -207,38 +218,101 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
     }
 }
 
-template <int KIND, int BN, bool GATED, int EPI, int SUB>
+// The prologue of a normed A: the epilogue warps (warp w: rows w, w + 16, ... of the block) turn the block's fp16 rows of
+// p.norm_x into int8 rows of the resident A, zero past M, and their scales into row_scales.
+template <int NKS>
+FRY_DEVICE void norm_rows_into_a(const GemmArgs& p, uint8_t* resident, float* row_scales, int m0, int M, int warp, int lane) {
+    constexpr int kChunks = NKS / 2, K = NKS * kTileKBytes;      // 256 columns a chunk, 128 a slice
+    constexpr int kRows = kBlockM / kEpilogueWarps, kAhead = 2;  // rows of a warp; rows in flight beyond the one worked on
+    float gain[kChunks][8];
+    load_gain<kChunks>(p.norm_gain, K, lane, gain);
+    const uint64_t unused = pair2(0.0f, 0.0f);
+    const uint4 no_original[1] = {make_uint4(0, 0, 0, 0)};
+    uint4 raw[kRows][kChunks];  // unrolled: kAhead + 1 of them live at a time
+    auto load = [&](int i) {
+        const int row = m0 + warp + i * kEpilogueWarps;
+        if (row < M) {
+            load_row_chunks<kChunks>(p.norm_x + static_cast<size_t>(row) * K, K, lane, raw[i]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) raw[i][c] = make_uint4(0, 0, 0, 0);
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) load(i);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+        if (i + kAhead < kRows) load(i + kAhead);
+        const int r = warp + i * kEpilogueWarps;
+        const SwizzledRowOut out{resident, r};
+        if (m0 + r < M) {  // uniform across the warp
+            norm_quant_row<kChunks, false, SwizzledRowOut>(raw[i], no_original, gain, unused, unused, p.norm_eps, K, lane, nullptr, out,
+                                                           row_scales + r);
+        } else {  // a row past M: zeros, so its accumulator rows stay 0
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c)
+                if ((c * 32 + lane) * 8 < K) out.put8((c * 32 + lane) * 8, make_uint2(0u, 0u));
+            if (lane == 0) row_scales[r] = 0.0f;
+        }
+    }
+}
+
+template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_residual,
                 const __grid_constant__ CUtensorMap map_original, const GemmArgs args, int M, int N, int K) {
-    using S = GemmShape<KIND, BN, GATED, EPI, SUB>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS>;
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023u) {  // uniform across the CTA: every thread leaves before any barrier
         if (threadIdx.x == 0) record_error(kMisaligned, 20);
         return;
     }
-    uint8_t* stages = smem;                                              // [kStages][A box | B box(es)]
+    uint8_t* resident = smem;                                            // a normed A: [NKS][128 rows][128 bytes, swizzled]
+    uint8_t* stages = smem + S::kResidentBytes;                          // [kStages][A box | B box(es)]
     uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kBoxes][128 rows][128 bytes, swizzled]
-    // sub-tiles in the order this CTA takes them: (tile, s) -> (tile, s + 1), or the next tile's first
-    auto advance = [&](int& tile, int& sub) {
-        if (++sub == S::kSubs) {
-            sub = 0;
-            tile += static_cast<int>(gridDim.x);
-        }
-    };
     float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][2 * BN]
-    uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes);
+    float* row_scales = reinterpret_cast<float*>(io + S::kIoBytes + S::kColumnBytes);  // a normed A's [128]
+    uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes + S::kRowScaleBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
     uint64_t* rows_full = tmem_empty + 2;       // [2]: a slot's row operands have landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rows_full + 2);
+    uint64_t* a_ready = rows_full + 2;          // a normed A's block is in place (all epilogue warps)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_ready + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = (N + BN - 1) / BN;
-    const int tiles = ((M + kBlockM - 1) / kBlockM) * n_blocks;
+    const int row_blocks = (M + kBlockM - 1) / kBlockM;
+    const int tiles = row_blocks * n_blocks;
     const int k_tiles = (K * S::kElem + kTileKBytes - 1) / kTileKBytes;
+    // Tile order (tile = row block * n_blocks + column tile). Plain: round robin over the tiles. Normed A: round robin over
+    // units, a unit being a row block's column tiles g, g + groups, ... (groups = gridDim.x / row_blocks, at least 1, the
+    // launch's choice), so a CTA makes a unit's A once and reuses it for each of the unit's tiles.
+    const int groups = NKS > 0 ? max(1, static_cast<int>(gridDim.x) / row_blocks) : 1;
+    auto unit_tile = [&](int unit) { return (unit / groups) * n_blocks + unit % groups; };
+    const int first_tile = NKS > 0 ? unit_tile(blockIdx.x) : static_cast<int>(blockIdx.x);
+    auto next_tile = [&](int tile) {
+        if (NKS == 0) return tile + static_cast<int>(gridDim.x);
+        const int column = tile % n_blocks;
+        if (column + groups < n_blocks) return tile + groups;
+        const int unit = (tile / n_blocks) * groups + column % groups + static_cast<int>(gridDim.x);
+        return unit / groups < row_blocks ? unit_tile(unit) : tiles;
+    };
+    auto unit_start = [&](int tile) { return NKS > 0 && tile % n_blocks < groups; };
+    // a tile's first output column. Normed A: row block b takes its column tiles rotated by b, so the CTAs, which start
+    // their units together, stream different B tiles rather than all the same one
+    auto column0 = [&](int tile) {
+        const int column = tile % n_blocks;
+        return (NKS > 0 ? (column + tile / n_blocks) % n_blocks : column) * BN;
+    };
+    // sub-tiles in the order this CTA takes them: (tile, s) -> (tile, s + 1), or the next tile's first
+    auto advance = [&](int& tile, int& sub) {
+        if (++sub == S::kSubs) {
+            sub = 0;
+            tile = next_tile(tile);
+        }
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::kStages; ++s) {
@@ -250,6 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&tmem_empty[b], kEpilogueWarps);
             mbar_init(&rows_full[b], 1);
         }
+        mbar_init(a_ready, kEpilogueWarps);
         fence_barrier_init();
     }
     if (warp == 0) {
@@ -270,8 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (elect_one()) {
             int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN;
+            for (int tile = first_tile; tile < tiles && ok; tile = next_tile(tile)) {
+                const int m0 = (tile / n_blocks) * kBlockM, n0 = column0(tile);
                 for (int kt = 0; kt < k_tiles; ++kt, ++it) {
                     const int s = it % S::kStages;
                     const uint32_t phase = (it / S::kStages) & 1;
@@ -280,9 +355,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         break;
                     }
                     uint8_t* a = stages + s * S::kStageBytes;
-                    uint8_t* b = a + S::kABytes;
+                    uint8_t* b = NKS > 0 ? a : a + S::kABytes;
                     mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-                    tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
+                    if constexpr (NKS == 0) tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
                     tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
                     if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
                 }
@@ -293,10 +368,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // gated: the gate's and the up's B boxes lie back to back, 2 BN rows at the swizzle's 1024 bytes per 8, so one MMA of
             // N = 2 BN fills both accumulator halves
             constexpr uint32_t idesc = instr_desc<KIND>(S::kAccCols);
-            int it = 0, local = 0;
+            int it = 0, local = 0, units = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local) {
+            for (int tile = first_tile; tile < tiles && ok; tile = next_tile(tile), ++local) {
                 const int buffer = local & 1;
+                if (unit_start(tile) && !mbar_wait(a_ready, (units++) & 1, 16)) break;  // the unit's A is made
                 if (!mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)) break;
                 tc_fence_after();
                 const uint32_t accumulator = tmem + buffer * S::kAccCols;
@@ -308,8 +384,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a = smem_addr(stages + s * S::kStageBytes);
-                    const uint32_t b = a + S::kABytes;
+                    const uint32_t stage = smem_addr(stages + s * S::kStageBytes);
+                    const uint32_t a = NKS > 0 ? smem_addr(resident) + kt * S::kABytes : stage;
+                    const uint32_t b = NKS > 0 ? stage : stage + S::kABytes;
 #pragma unroll
                     for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
                         const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
@@ -331,22 +408,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             auto load_rows = [&](int tile, int sub, int slot) {
                 if (!issuer || !has_rows || tile >= tiles) return;
                 load_sub_rows<EPI, SUB>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
-                                        (tile / n_blocks) * kBlockM, (tile % n_blocks) * BN + sub * SUB, N);
+                                        (tile / n_blocks) * kBlockM, column0(tile) + sub * SUB, N);
             };
-            int ahead_tile = blockIdx.x, ahead_sub = 0;  // the sub-tile two ahead of the one being stored
+            int ahead_tile = first_tile, ahead_sub = 0;  // the sub-tile two ahead of the one being stored
             load_rows(ahead_tile, ahead_sub, 0);
             advance(ahead_tile, ahead_sub);
             load_rows(ahead_tile, ahead_sub, 1);
             advance(ahead_tile, ahead_sub);
             epilogue_sync();  // the first tile's column operands are staged
             int j = 0;
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            for (int tile = first_tile; tile < tiles; tile = next_tile(tile)) {
                 for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
                     const int slot = j & 1;
                     __syncwarp();
                     epilogue_sync();  // sub-tile j is staged
                     if (issuer) {
-                        const int m0 = (tile / n_blocks) * kBlockM, n0 = (tile % n_blocks) * BN + sub * SUB;
+                        const int m0 = (tile / n_blocks) * kBlockM, n0 = column0(tile) + sub * SUB;
                         uint8_t* staged = io + slot * S::kSlotBytes;
                         for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
                             tma_store_2d(&map_out, staged + b * kBoxBytes, n0 + b * kBoxCols, m0);
@@ -360,7 +437,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (issuer) bulk_wait_all();
         } else {
             epilogue_sync();
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) epilogue_sync();
+            for (int tile = first_tile; tile < tiles; tile = next_tile(tile)) epilogue_sync();
         }
     } else {
         // warps 0-15: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows m0 + 32 (w % 4) + lane) and the 16-column chunks
@@ -375,7 +452,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
         auto tile_origin = [&](int tile, int& m0, int& n0) {
             m0 = (tile / n_blocks) * kBlockM;
-            n0 = (tile % n_blocks) * BN;
+            n0 = column0(tile);
         };
         // a tile's column operands and this thread's row scale are fetched during the tile before (the first tile's here),
         // into the other of two column buffers, so one barrier a tile publishes both the staged outputs and them
@@ -385,21 +462,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
-            if constexpr (EPI <= kEpiMix) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
+            if constexpr (EPI <= kEpiMix && NKS == 0) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
             if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, column_buffers + buffer * 2 * BN, n0, N, threadIdx.x);
         };
-        fetch_operands(blockIdx.x, 0);
+        fetch_operands(first_tile, 0);
         epilogue_sync();
         // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
         // epilogue warps never wait at the barrier for it
-        int local = 0, j = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+        int local = 0, j = 0, units = 0;
+        float xs_unit = 0.0f;
+        for (int tile = first_tile; tile < tiles; tile = next_tile(tile), ++local) {
             const int buffer = local & 1;
-            const int next = tile + static_cast<int>(gridDim.x);
+            const int next = next_tile(tile);
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
-            const float xs = xs_next;
+            if constexpr (NKS > 0) {
+                if (unit_start(tile)) {
+                    // the unit's A: every earlier tile's accumulator has been read, so the MMAs that read the last A are done
+                    if (alive) norm_rows_into_a<NKS>(args, resident, row_scales, m0, M, warp, lane);
+                    fence_proxy_async_shared();  // this thread's A bytes, visible to the MMAs
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(a_ready);
+                    if (alive && !mbar_wait(a_ready, (units++) & 1, 15)) alive = false;
+                    xs_unit = alive ? row_scales[row_in_tile] : 0.0f;
+                }
+            }
+            const float xs = NKS > 0 ? xs_unit : xs_next;
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             const float* columns = column_buffers + buffer * 2 * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -507,15 +596,19 @@ bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::s
     return true;
 }
 
-template <int KIND, int BN, bool GATED, int EPI, int SUB = BN>
+template <int KIND, int BN, bool GATED, int EPI, int SUB = BN, int NKS = 0>
 cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
-    using S = GemmShape<KIND, BN, GATED, EPI, SUB>;
-    auto kernel = gemm_kernel<KIND, BN, GATED, EPI, SUB>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS>;
+    auto kernel = gemm_kernel<KIND, BN, GATED, EPI, SUB, NKS>;
     const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
     if (attribute != cudaSuccess) return attribute;
     CUtensorMap map_a, map_b, map_out, map_residual, map_original;
-    if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error) || !make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error))
+    if (!make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error)) return cudaErrorInvalidValue;
+    if (NKS > 0) {
+        map_a = map_b;  // a normed A is made in shared memory, not loaded
+    } else if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error)) {
         return cudaErrorInvalidValue;
+    }
     // the staged epilogues' maps; unused ones repeat the output's, which is always valid
     map_out = map_residual = map_original = map_a;
     if constexpr (S::kStaged) {
@@ -524,13 +617,21 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
         if (args.residual && !make_box_map(&map_residual, args.residual, N, M, error)) return cudaErrorInvalidValue;
         if (EPI == kEpiMix && !make_box_map(&map_original, args.original, N, M, error)) return cudaErrorInvalidValue;
     }
-    const int tiles = ((M + kBlockM - 1) / kBlockM) * ((N + BN - 1) / BN);
+    const int row_blocks = (M + kBlockM - 1) / kBlockM, n_blocks = (N + BN - 1) / BN, tiles = row_blocks * n_blocks;
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    return launch_dependent(kernel, dim3(tiles < multiprocessors ? tiles : multiprocessors), dim3(kGemmThreads), S::kSmemBytes, stream, map_a,
-                            map_b, map_out, map_residual, map_original, args, M, N, K);
+    int grid = tiles < multiprocessors ? tiles : multiprocessors;
+    if (NKS > 0) {
+        // units: each row block's column tiles in as many groups as leave every SM one unit (at least one a block); the
+        // kernel reads the group count back as grid / row blocks
+        int groups = multiprocessors / row_blocks;
+        groups = groups < 1 ? 1 : groups > n_blocks ? n_blocks : groups;
+        grid = row_blocks * groups < multiprocessors ? row_blocks * groups : multiprocessors;
+    }
+    return launch_dependent(kernel, dim3(grid), dim3(kGemmThreads), S::kSmemBytes, stream, map_a, map_b, map_out, map_residual,
+                            map_original, args, M, N, K);
 }
 
 }  // namespace
@@ -549,6 +650,20 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
     auto tiles = [&](int bn) { return row_blocks * ((N + bn - 1) / bn); };
     // the widest tile whose count fills the SMs (or the narrowest)
     const int width = tiles(256) >= multiprocessors ? 256 : tiles(128) >= multiprocessors ? 128 : 64;
+    if (args.norm_x) {
+        // a normed A (NKS = 6 resident K slices: the model width 768); 128-column tiles leave room for 6 pipeline stages
+        // beside it, 64-column ones fill the SMs at small batches
+        if (kind != 0 || K != kNormedK || (epilogue != kEpiBias && epilogue != kEpiGated)) {
+            if (error) *error = "a normed A takes the int8 bias or gated epilogue and K = " + std::to_string(kNormedK);
+            return cudaErrorInvalidValue;
+        }
+        const bool wide = tiles(128) >= multiprocessors;
+        if (epilogue == kEpiBias)
+            return wide ? launch<0, 128, false, kEpiBias, 64, kNormedSlices>(a, b, args, M, N, K, stream, error)
+                        : launch<0, 64, false, kEpiBias, 64, kNormedSlices>(a, b, args, M, N, K, stream, error);
+        return wide ? launch<0, 128, true, kEpiGated, 64, kNormedSlices>(a, b, args, M, N, K, stream, error)
+                    : launch<0, 64, true, kEpiGated, 64, kNormedSlices>(a, b, args, M, N, K, stream, error);
+    }
     if (kind == 0) {
         switch (epilogue) {
             case kEpiBias:

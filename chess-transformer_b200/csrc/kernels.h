@@ -30,6 +30,11 @@ struct GemmArgs {
     const uint16_t* residual_scale = nullptr;  // fp16 scalar
     const uint16_t* input_scale = nullptr;     // fp16 scalar
     void* out = nullptr;                     // [M, N]
+    // Normed A (kind 0, bias or gated epilogue, K = 768): A is norm_quant(norm_x) with norm_gain and norm_eps, made in
+    // the GEMM's prologue; `a` and x_scale are then unused.
+    const uint16_t* norm_x = nullptr;        // fp16 [M, K]
+    const uint16_t* norm_gain = nullptr;     // fp16 [K]
+    float norm_eps = 0.0f;
 };
 
 // kind 0: int8 A [M, K], B [N, K] (gated: [2N, K]); kind 1: fp16 A [M, K], B [N, K].

@@ -9,10 +9,29 @@
 
 namespace fry {
 
+// fp16 -> fp32 on the FMA pipe rather than the conversion unit, which bounds a row's throughput otherwise: the mixed
+// precision add (PTX add.f32.f16, sm_100) of -0.0: exact for every finite or infinite input (a NaN stays a NaN).
+FRY_DEVICE float h2f_exact(uint16_t bits) {
+    float value;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(value) : "h"(bits), "f"(-0.0f));
+    return value;
+}
+
 FRY_DEVICE void unpack8(const uint4& u, float (&v)[8]) {
     const uint16_t* h = reinterpret_cast<const uint16_t*>(&u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = h2f_bits(h[i]);
+    for (int i = 0; i < 8; ++i) v[i] = h2f_exact(h[i]);
+}
+
+// The gain's values at this lane's columns of each chunk (zero past `width`), unpacked once for every row a warp takes
+// where registers allow; norm_quant_row also takes the packed fp16 chunks (load_row_chunks) and unpacks them per row.
+template <int CHUNKS>
+FRY_DEVICE void load_gain(const uint16_t* gain, int width, int lane, float (&to)[CHUNKS][8]) {
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        unpack8(col < width ? *reinterpret_cast<const uint4*>(gain + col) : make_uint4(0, 0, 0, 0), to[c]);
+    }
 }
 
 // The row's fp16 chunks of this lane, zero past `width` columns.
@@ -25,15 +44,18 @@ FRY_DEVICE void load_row_chunks(const uint16_t* row, int width, int lane, uint4 
     }
 }
 
-// rint(v * step) for 8 values as 8 int8 bytes: the low byte of each int32, placed by byte permutes.
+// rint(v * step) for 8 values (|v * step| < 2^22) as 8 int8 bytes. The product, rounded to fp32, plus 1.5 * 2^23 lands
+// in [2^23, 2^24), where the fp32 spacing is 1, so the add's round-to-nearest-even leaves rint(product) in the low
+// mantissa bits: the sum's low byte is rint(product) mod 256, the int8 byte. An add, not an fma, so the product is
+// rounded first, as __float2int_rn(product) rounds it; and no conversion unit.
 FRY_DEVICE uint2 quantize8(const float (&v)[8], float step) {
-    const uint64_t step2 = pair2(step, step);
-    int q[8];
+    const uint64_t step2 = pair2(step, step), magic2 = pair2(12582912.0f, 12582912.0f);
+    uint32_t q[8];
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-        const float2 scaled = lanes(mul2(pair2(v[i], v[i + 1]), step2));
-        q[i] = __float2int_rn(scaled.x);
-        q[i + 1] = __float2int_rn(scaled.y);
+        const float2 shifted = lanes(add2(mul2(pair2(v[i], v[i + 1]), step2), magic2));
+        q[i] = __float_as_uint(shifted.x);
+        q[i + 1] = __float_as_uint(shifted.y);
     }
     uint32_t words[2];
 #pragma unroll
@@ -44,12 +66,35 @@ FRY_DEVICE uint2 quantize8(const float (&v)[8], float step) {
     return make_uint2(words[0], words[1]);
 }
 
+// Where norm_quant_row puts a row's int8 values: a plain row in global memory...
+struct RowOut {
+    int8_t* q;
+    FRY_DEVICE void put8(int col, uint2 bytes) const { *reinterpret_cast<uint2*>(q + col) = bytes; }
+};
+// ...or row r of a K-major int8 operand resident in shared memory as the MMA reads it: 128-byte K slices of 128 rows
+// (16 KB each) in the 128-byte swizzle, 16-byte unit u of row r at u ^ (r % 8).
+struct SwizzledRowOut {
+    uint8_t* tile;
+    int row;
+    FRY_DEVICE void put8(int col, uint2 bytes) const {
+        uint8_t* slice = tile + (col >> 7) * (128 * 128) + row * 128;
+        const int unit = (col & 127) >> 4;
+        *reinterpret_cast<uint2*>(slice + ((unit ^ (row & 7)) << 4) + (col & 15)) = bytes;
+    }
+};
+
 // norm_quant of one row of D columns (D <= 256 CHUNKS): x (and with MIX, original: the row first becomes
 // fp16(fma(rs, x, is * original)), stored to mixed) -> RMSNorm with gain in fp32 -> int8 by round-half-even into q,
 // absmax / 127 into *scale. Arithmetic order: per lane over its chunks, then the warp's tree.
-template <int CHUNKS, bool MIX>
-FRY_DEVICE void norm_quant_row(const uint4 (&raw)[CHUNKS], const uint4 (&raw_original)[MIX ? CHUNKS : 1], const uint4 (&raw_gain)[CHUNKS],
-                               uint64_t rs2, uint64_t is2, float eps, int D, int lane, uint16_t* mixed, int8_t* q, float* scale) {
+FRY_DEVICE void gain_chunk(const uint4& packed, float (&to)[8]) { unpack8(packed, to); }
+FRY_DEVICE void gain_chunk(const float (&values)[8], float (&to)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) to[i] = values[i];
+}
+
+template <int CHUNKS, bool MIX, typename Out = RowOut, typename GainChunk>
+FRY_DEVICE void norm_quant_row(const uint4 (&raw)[CHUNKS], const uint4 (&raw_original)[MIX ? CHUNKS : 1], const GainChunk (&gain)[CHUNKS],
+                               uint64_t rs2, uint64_t is2, float eps, int D, int lane, uint16_t* mixed, const Out& q, float* scale) {
     float v[CHUNKS][8];
     float squares = 0.0f;
 #pragma unroll
@@ -85,7 +130,7 @@ FRY_DEVICE void norm_quant_row(const uint4 (&raw)[CHUNKS], const uint4 (&raw_ori
         const int col = (c * 32 + lane) * 8;
         if (col < D) {
             float g[8];
-            unpack8(raw_gain[c], g);
+            gain_chunk(gain[c], g);
 #pragma unroll
             for (int i = 0; i < 8; i += 2) {
                 const float2 y = lanes(mul2(mul2(pair2(v[c][i], v[c][i + 1]), inverse2), pair2(g[i], g[i + 1])));
@@ -95,12 +140,12 @@ FRY_DEVICE void norm_quant_row(const uint4 (&raw)[CHUNKS], const uint4 (&raw_ori
             }
         }
     }
-    absmax = fmaxf(warp_max(absmax), 1e-20f);
+    absmax = fmaxf(warp_max_redux(absmax), 1e-20f);
     const float step_inverse = __fdiv_rn(127.0f, absmax);
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
-        if (col < D) *reinterpret_cast<uint2*>(q + col) = quantize8(v[c], step_inverse);
+        if (col < D) q.put8(col, quantize8(v[c], step_inverse));
     }
     if (lane == 0) *scale = __fdiv_rn(absmax, 127.0f);
 }
@@ -139,7 +184,7 @@ FRY_DEVICE void rotate_quant_row(const uint4 (&raw)[4], int width, int lane, int
     for (int part = 0; part < 4; ++part)
 #pragma unroll
         for (int i = 0; i < 8; ++i) absmax = fmaxf(absmax, fabsf(v[part][i]));
-    absmax = fmaxf(warp_max(absmax), 1e-20f);
+    absmax = fmaxf(warp_max_redux(absmax), 1e-20f);
     const float step_inverse = __fdiv_rn(127.0f, absmax);
 #pragma unroll
     for (int part = 0; part < 4; ++part) {

@@ -46,17 +46,13 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) norm_quant_kern
             if constexpr (MIX) to_original[c] = col < D ? *reinterpret_cast<const uint4*>(original + at) : make_uint4(0, 0, 0, 0);
         }
     };
-#pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-        const int col = (c * 32 + lane) * 8;
-        raw_gain[c] = col < D ? *reinterpret_cast<const uint4*>(gain + col) : make_uint4(0, 0, 0, 0);
-    }
+    load_row_chunks<CHUNKS>(gain, D, lane, raw_gain);  // packed: the unpacked gain would not fit 3 CTAs an SM
     load_row(row, raw, raw_original);
     for (; row < M; row += stride) {  // uniform across the warp
         uint4 next[CHUNKS], next_original[MIX ? CHUNKS : 1];
         if (row + stride < M) load_row(row + stride, next, next_original);
         const size_t base = static_cast<size_t>(row) * D;
-        norm_quant_row<CHUNKS, MIX>(raw, raw_original, raw_gain, rs2, is2, eps, D, lane, mixed + base, q + base, scale + row);
+        norm_quant_row<CHUNKS, MIX>(raw, raw_original, raw_gain, rs2, is2, eps, D, lane, mixed + base, RowOut{q + base}, scale + row);
 #pragma unroll
         for (int c = 0; c < CHUNKS; ++c) {
             raw[c] = next[c];

@@ -60,6 +60,31 @@ def _(x, x_scale, weight, weight_scale, bias, residual, gated, matmul, original=
     return x.new_empty(*x.shape[:-1], weight.shape[0] // 2 if gated else weight.shape[0], dtype=torch.float16)
 
 
+@torch.library.custom_op("fry::int8_linear_normed", mutates_args=())
+def int8_linear_normed(x: torch.Tensor, gain: torch.Tensor, eps: float, weight: torch.Tensor, weight_scale: torch.Tensor,
+                       bias: torch.Tensor | None, gated: bool) -> torch.Tensor:
+    """`chess::norm_quant` then `chess::int8_linear` (model/int8_blocks.py:191-193, :132-139) as one kernel, the pair
+    `Int8Block.forward` runs for ln1 -> projection and ln2 -> gate_up (model/int8_blocks.py:274-288); the same bits as
+    `int8_linear(*norm_quant(x, gain, eps), ...)`. x fp16 [..., 768]."""
+    _cuda("int8_linear_normed", x, gain, weight, weight_scale, bias)
+    _dtype("int8_linear_normed", x, torch.float16, "x")
+    _dtype("int8_linear_normed", weight, torch.int8, "weight")
+    rows, K = weight.shape
+    N = rows // 2 if gated else rows
+    x = x.contiguous()
+    M = x.numel() // K
+    out = torch.empty(*x.shape[:-1], N, device=x.device, dtype=torch.float16)
+    bias = bias.half().contiguous() if bias is not None else None
+    library().fry_int8_linear_normed(_ptr(x), _ptr(gain.half().contiguous()), eps, _ptr(weight.contiguous()),
+                                     _ptr(weight_scale.contiguous().float()), _ptr(bias), _ptr(out), M, N, K, int(gated), _stream(x))
+    return out
+
+
+@int8_linear_normed.register_fake
+def _(x, gain, eps, weight, weight_scale, bias, gated):
+    return x.new_empty(*x.shape[:-1], weight.shape[0] // 2 if gated else weight.shape[0], dtype=torch.float16)
+
+
 @torch.library.custom_op("fry::int8_matmul_i32", mutates_args=())
 def int8_matmul_i32(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """The int32 sums x . weight^T of the int8 tensor-core kernel (what int8_linear's epilogue starts from)."""

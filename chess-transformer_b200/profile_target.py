@@ -16,10 +16,12 @@ sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 # the GEMMs of a block at M = batch x 70: name -> (output columns N, depth K, kind), and how many of the 28 blocks run
 # each: the projection at dq 8/16/24, gate_up, down mixing the next block's input (the last block's adds its residual
-# only), and the attention-out fp16 linear
+# only), and the attention-out fp16 linear; then the GEMMs with the norm in their prologue (kinds "_normed"), which the
+# forward does not run (count 0), for profiling them beside the others
 GEMMS = {"projection864": (864, 768, "bias", 10), "projection1152": (1152, 768, "bias", 9), "projection1440": (1440, 768, "bias", 9),
          "gate_up": (992, 768, "gated", 28), "down": (768, 1024, "mixing", 27), "down_last": (768, 1024, "residual", 1),
-         "combine": (768, 768, "fp16", 28)}
+         "combine": (768, 768, "fp16", 28), "projection1152_normed": (1152, 768, "bias_normed", 0),
+         "gate_up_normed": (992, 768, "gated_normed", 0)}
 
 
 def gemm_runner(torch, ops, name: str, M: int):
@@ -34,7 +36,14 @@ def gemm_runner(torch, ops, name: str, M: int):
         from chess_transformer_b200 import library
         return lambda: library().fry_linear(x.data_ptr(), weight.data_ptr(), bias.data_ptr(), residual.data_ptr(), out.data_ptr(), M, N,
                                             K, 0, torch.cuda.current_stream().cuda_stream)
-    gated = kind == "gated"
+    gated = kind.startswith("gated")
+    if kind.endswith("_normed"):
+        x = (torch.randn(M, K, generator=generator) * 3).half().cuda()
+        gain = (torch.rand(K, generator=generator) + 0.5).half().cuda()
+        w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
+        ws = (torch.rand(len(w), generator=generator) / 100).cuda()
+        bias = None if gated else torch.randn(N, generator=generator).half().cuda()
+        return lambda: ops.int8_linear_normed(x, gain, 1e-5, w, ws, bias, gated)
     x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
     w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
     xs, ws = (torch.rand(M, generator=generator) / 100).cuda(), (torch.rand(len(w), generator=generator) / 100).cuda()

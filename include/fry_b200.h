@@ -48,6 +48,14 @@ int fry_int8_linear(const int8_t* x, const float* x_scale, const int8_t* weight,
                     const uint16_t* residual, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
                     uint16_t* out, int M, int N, int K, int gated, void* stream);
 
+/* `chess::norm_quant` feeding `chess::int8_linear` as one kernel: out = int8_linear(norm_quant(x, gain, eps)) with the
+ * bias (gated == 0; bias may be NULL) or the gated epilogue, the pair `Int8Block.forward` runs for ln1 -> projection and
+ * ln2 -> gate_up (model/int8_blocks.py:274-288; ops :191-193 and :132-139). The int8 rows and their scales are made in
+ * the GEMM's prologue and stay in shared memory; the bits equal those of fry_norm_quant then fry_int8_linear.
+ * x fp16 [M, K] and gain fp16 [K], 16-byte aligned; K must be 768 (the model width), N a multiple of 8. */
+int fry_int8_linear_normed(const uint16_t* x, const uint16_t* gain, float eps, const int8_t* weight, const float* weight_scale,
+                           const uint16_t* bias, uint16_t* out, int M, int N, int K, int gated, void* stream);
+
 /* The int32 sums x[M, K] . weight[N, K]^T of the same tensor-core kernel, for bit-exact checks. No reference
  * counterpart exposes them; they are the `acc` of model/int8_blocks.py:85-92. */
 int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int M, int N, int K, void* stream);

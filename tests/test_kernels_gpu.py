@@ -102,6 +102,39 @@ def test_int8_linear_is_the_oracle_on_fry_shapes(M, epilogue):
     assert steps.max() <= (1 if epilogue == "gated" else 0)
 
 
+# the fused norm: units of a row block's column tiles (1, 5 and 70 rows: one row block split over up to 23 CTAs; 4480: 35
+# blocks, 4 groups; 17920: 140 blocks, one CTA each; 19001: 149 blocks, a CTA takes two, the last one partial)
+@pytest.mark.parametrize("M", [1, 5, 70, 4480, 17920, 19001])
+@pytest.mark.parametrize("epilogue, N", [("bias", 864), ("bias", 1152), ("bias", 1440), ("gated", 992), ("gated", 1024)])
+def test_int8_linear_normed_is_norm_quant_then_int8_linear(M, epilogue, N):
+    g = torch.Generator().manual_seed(M + N)
+    K = 768
+    x = (torch.randn(M, K, generator=g) * 3).half().cuda()
+    gain = (torch.rand(K, generator=g) + 0.5).half().cuda()
+    gated = epilogue == "gated"
+    w = torch.randint(-127, 128, (2 * N if gated else N, K), generator=g, dtype=torch.int8).cuda()
+    ws = (torch.rand(len(w), generator=g) / 100).cuda()
+    bias = None if gated else torch.randn(N, generator=g).half().cuda()
+    found = ops.int8_linear_normed(x, gain, 1e-5, w, ws, bias, gated)
+    # the same bits as the two kernels it replaces
+    q, scale = ops.norm_quant(x, gain, 1e-5)
+    pair = ops.int8_linear(q, scale, w, ws, bias, None, gated, epilogue)
+    assert torch.equal(found.cpu(), pair.cpu())
+    # and the oracle's: its int8_linear on those int8 rows (the gate's sigmoid one fp16 step apart at most), its norm_quant
+    # within one int8 step (rsqrt)
+    expected = oi.int8_linear(q.cpu(), scale.cpu(), w.cpu(), ws.cpu(), bias=None if bias is None else bias.cpu(), gated=gated)
+    assert fp16_steps(found, expected).max() <= (1 if gated else 0)
+    oq, _ = oi.norm_quant(x.cpu(), gain.cpu())
+    assert (q.cpu().int() - oq.int()).abs().max() <= 1
+
+
+def test_int8_linear_normed_refuses_other_widths():
+    x = torch.zeros(70, 512, dtype=torch.float16, device="cuda")
+    with pytest.raises(Exception, match="K = 768"):
+        ops.int8_linear_normed(x, x[0], 1e-5, torch.zeros(64, 512, dtype=torch.int8, device="cuda"),
+                               torch.ones(64, device="cuda"), None, False)
+
+
 @pytest.mark.parametrize("M, N, K", [(70, 200, 128), (4480, 768, 768)])
 def test_fp16_linear_is_the_oracle(M, N, K):
     g = torch.Generator().manual_seed(N)
