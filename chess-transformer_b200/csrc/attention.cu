@@ -34,11 +34,10 @@ FRY_DEVICE void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-FRY_DEVICE uint32_t pack_half2(float lo, float hi) {
-    return static_cast<uint32_t>(f2h_bits(lo)) | (static_cast<uint32_t>(f2h_bits(hi)) << 16);
-}
-FRY_DEVICE float low_half(uint32_t pair) { return h2f_bits(static_cast<uint16_t>(pair & 0xffff)); }
-FRY_DEVICE float high_half(uint32_t pair) { return h2f_bits(static_cast<uint16_t>(pair >> 16)); }
+// fp16 <-> fp32 off the conversion unit where possible: widening by the mixed-precision add, narrowing two at a time
+FRY_DEVICE uint32_t pack_half2(float lo, float hi) { return pack_half2_rn(lo, hi); }
+FRY_DEVICE float low_half(uint32_t pair) { return h2f_exact(static_cast<uint16_t>(pair & 0xffff)); }
+FRY_DEVICE float high_half(uint32_t pair) { return h2f_exact(static_cast<uint16_t>(pair >> 16)); }
 FRY_DEVICE float quad_sum(float v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     return v + __shfl_xor_sync(0xffffffffu, v, 2);
@@ -46,10 +45,7 @@ FRY_DEVICE float quad_sum(float v) {
 FRY_DEVICE float lane0(uint64_t v) { return lanes(v).x; }
 FRY_DEVICE float lane1(uint64_t v) { return lanes(v).y; }
 // the fp16 pair (low, high) as two fp32 lanes
-FRY_DEVICE uint64_t widen2(uint32_t pair) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pair));
-    return pair2(f.x, f.y);
-}
+FRY_DEVICE uint64_t widen2(uint32_t pair) { return pair2(low_half(pair), high_half(pair)); }
 FRY_DEVICE uint32_t narrow2(uint64_t v) { return pack_half2(lane0(v), lane1(v)); }
 
 FRY_DEVICE float quad_max(float v) {
@@ -165,7 +161,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
                 const int i = part * 8 + 2 * w;
-                const float g0 = i < dq ? h2f_bits(k_gain[i]) : 0.0f, g1 = i + 1 < dq ? h2f_bits(k_gain[i + 1]) : 0.0f;
+                const float g0 = i < dq ? h2f_exact(k_gain[i]) : 0.0f, g1 = i + 1 < dq ? h2f_exact(k_gain[i + 1]) : 0.0f;
                 words[w] = key < kAttnTokens ? pack_half2(__fmul_rn(__fmul_rn(k[i], inverse), g0), __fmul_rn(__fmul_rn(k[i + 1], inverse), g1))
                                              : 0u;
             }
@@ -196,7 +192,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int col = ks * 16 + half * 8 + 2 * t + e;
-                qg[ks][half][e] = col < dq ? h2f_bits(q_gain[col]) : 0.0f;
+                qg[ks][half][e] = col < dq ? h2f_exact(q_gain[col]) : 0.0f;
             }
     uint32_t raw_q[KS][2][2];
     load_queries<KS>(raw_q, board, phase_begin * kSlab, width, head, dq, g, t);

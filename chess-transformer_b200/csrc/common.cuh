@@ -283,6 +283,18 @@ FRY_DEVICE float warp_max_redux(float v) {
     asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
     return m;
 }
+// fp16 -> fp32 on the FMA pipe rather than the conversion unit (a quarter of its rate or less): the mixed-precision add
+// (PTX add.f32.f16, sm_100) of -0.0, exact for every finite or infinite input (a NaN stays a NaN).
+FRY_DEVICE float h2f_exact(uint16_t bits) {
+    float value;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(value) : "h"(bits), "f"(-0.0f));
+    return value;
+}
+// Two fp32 values rounded to fp16 and packed (lo in the low half) by one conversion instruction.
+FRY_DEVICE uint32_t pack_half2_rn(float lo, float hi) {
+    const __half2 pair = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&pair);
+}
 FRY_DEVICE float h2f(__half h) { return __half2float(h); }
 FRY_DEVICE float h2f_bits(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
 FRY_DEVICE uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }

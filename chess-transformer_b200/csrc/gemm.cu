@@ -182,6 +182,8 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
             }
         }
+        // fp16 operands widen on the FMA pipe (h2f_exact); the conversion unit is left the int32 sums, the gate's 2^x and
+        // reciprocal, and the fp16 roundings, two at a time
         float values[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -195,24 +197,26 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
                 value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], h2f_bits(res[e]));
-                if constexpr (EPI == kEpiMix) {
-                    const float stream = __half2float(__float2half_rn(value));
-                    value = __fmaf_rn(stream, rs, __fmul_rn(h2f_bits(orig[e]), is));
-                }
+                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], h2f_exact(res[e]));
             } else {  // kEpiLinearF16: (acc + bias) + residual
                 value = __fadd_rn(__uint_as_float(acc[e]), second_v[e]);
-                if (p.residual) value = __fadd_rn(value, h2f_bits(res[e]));
+                if (p.residual) value = __fadd_rn(value, h2f_exact(res[e]));
             }
             values[e] = value;
+        }
+        if constexpr (EPI == kEpiMix) {
+            // the residual sum rounded to fp16 (a pair an instruction), then mixed with the original
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const uint32_t stream = pack_half2_rn(values[e], values[e + 1]);
+                values[e] = __fmaf_rn(h2f_exact(static_cast<uint16_t>(stream & 0xffff)), rs, __fmul_rn(h2f_exact(orig[e]), is));
+                values[e + 1] = __fmaf_rn(h2f_exact(static_cast<uint16_t>(stream >> 16)), rs, __fmul_rn(h2f_exact(orig[e + 1]), is));
+            }
         }
         // two fp16 roundings an instruction, over the staged residual
         uint32_t result[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const __half2 pair = __floats2half2_rn(values[2 * i], values[2 * i + 1]);
-            result[i] = *reinterpret_cast<const uint32_t*>(&pair);
-        }
+        for (int i = 0; i < 8; ++i) result[i] = pack_half2_rn(values[2 * i], values[2 * i + 1]);
         *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
         *staged.at(1) = make_uint4(result[4], result[5], result[6], result[7]);
     }

@@ -9,14 +9,6 @@
 
 namespace fry {
 
-// fp16 -> fp32 on the FMA pipe rather than the conversion unit, which bounds a row's throughput otherwise: the mixed
-// precision add (PTX add.f32.f16, sm_100) of -0.0: exact for every finite or infinite input (a NaN stays a NaN).
-FRY_DEVICE float h2f_exact(uint16_t bits) {
-    float value;
-    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(value) : "h"(bits), "f"(-0.0f));
-    return value;
-}
-
 FRY_DEVICE void unpack8(const uint4& u, float (&v)[8]) {
     const uint16_t* h = reinterpret_cast<const uint16_t*>(&u);
 #pragma unroll
@@ -109,11 +101,9 @@ FRY_DEVICE void norm_quant_row(const uint4 (&raw)[CHUNKS], const uint4 (&raw_ori
 #pragma unroll
                 for (int i = 0; i < 8; i += 2) {
                     const float2 m = lanes(fma2(rs2, pair2(v[c][i], v[c][i + 1]), mul2(is2, pair2(o[i], o[i + 1]))));
-                    const __half2 h = __floats2half2_rn(m.x, m.y);
-                    packed[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
-                    const float2 back = __half22float2(h);
-                    v[c][i] = back.x;
-                    v[c][i + 1] = back.y;
+                    packed[i / 2] = pack_half2_rn(m.x, m.y);
+                    v[c][i] = h2f_exact(static_cast<uint16_t>(packed[i / 2] & 0xffff));
+                    v[c][i + 1] = h2f_exact(static_cast<uint16_t>(packed[i / 2] >> 16));
                 }
                 *reinterpret_cast<uint4*>(mixed + col) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             }
