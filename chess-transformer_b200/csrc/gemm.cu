@@ -182,36 +182,42 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
             }
         }
-        // fp16 operands widen on the FMA pipe (h2f_exact); the conversion unit is left the int32 sums, the gate's 2^x and
-        // reciprocal, and the fp16 roundings, two at a time
+        // the arithmetic two columns at a time in paired fp32 (f32x2: each lane rounds as the scalar instruction does); fp16
+        // operands widen on the FMA pipe (h2f_exact)
+        const uint64_t xs2 = pair2(xs, xs);
         float values[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            float value;
+        for (int e = 0; e < 16; e += 2) {
+            const uint64_t scale2 = pair2(scale_v[e], scale_v[e + 1]), second2 = pair2(second_v[e], second_v[e + 1]);
+            const uint64_t acc2 = pair2(static_cast<float>(static_cast<int32_t>(acc[e])), static_cast<float>(static_cast<int32_t>(acc[e + 1])));
+            uint64_t value2;
             if constexpr (EPI == kEpiBias) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], second_v[e]);
+                value2 = fma2(mul2(acc2, xs2), scale2, second2);
             } else if constexpr (EPI == kEpiGated) {
-                const float gate = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e]);
-                const float u = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(up[e])), xs), second_v[e]);
+                const uint64_t gate2 = mul2(mul2(acc2, xs2), scale2);
+                const uint64_t up2 = mul2(mul2(pair2(static_cast<float>(static_cast<int32_t>(up[e])), static_cast<float>(static_cast<int32_t>(up[e + 1]))), xs2),
+                                          second2);
                 // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
-                const float sigmoid = div_full(1.0f, __fadd_rn(ex2_approx(__fmul_rn(gate, -1.4426950408889634f)), 1.0f));
-                value = __fmul_rn(__fmul_rn(gate, sigmoid), u);
+                const float2 power = lanes(mul2(gate2, pair2(-1.4426950408889634f, -1.4426950408889634f)));
+                const float2 denominator = lanes(add2(pair2(ex2_approx(power.x), ex2_approx(power.y)), pair2(1.0f, 1.0f)));
+                const uint64_t sigmoid2 = pair2(div_full(1.0f, denominator.x), div_full(1.0f, denominator.y));
+                value2 = mul2(mul2(gate2, sigmoid2), up2);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
-                value = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc[e])), xs), scale_v[e], h2f_exact(res[e]));
+                value2 = fma2(mul2(acc2, xs2), scale2, pair2(h2f_exact(res[e]), h2f_exact(res[e + 1])));
+                if constexpr (EPI == kEpiMix) {
+                    // the residual sum rounded to fp16, then mixed with the original
+                    const float2 sum = lanes(value2);
+                    const uint32_t stream = pack_half2_rn(sum.x, sum.y);
+                    const uint64_t stream2 = pair2(h2f_exact(static_cast<uint16_t>(stream & 0xffff)), h2f_exact(static_cast<uint16_t>(stream >> 16)));
+                    value2 = fma2(stream2, pair2(rs, rs), mul2(pair2(h2f_exact(orig[e]), h2f_exact(orig[e + 1])), pair2(is, is)));
+                }
             } else {  // kEpiLinearF16: (acc + bias) + residual
-                value = __fadd_rn(__uint_as_float(acc[e]), second_v[e]);
-                if (p.residual) value = __fadd_rn(value, h2f_exact(res[e]));
+                value2 = add2(pair2(__uint_as_float(acc[e]), __uint_as_float(acc[e + 1])), second2);
+                if (p.residual) value2 = add2(value2, pair2(h2f_exact(res[e]), h2f_exact(res[e + 1])));
             }
-            values[e] = value;
-        }
-        if constexpr (EPI == kEpiMix) {
-            // the residual sum rounded to fp16 (a pair an instruction), then mixed with the original
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                const uint32_t stream = pack_half2_rn(values[e], values[e + 1]);
-                values[e] = __fmaf_rn(h2f_exact(static_cast<uint16_t>(stream & 0xffff)), rs, __fmul_rn(h2f_exact(orig[e]), is));
-                values[e + 1] = __fmaf_rn(h2f_exact(static_cast<uint16_t>(stream >> 16)), rs, __fmul_rn(h2f_exact(orig[e + 1]), is));
-            }
+            const float2 value = lanes(value2);
+            values[e] = value.x;
+            values[e + 1] = value.y;
         }
         // two fp16 roundings an instruction, over the staged residual
         uint32_t result[8];
