@@ -79,7 +79,10 @@ struct GemmShape {
     static constexpr int kSlots = 2;
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
-    static constexpr int kColumnBytes = 2 * 2 * BN * 4;
+    // (the mix and residual epilogues use the scales alone, the fp16 linears the bias alone: one array)
+    static constexpr int kColumnArrays = (EPI == kEpiBias || EPI == kEpiGated) ? 2 : 1;
+    static constexpr int kSecond = kColumnArrays == 2 ? BN : 0;  // where the second operand (up's scales, the bias) starts
+    static constexpr int kColumnBytes = 2 * kColumnArrays * BN * 4;
     static constexpr int kStagesFit = (kSmemBudget - kResidentBytes - kRowScaleBytes - kIoBytes - kColumnBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
@@ -93,9 +96,10 @@ struct GemmShape {
 
 FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads + 32) : "memory"); }
 
-// The tile's column operands into shared memory (all epilogue threads together): columns[0] the weight scales,
-// columns[1] up's scales (gated) or the bias as floats, zero past N.
-template <int EPI, int BN>
+// The tile's column operands into shared memory (all epilogue threads together): columns[0, BN) the weight scales,
+// columns[SECOND, SECOND + BN) up's scales (gated) or the bias as floats, zero past N; the linears have no scales and
+// the mix and residual epilogues no second operand, so theirs share the one array (SECOND = 0).
+template <int EPI, int BN, int SECOND>
 FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, int tid) {
     for (int i = tid; i < BN; i += kEpilogueThreads) {
         const int n = n0 + i;
@@ -105,8 +109,8 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
         if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
         if constexpr (EPI == kEpiBias || EPI == kEpiLinearF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
         if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
-        columns[i] = scale;
-        columns[BN + i] = second;
+        if constexpr (EPI <= kEpiMix) columns[i] = scale;
+        if constexpr (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearF16 || EPI == kEpiLinearF32) columns[SECOND + i] = second;
     }
 }
 
@@ -473,7 +477,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
             if constexpr (EPI <= kEpiMix && NKS == 0) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
-            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN>(args, column_buffers + buffer * 2 * BN, n0, N, threadIdx.x);
+            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN, S::kSecond>(args, column_buffers + buffer * S::kColumnArrays * BN, n0, N, threadIdx.x);
         };
         fetch_operands(first_tile, 0);
         epilogue_sync();
@@ -500,7 +504,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             const float xs = NKS > 0 ? xs_unit : xs_next;
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
-            const float* columns = column_buffers + buffer * 2 * BN;
+            const float* columns = column_buffers + buffer * S::kColumnArrays * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
             for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
                 // sub-tile j stages into slot j % 2, which the stores of sub-tile j - 2 had read before the barrier that ended
@@ -521,7 +525,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const StagedChunk original{staged_sub + (S::kBoxes + box) * kBoxBytes + row_in_tile * 128, unit, swizzle};
                         const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
                         if (S::kStaged || m < M)
-                            epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + BN + c, staged, original,
+                            epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + S::kSecond + c, staged, original,
                                             static_cast<size_t>(m) * N + n0 + c, valid);
                     }
                 }
@@ -647,7 +651,8 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 }  // namespace
 
 // Tile widths: one N = 256 MMA a K step where N allows (gate_up's 128 columns hold 256 accumulators, its gate and its
-// up), staged in 128-column sub-tiles, mixing's in 64-column ones (two row operands a slot). When that leaves fewer tiles
+// up), staged in 128-column sub-tiles. Mixing stages 64-column sub-tiles (two row operands a slot) and, in place of 256,
+// takes 192-column tiles, whose 40 KB stages fit four deep beside its 64 KB of slots (three at 256). When that leaves fewer tiles
 // than SMs (small batches), narrower tiles (128, then 64 columns: more CTAs streaming the weights, deeper pipelines)
 // take their place. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
@@ -688,7 +693,7 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 128) return launch<0, 128, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
             case kEpiMix:
-                if (width == 256) return launch<0, 256, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 192, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
