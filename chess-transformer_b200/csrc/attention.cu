@@ -360,14 +360,15 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     }
     const int kv_per_cta = per_cta / group;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dq)));  // 1 / math.sqrt(dq), rounded once to fp32
-    // small batches: the phases shared among up to 5 CTAs (each stages the keys and values again), as many as still fit
-    // the SMs at once (3 CTAs an SM), so more SMs share a board
+    // small batches: the phases shared among up to 5 CTAs (each stages the keys and values again), as many as keep the
+    // CTAs within 1.5 waves of the SMs (3 CTAs an SM), so more SMs share a board. (One wave was the first bound; 1.5
+    // measured 3-5% faster forwards at 32 to 96 boards and the same from 128 boards up.)
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
     // 1, 2, 3 or 5 groups: each has a phase (4 groups of 2 phases would leave the last without one)
-    const int ctas = heads / per_cta * B, fit = 3 * multiprocessors / ctas;
+    const int ctas = heads / per_cta * B, fit = 9 * multiprocessors / (2 * ctas);
     const dim3 grid(heads / per_cta, B, fit >= 5 ? 5 : fit >= 3 ? 3 : fit >= 2 ? 2 : 1);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
