@@ -254,6 +254,7 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
         projection.w_scale = b.projection_scale;
         projection.bias = b.projection_bias;
         projection.out = projected;
+        projection.b_constant = true;
         status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
         if (status != cudaSuccess) return check(status, where + " projection", detail);
         status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
@@ -263,6 +264,7 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
         combine.bias = b.combine_heads_bias;
         combine.residual = x;
         combine.out = x;
+        combine.b_constant = true;
         status = fry::gemm(1, fry::kEpiLinearF16, attended, b.combine_heads, combine, M, D, D, s, &detail);
         if (status != cudaSuccess) return check(status, where + " combine_heads", detail);
         status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
@@ -271,6 +273,7 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
         gate_up.x_scale = scale;
         gate_up.w_scale = b.gate_up_scale;
         gate_up.out = hidden;
+        gate_up.b_constant = true;
         status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
         if (status != cudaSuccess) return check(status, where + " gate_up", detail);
         status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
@@ -280,6 +283,7 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
         down.w_scale = b.down_scale;
         down.residual = x;
         down.out = x;
+        down.b_constant = true;
         const bool mixes = i + 1 < n->layers;
         if (mixes) {
             down.original = original;

@@ -71,8 +71,8 @@ FRY_DEVICE void make_bias_slab(uint16_t* bias, const uint16_t* board, const uint
         const int i0 = slab * kSlab + 2 * pair, i1 = i0 + 1;
         uint32_t a0 = 0, a3 = 0;
         if (g < heads_here) {
-            a0 = *reinterpret_cast<const uint32_t*>(board + i0 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t);
-            a3 = *reinterpret_cast<const uint32_t*>(board + i1 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t);
+            a0 = __ldcs(reinterpret_cast<const uint32_t*>(board + i0 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t));
+            a3 = __ldcs(reinterpret_cast<const uint32_t*>(board + i1 * width + c_offset + (first_head + g) * kAttnTemplates + 2 * t));
         }
         const uint16_t* t0 = paired + (i0 * kAttnSquares + g) * kAttnTemplates + 2 * t;
         const uint16_t* t1 = paired + (i1 * kAttnSquares + g) * kAttnTemplates + 2 * t;
@@ -100,7 +100,7 @@ FRY_DEVICE void load_queries(uint32_t (&raw)[KS][2][2], const uint16_t* board, i
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int row = first + g + 8 * r, col = ks * 16 + half * 8 + 2 * t;
-                raw[ks][r][half] = (row < kAttnTokens && col < dq) ? *reinterpret_cast<const uint32_t*>(board + row * width + head * dq + col) : 0u;
+                raw[ks][r][half] = (row < kAttnTokens && col < dq) ? __ldcs(reinterpret_cast<const uint32_t*>(board + row * width + head * dq + col)) : 0u;
             }
 }
 
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
 #pragma unroll
             for (int part = 0; part < DQP / 8; ++part)
                 if (part * 8 < dq) {
-                    const uint4 raw = *reinterpret_cast<const uint4*>(from + part * 8);
+                    const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(from + part * 8));
                     const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                     for (int w = 0; w < 4; ++w) {
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
     for (int item = tid; item < kv_here * kAttnKeys * (kAttnDv / 8); item += blockDim.x) {
         const int kv = item / (kAttnKeys * 4), rest = item % (kAttnKeys * 4), key = rest / 4, part = rest % 4;
         uint4 raw = make_uint4(0, 0, 0, 0);
-        if (key < kAttnTokens) raw = *reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8);
+        if (key < kAttnTokens) raw = __ldcs(reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8));
         *reinterpret_cast<uint4*>(values + (kv * kAttnKeys + key) * kValueRow + part * 8) = raw;
     }
     // this CTA's phases: all five, or with a phase split (blockIdx.z, small batches), a share of them

@@ -35,6 +35,9 @@ struct GemmArgs {
     const uint16_t* norm_x = nullptr;        // fp16 [M, K]
     const uint16_t* norm_gain = nullptr;     // fp16 [K]
     float norm_eps = 0.0f;
+    // B is a weight that no kernel launched before this one writes: its first stages load before the wait for the
+    // earlier kernels (programmatic dependent launch), overlapping their tail
+    bool b_constant = false;
 };
 
 // kind 0: int8 A [M, K], B [N, K] (gated: [2N, K]); kind 1: fp16 A [M, K], B [N, K].

@@ -26,13 +26,14 @@ FRY_DEVICE void load_gain(const uint16_t* gain, int width, int lane, float (&to)
     }
 }
 
-// The row's fp16 chunks of this lane, zero past `width` columns.
-template <int CHUNKS>
+// The row's fp16 chunks of this lane, zero past `width` columns; STREAM: read once, so loaded evict-first (ld.global.cs).
+template <int CHUNKS, bool STREAM = false>
 FRY_DEVICE void load_row_chunks(const uint16_t* row, int width, int lane, uint4 (&to)[CHUNKS]) {
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
         const int col = (c * 32 + lane) * 8;
-        to[c] = col < width ? *reinterpret_cast<const uint4*>(row + col) : make_uint4(0, 0, 0, 0);
+        const uint4* at = reinterpret_cast<const uint4*>(row + col);
+        to[c] = col < width ? (STREAM ? __ldcs(at) : *at) : make_uint4(0, 0, 0, 0);
     }
 }
 

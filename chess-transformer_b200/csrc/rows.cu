@@ -105,10 +105,10 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) rotate_quant_ke
     int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     if (row >= M) return;
     uint4 raw[4];
-    load_row_chunks<4>(h + static_cast<size_t>(row) * hidden, hidden, lane, raw);
+    load_row_chunks<4, true>(h + static_cast<size_t>(row) * hidden, hidden, lane, raw);
     for (; row < M; row += stride) {  // uniform across the warp
         uint4 next[4];
-        if (row + stride < M) load_row_chunks<4>(h + static_cast<size_t>(row + stride) * hidden, hidden, lane, next);
+        if (row + stride < M) load_row_chunks<4, true>(h + static_cast<size_t>(row + stride) * hidden, hidden, lane, next);
         rotate_quant_row(raw, width, lane, q + static_cast<size_t>(row) * width, scale + row);
 #pragma unroll
         for (int c = 0; c < 4; ++c) raw[c] = next[c];
