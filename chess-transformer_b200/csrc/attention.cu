@@ -105,9 +105,10 @@ FRY_DEVICE void load_queries(uint32_t (&raw)[KS][2][2], const uint16_t* board, i
 }
 
 // DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values [kv][80][40], one bias slab (at most
-// 70 KB, so three CTAs share an SM).
+// 70 KB). Two CTAs an SM, with up to 128 registers a thread: three (80 registers, some spilled) measured the same at 256
+// boards and 3-6% slower at 8, 16 and 192.
 template <int DQP>
-__global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 3)
+__global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     attention_kernel(const uint16_t* __restrict__ projected, const uint16_t* __restrict__ paired, const uint16_t* __restrict__ q_gain,
                      const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out, int heads, int kv_heads, int dq, float eps, float scale) {
     grid_dependency_start();
@@ -361,8 +362,8 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     const int kv_per_cta = per_cta / group;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dq)));  // 1 / math.sqrt(dq), rounded once to fp32
     // small batches: the phases shared among up to 5 CTAs (each stages the keys and values again), as many as keep the
-    // CTAs within 1.5 waves of the SMs (3 CTAs an SM), so more SMs share a board. (One wave was the first bound; 1.5
-    // measured 3-5% faster forwards at 32 to 96 boards and the same from 128 boards up.)
+    // CTAs within 4.5 an SM, so more SMs share a board (measured: 3 an SM was 3-5% slower at 32 to 96 boards, 6 an SM
+    // slower at 96 and 128)
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
