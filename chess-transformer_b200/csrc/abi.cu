@@ -172,6 +172,26 @@ int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, cons
                  "fry_linear", detail);
 }
 
+int fry_linear_norm_quant(const uint16_t* x, const uint16_t* weight, const uint16_t* bias, const uint16_t* residual, uint16_t* out,
+                          const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int N, int K, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 256 != 0 || N > 1024 || K % 8 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_linear_norm_quant takes N a multiple of 256 up to 1024 and K a multiple of 8, got N " +
+                                         std::to_string(N) + ", K " + std::to_string(K));
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || !aligned16(gain) || !aligned16(q) || !scale || (residual && !aligned16(residual)))
+        return fail(FRY_ERROR_SHAPE, "fry_linear_norm_quant needs 16-byte aligned tensors and a scale output");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.bias = bias;
+    args.residual = residual;
+    args.out = out;
+    args.norm_gain = gain;
+    args.norm_eps = eps;
+    args.norm_q = q;
+    args.norm_scale = scale;
+    std::string detail;
+    return check(fry::gemm(1, fry::kEpiLinearNorm, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_linear_norm_quant", detail);
+}
+
 int fry_board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table, uint16_t* out,
                         int B, int D, void* stream) {
     if (B < 0 || D <= 0 || D % 8 != 0) return fail(FRY_ERROR_SHAPE, "fry_board_embedding takes D a multiple of 8");
@@ -236,8 +256,10 @@ int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, 
     const size_t heads_bytes = fry::heads_workspace_bytes(B, D);
     void* heads_workspace = take(heads_bytes);
 
-    // ln1 and ln2 run as their own kernels: the GEMMs with the norm in their prologue (fry_int8_linear_normed) measured
-    // no faster at 256 boards and slower at small batches, where each CTA of a row block repeats the block's norm
+    // ln1 and ln2 run as their own kernels. Fused into a neighbouring GEMM they measured slower: in the int8 GEMM's prologue
+    // (fry_int8_linear_normed) no faster at 256 boards and slower at small batches, where each CTA of a row block repeats
+    // the block's norm; in the attention-out GEMM's epilogue (fry_linear_norm_quant) slower at every batch, its clusters
+    // of 3 CTAs taking up to 4 row blocks where single CTAs take 3 tiles, and its cluster exchange adding to each tile
     std::string detail;
     cudaError_t status = fry::board_embedding(boards, n->embed, n->position, n->table, original, B, D, s);
     if (status != cudaSuccess) return check(status, "fry_forward: embedding");

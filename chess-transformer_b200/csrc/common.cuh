@@ -82,6 +82,52 @@ FRY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
     return false;
 }
 
+// ---- thread-block clusters: distributed shared memory and remote mbarrier arrivals ----
+FRY_DEVICE uint32_t cluster_rank() {
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    return rank;
+}
+// The address of `p` (this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+FRY_DEVICE uint32_t peer_smem(const void* p, uint32_t rank) {
+    uint32_t address;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(address) : "r"(smem_addr(p)), "r"(rank));
+    return address;
+}
+FRY_DEVICE void st_peer_f32x2(uint32_t address, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(address), "f"(a), "f"(b) : "memory");
+}
+// An arrival on a cluster CTA's mbarrier, releasing this thread's earlier writes (its st.shared::cluster among them).
+FRY_DEVICE void mbar_arrive_peer(uint32_t address) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(address) : "memory");
+}
+FRY_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// mbar_wait for a barrier that other CTAs of the cluster arrive on (acquiring their writes), bounded the same way.
+FRY_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int where) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) break;
+    }
+    record_error(kWaitTimeout, where);
+    return false;
+}
+// Every thread of every CTA of the cluster (all threads reach it: it does not wait for ever only if they do).
+FRY_DEVICE void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // 2-D tiled TMA load of box {x, y} (x the contiguous coordinate) into shared memory, completing on bar.
 FRY_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(
@@ -225,6 +271,44 @@ inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 b
     config.attrs = attribute;
     config.numAttrs = 1;
     return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
+// launch_dependent in thread-block clusters of `cluster` CTAs along x (grid.x a multiple of it).
+template <typename... Params, typename... Args>
+inline cudaError_t launch_dependent_cluster(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, int cluster, cudaStream_t stream,
+                                            Args... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[2];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    attribute[1].id = cudaLaunchAttributeClusterDimension;
+    attribute[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attribute[1].val.clusterDim.y = 1;
+    attribute[1].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 2;
+    return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
+// How many clusters of `cluster` CTAs of the kernel (with this block and shared memory) the device holds at once.
+template <typename... Params>
+inline cudaError_t max_active_clusters(void (*kernel)(Params...), dim3 block, size_t smem, int cluster, int* count) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(cluster);
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(count, reinterpret_cast<const void*>(kernel), &config);
 }
 
 // ---- small numeric helpers -----------------------------------------------------------------------------

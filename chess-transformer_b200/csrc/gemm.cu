@@ -51,6 +51,10 @@ constexpr int kBoxBytes = kBlockM * kBoxCols * 2;  // a staged fp16 box: 128 row
 constexpr int kBarrierBytes = 256;
 constexpr int kSmemBudget = 227 * 1024 - kBarrierBytes;
 constexpr int kNormedK = 768, kNormedSlices = kNormedK / kTileKBytes;  // the one width a normed A is built for
+constexpr int kMaxCluster = 4;  // kEpiLinearNorm: CTAs (column tiles) of a row block, one cluster
+constexpr int kNormBarrier = 2;  // named barrier of the 16 epilogue warps alone
+// fp16 linear epilogues (the bias and the residual optional)
+__host__ __device__ constexpr bool linear16(int epi) { return epi == kEpiLinearF16 || epi == kEpiLinearNorm; }
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
@@ -68,8 +72,11 @@ struct GemmShape {
     // fp16 outputs are staged for TMA stores; int32 and fp32 outputs are stored by their threads
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
     // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
-    static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || EPI == kEpiLinearF16) ? 1 : 0;
+    static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || linear16(EPI)) ? 1 : 0;
+    // chunks of 16 columns a thread takes in a sub-tile (the 4 warps of a TMEM lane quarter share a sub-tile's chunks)
+    static constexpr int kChunksPerSub = SUB / (kChunkCols * kChunkParts) > 0 ? SUB / (kChunkCols * kChunkParts) : 1;
     static constexpr int kSubs = BN / SUB;       // sub-tiles a tile
+    static constexpr int kSub = SUB;
     static constexpr int kBoxes = SUB / kBoxCols;  // staged boxes a sub-tile (per row tensor)
     static_assert(!kStaged || (SUB % kBoxCols == 0 && BN % SUB == 0), "a staged sub-tile is whole 64-column boxes");
     static_assert(kStaged || SUB == BN, "unstaged epilogues take the tile whole");
@@ -80,16 +87,21 @@ struct GemmShape {
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
     // (the mix and residual epilogues use the scales alone, the fp16 linears the bias alone: one array)
-    static constexpr int kColumnArrays = (EPI == kEpiBias || EPI == kEpiGated) ? 2 : 1;
+    static constexpr int kColumnArrays = (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearNorm) ? 2 : 1;
+    // kEpiLinearNorm: the cluster's exchange of row partials [2 tiles][kMaxCluster ranks][128 rows][2] and the epilogue
+    // warps' own [2][4 parts][128 rows], floats
+    static constexpr int kNormBytes = EPI == kEpiLinearNorm ? (2 * kMaxCluster * kBlockM * 2 + 2 * 4 * kBlockM) * 4 : 0;
+    static_assert(EPI != kEpiLinearNorm || (KIND == 1 && SUB == 128), "the norm epilogue keeps 4 chunks a thread (fp16 linear, 128-column sub-tiles)");
     static constexpr int kSecond = kColumnArrays == 2 ? BN : 0;  // where the second operand (up's scales, the bias) starts
     static constexpr int kColumnBytes = 2 * kColumnArrays * BN * 4;
-    static constexpr int kStagesFit = (kSmemBudget - kResidentBytes - kRowScaleBytes - kIoBytes - kColumnBytes) / kStageBytes;
+    static constexpr int kStagesFit = (kSmemBudget - kResidentBytes - kRowScaleBytes - kIoBytes - kColumnBytes - kNormBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
     static_assert(kStages >= 2, "at least two pipeline stages");
     static constexpr int kAccCols = BN * (GATED ? 2 : 1);  // one accumulator; two are allocated
     static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
     static_assert(2 * kAccCols <= 512, "two accumulators fit TMEM's 512 columns");
-    static constexpr int kSmemBytes = kResidentBytes + kIoBytes + kStages * kStageBytes + kColumnBytes + kRowScaleBytes + kBarrierBytes;
+    static constexpr int kSmemBytes =
+        kResidentBytes + kIoBytes + kStages * kStageBytes + kColumnBytes + kRowScaleBytes + kNormBytes + kBarrierBytes;
     static_assert(kAccCols % 16 == 0 && kAccCols >= 16 && kAccCols <= 256, "an M=128 MMA takes N in steps of 16 up to 256");
     static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzle atoms");
 };
@@ -107,10 +119,11 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
         float scale = 0.0f, second = 0.0f;
         if constexpr (EPI <= kEpiMix) scale = ok ? p.w_scale[n] : 0.0f;
         if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
-        if constexpr (EPI == kEpiBias || EPI == kEpiLinearF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
+        if constexpr (EPI == kEpiBias || linear16(EPI)) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
         if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
         if constexpr (EPI <= kEpiMix) columns[i] = scale;
-        if constexpr (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearF16 || EPI == kEpiLinearF32) columns[SECOND + i] = second;
+        if constexpr (EPI == kEpiLinearNorm) columns[i] = (ok && p.norm_gain) ? h2f_bits(p.norm_gain[n]) : 0.0f;
+        if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32) columns[SECOND + i] = second;
     }
 }
 
@@ -141,11 +154,11 @@ struct StagedChunk {
 // Applies the epilogue to one row's 16 consecutive columns. acc (and up, gated) hold the raw TMEM words, xs the row's
 // activation scale, rs and is the next block's input-mix scales, scale and second the chunk's column operands in shared
 // memory. Staged epilogues read the row's residual (and original) from its staged chunk and write the fp16 results over
-// it; int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
+// it (and into result, as fp16 pairs); int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
 template <int EPI>
 FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, const uint32_t (&acc)[16], const uint32_t (&up)[16],
                            const float* scale, const float* second, const StagedChunk& staged, const StagedChunk& original, size_t row,
-                           int valid) {
+                           int valid, uint32_t (&result)[8]) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -165,10 +178,10 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
             }
         return;
     } else {
-        constexpr bool kResidual = EPI == kEpiResidual || EPI == kEpiMix || EPI == kEpiLinearF16;
+        constexpr bool kResidual = EPI == kEpiResidual || EPI == kEpiMix || linear16(EPI);
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if constexpr (kResidual) {
-            if (EPI != kEpiLinearF16 || p.residual != nullptr) residual_words[0] = *staged.at(0), residual_words[1] = *staged.at(1);
+            if (!linear16(EPI) || p.residual != nullptr) residual_words[0] = *staged.at(0), residual_words[1] = *staged.at(1);
         }
         if constexpr (EPI == kEpiMix) original_words[0] = *original.at(0), original_words[1] = *original.at(1);
         const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
@@ -177,11 +190,11 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
         float scale_v[16], second_v[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if constexpr (EPI != kEpiLinearF16) {
+            if constexpr (EPI <= kEpiMix) {
                 const float4 a = reinterpret_cast<const float4*>(scale)[q];
                 scale_v[4 * q] = a.x, scale_v[4 * q + 1] = a.y, scale_v[4 * q + 2] = a.z, scale_v[4 * q + 3] = a.w;
             }
-            if constexpr (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearF16) {
+            if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI)) {
                 const float4 b = reinterpret_cast<const float4*>(second)[q];
                 second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
             }
@@ -224,7 +237,6 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
             values[e + 1] = value.y;
         }
         // two fp16 roundings an instruction, over the staged residual
-        uint32_t result[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) result[i] = pack_half2_rn(values[2 * i], values[2 * i + 1]);
         *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
@@ -271,6 +283,76 @@ FRY_DEVICE void norm_rows_into_a(const GemmArgs& p, uint8_t* resident, float* ro
     }
 }
 
+FRY_DEVICE void norm_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kNormBarrier), "n"(kEpilogueThreads) : "memory"); }
+
+// kEpiLinearNorm, after a tile's epilogue: norm_quant of the tile's 128 rows, whose 768 (or N) columns lie in the N / BN
+// CTAs of this cluster, one column tile each. Each thread holds its row's fp16 outputs of its chunks (kept) and their
+// partial sum of squares and largest |x * gain|. The 4 threads of a row add theirs in shared memory; each rank's row
+// partials go to every rank (distributed shared memory, an arrival on each rank's xready); each thread then adds the
+// ranks' partials in rank order, and quantises its kept values: inverse = 1 / sqrt(sum / N + eps), absmax = inverse *
+// the largest |x * gain| (the largest |(x * inverse) * gain| to within fp32 rounding), q = rint((x * inverse) * gain *
+// 127 / absmax), the row's scale absmax / 127 (written by rank 0). A thread whose earlier wait timed out still takes every
+// barrier and arrival, so no rank waits on it for ever.
+template <typename S, int KEPT>
+FRY_DEVICE void norm_rows_of_tile(const GemmArgs& p, float* norm_smem, uint64_t* xready, const float* columns, const uint32_t (&kept)[KEPT][8],
+                                  float squares, float largest, int local, int m, int n0, int M, int N, int ranks, int row, int part,
+                                  int lane, bool& alive) {
+    const int tb = local & 1;  // exchange buffer and barrier of this tile (tiles alternate)
+    float* exchange = norm_smem;                              // [2][kMaxCluster][128][2]
+    float* parts = norm_smem + 2 * kMaxCluster * kBlockM * 2;  // [2][4][128]
+    parts[part * kBlockM + row] = squares;
+    parts[(kChunkParts + part) * kBlockM + row] = largest;
+    norm_sync();
+    const uint32_t rank = cluster_rank();
+    if (part == 0) {  // warps 0-3: a thread a row
+        float sum = parts[row], top = parts[kChunkParts * kBlockM + row];
+#pragma unroll
+        for (int q = 1; q < kChunkParts; ++q) {
+            sum = __fadd_rn(sum, parts[q * kBlockM + row]);
+            top = fmaxf(top, parts[(kChunkParts + q) * kBlockM + row]);
+        }
+        float* mine = exchange + ((tb * kMaxCluster + rank) * kBlockM + row) * 2;
+        for (int peer = 0; peer < ranks; ++peer) st_peer_f32x2(peer_smem(mine, peer), sum, top);
+        __syncwarp();
+        if (lane == 0)
+            for (int peer = 0; peer < ranks; ++peer) mbar_arrive_peer(peer_smem(&xready[tb], peer));
+    }
+    if (!mbar_wait_cluster(&xready[tb], (local >> 1) & 1, 17)) alive = false;
+    if (!alive) return;
+    float sum = 0.0f, top = 0.0f;
+    for (int r = 0; r < ranks; ++r) {
+        const float* entry = exchange + ((tb * kMaxCluster + r) * kBlockM + row) * 2;
+        sum = r == 0 ? entry[0] : __fadd_rn(sum, entry[0]);
+        top = fmaxf(top, entry[1]);
+    }
+    const float inverse = rsqrtf(__fadd_rn(__fdiv_rn(sum, static_cast<float>(N)), p.norm_eps));
+    const float absmax = fmaxf(__fmul_rn(inverse, top), 1e-20f);
+    const float step_inverse = __fdiv_rn(127.0f, absmax);
+    if (m >= M) return;
+    if (rank == 0 && part == 0) p.norm_scale[m] = __fdiv_rn(absmax, 127.0f);
+    const uint64_t inverse2 = pair2(inverse, inverse);
+#pragma unroll
+    for (int k = 0; k < KEPT; ++k) {
+        const int sub = k / S::kChunksPerSub, c = sub * S::kSub + part * kChunkCols + (k % S::kChunksPerSub) * kChunkCols * kChunkParts;
+        uint2 bytes[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const uint32_t pair = kept[k][h * 4 + i / 2];
+                const float2 v = lanes(mul2(mul2(pair2(h2f_exact(static_cast<uint16_t>(pair & 0xffff)), h2f_exact(static_cast<uint16_t>(pair >> 16))),
+                                                 inverse2),
+                                            pair2(columns[c + h * 8 + i], columns[c + h * 8 + i + 1])));
+                y[i] = v.x;
+                y[i + 1] = v.y;
+            }
+            bytes[h] = quantize8(y, step_inverse);
+        }
+        *reinterpret_cast<uint4*>(p.norm_q + static_cast<size_t>(m) * N + n0 + c) = make_uint4(bytes[0].x, bytes[0].y, bytes[1].x, bytes[1].y);
+    }
+}
+
 template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -280,6 +362,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023u) {  // uniform across the CTA: every thread leaves before any barrier
         if (threadIdx.x == 0) record_error(kMisaligned, 20);
+        if constexpr (EPI == kEpiLinearNorm) cluster_sync();  // its peers leave the same way
         return;
     }
     uint8_t* resident = smem;                                            // a normed A: [NKS][128 rows][128 bytes, swizzled]
@@ -287,13 +370,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* io = stages + S::kStages * S::kStageBytes;                  // [kSlots][tensors][kBoxes][128 rows][128 bytes, swizzled]
     float* column_buffers = reinterpret_cast<float*>(io + S::kIoBytes);  // [2][2 * BN]
     float* row_scales = reinterpret_cast<float*>(io + S::kIoBytes + S::kColumnBytes);  // a normed A's [128]
-    uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes + S::kRowScaleBytes);
+    float* norm_smem = reinterpret_cast<float*>(io + S::kIoBytes + S::kColumnBytes + S::kRowScaleBytes);  // kEpiLinearNorm's
+    uint64_t* full = reinterpret_cast<uint64_t*>(io + S::kIoBytes + S::kColumnBytes + S::kRowScaleBytes + S::kNormBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
     uint64_t* rows_full = tmem_empty + 2;       // [2]: a slot's row operands have landed
     uint64_t* a_ready = rows_full + 2;          // a normed A's block is in place (all epilogue warps)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_ready + 1);
+    uint64_t* xready = a_ready + 1;             // [2]: every rank's row partials of a tile have arrived (kEpiLinearNorm)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xready + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = (N + BN - 1) / BN;
@@ -339,6 +424,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&rows_full[b], 1);
         }
         mbar_init(a_ready, kEpilogueWarps);
+        for (int b = 0; b < 2; ++b) mbar_init(&xready[b], EPI == kEpiLinearNorm ? n_blocks * 4 : 1);  // 4 warps a rank
         fence_barrier_init();
     }
     if (warp == 0) {
@@ -351,6 +437,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (EPI == kEpiLinearNorm) cluster_sync();  // every rank's barriers are initialised before any remote arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // weights that no earlier kernel writes (args.b_constant): the producer loads B of the first stages (the ring is
@@ -436,7 +523,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // the slot, the row operands of sub-tile j + 2 into it (those of sub-tiles 0 and 1 first). Waiting for the reads
         // before the next barrier also frees the slot for sub-tile j + 2's outputs.
         if constexpr (S::kStaged) {
-            const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
+            const bool has_rows = S::kRowTensors > 0 && (!linear16(EPI) || args.residual != nullptr);
             const bool issuer = lane == 0;
             auto load_rows = [&](int tile, int sub, int slot) {
                 if (!issuer || !has_rows || tile >= tiles) return;
@@ -482,7 +569,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             rs = h2f_bits(*args.residual_scale);
             is = h2f_bits(*args.input_scale);
         }
-        const bool has_rows = S::kRowTensors > 0 && (EPI != kEpiLinearF16 || args.residual != nullptr);
+        const bool has_rows = S::kRowTensors > 0 && (!linear16(EPI) || args.residual != nullptr);
         auto tile_origin = [&](int tile, int& m0, int& n0) {
             m0 = (tile / n_blocks) * kBlockM;
             n0 = column0(tile);
@@ -525,6 +612,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             const float* columns = column_buffers + buffer * S::kColumnArrays * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+            // kEpiLinearNorm: this thread's fp16 outputs (its row, its chunks) and their partial sums for the row's norm:
+            // the squares, and the largest |x * gain|
+            constexpr int kKept = EPI == kEpiLinearNorm ? S::kSubs * S::kChunksPerSub : 1;
+            uint32_t kept[kKept][8];
+            float squares = 0.0f, largest = 0.0f;
+#pragma unroll(EPI == kEpiLinearNorm ? S::kSubs : 1)
             for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
                 // sub-tile j stages into slot j % 2, which the stores of sub-tile j - 2 had read before the barrier that ended
                 // sub-tile j - 1; every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
@@ -533,7 +626,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 uint8_t* staged_sub = io + slot * S::kSlotBytes;
                 if (alive) {
                     tc_fence_after();
-                    for (int c = sub * SUB + part * kChunkCols; c < (sub + 1) * SUB && n0 + c < N; c += kChunkCols * kChunkParts) {  // uniform
+#pragma unroll
+                    for (int k = 0; k < S::kChunksPerSub; ++k) {
+                        const int c = sub * SUB + part * kChunkCols + k * kChunkCols * kChunkParts;
+                        if (c >= (sub + 1) * SUB || n0 + c >= N) break;  // uniform
                         uint32_t acc[16], up[16];
                         tmem_load16(lane_base + c, acc);
                         if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
@@ -543,9 +639,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const StagedChunk staged{staged_sub + box * kBoxBytes + row_in_tile * 128, unit, swizzle};
                         const StagedChunk original{staged_sub + (S::kBoxes + box) * kBoxBytes + row_in_tile * 128, unit, swizzle};
                         const int valid = N - n0 - c >= 16 ? 16 : N - n0 - c;  // 8 or 16: N is a multiple of 8
+                        uint32_t result[8];
                         if (S::kStaged || m < M)
                             epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + S::kSecond + c, staged, original,
-                                            static_cast<size_t>(m) * N + n0 + c, valid);
+                                            static_cast<size_t>(m) * N + n0 + c, valid, result);
+                        if constexpr (EPI == kEpiLinearNorm) {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                kept[sub * S::kChunksPerSub + k][i] = result[i];
+                                const float x0 = h2f_exact(static_cast<uint16_t>(result[i] & 0xffff));
+                                const float x1 = h2f_exact(static_cast<uint16_t>(result[i] >> 16));
+                                squares = __fmaf_rn(x1, x1, __fmaf_rn(x0, x0, squares));
+                                largest = fmaxf(largest, fmaxf(fabsf(__fmul_rn(x0, columns[c + 2 * i])), fabsf(__fmul_rn(x1, columns[c + 2 * i + 1]))));
+                            }
+                        }
                     }
                 }
                 if (sub == S::kSubs - 1) {
@@ -559,6 +666,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if constexpr (S::kStaged) fence_proxy_async_shared();
                 epilogue_sync();
             }
+            if constexpr (EPI == kEpiLinearNorm)
+                norm_rows_of_tile<S>(args, norm_smem, xready, columns, kept, squares, largest, local, m, n0, M, N, n_blocks, row_in_tile,
+                                     part, lane, alive);
         }
     }
     tc_fence_before();
@@ -567,6 +677,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, S::kTmemCols);
     }
+    // no rank leaves while a peer may still write its shared memory or arrive on its barriers
+    if constexpr (EPI == kEpiLinearNorm) cluster_sync();
 }
 
 // ---- host side ---------------------------------------------------------------------------------------------
@@ -656,6 +768,20 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
     int grid = tiles < multiprocessors ? tiles : multiprocessors;
+    if constexpr (EPI == kEpiLinearNorm) {
+        // clusters of a row block's n_blocks CTAs, as many as the device holds at once (a persistent cluster takes row
+        // blocks b, b + clusters, ...)
+        int clusters = 0;
+        status = max_active_clusters(kernel, dim3(kGemmThreads), S::kSmemBytes, n_blocks, &clusters);
+        if (status != cudaSuccess) return status;
+        if (clusters < 1) {
+            if (error) *error = "no cluster of " + std::to_string(n_blocks) + " GEMM CTAs fits the device";
+            return cudaErrorInvalidValue;
+        }
+        grid = (row_blocks < clusters ? row_blocks : clusters) * n_blocks;
+        return launch_dependent_cluster(kernel, dim3(grid), dim3(kGemmThreads), S::kSmemBytes, n_blocks, stream, map_a, map_b, map_out,
+                                        map_residual, map_original, args, M, N, K);
+    }
     if (NKS > 0) {
         // units: each row block's column tiles in as many groups as leave every SM one unit (at least one a block); the
         // kernel reads the group count back as grid / row blocks
@@ -725,6 +851,12 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 128) return launch<1, 128, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearNorm:
+                if (N % 256 != 0 || N / 256 > kMaxCluster || !args.norm_q || !args.norm_scale || !args.norm_gain) {
+                    if (error) *error = "the norm epilogue takes N a multiple of 256 up to " + std::to_string(256 * kMaxCluster) + " and its outputs";
+                    return cudaErrorInvalidValue;
+                }
+                return launch<1, 256, false, kEpiLinearNorm, 128>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     }

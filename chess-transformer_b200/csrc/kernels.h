@@ -18,6 +18,8 @@ enum GemmEpilogue : int {
     kEpiInt32 = 4,      // int8: the raw int32 sums
     kEpiLinearF16 = 5,  // fp16: fp16((acc + bias) + residual), bias and residual optional
     kEpiLinearF32 = 6,  // fp16: fp32 acc + fp32 bias (optional)
+    kEpiLinearNorm = 7, // fp16: as kEpiLinearF16, then norm_quant of each output row into norm_q / norm_scale (a cluster of
+                        // the N / 256 CTAs of a row block sums the rows' squares through distributed shared memory)
 };
 
 struct GemmArgs {
@@ -38,6 +40,9 @@ struct GemmArgs {
     // B is a weight that no kernel launched before this one writes: its first stages load before the wait for the
     // earlier kernels (programmatic dependent launch), overlapping their tail
     bool b_constant = false;
+    // kEpiLinearNorm: the int8 rows [M, N] and their scales [M] of norm_quant(out) with norm_gain and norm_eps
+    int8_t* norm_q = nullptr;
+    float* norm_scale = nullptr;
 };
 
 // kind 0: int8 A [M, K], B [N, K] (gated: [2N, K]); kind 1: fp16 A [M, K], B [N, K].

@@ -223,6 +223,33 @@ def _(x, weight, bias=None, residual=None, gated=False, accumulate_fp32=False, o
     return x.new_empty(*x.shape[:-1], weight.shape[1], dtype=torch.float32 if accumulate_fp32 else x.dtype)
 
 
+@torch.library.custom_op("fry::linear_norm_quant", mutates_args=())
+def linear_norm_quant(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, residual: torch.Tensor | None, gain: torch.Tensor,
+                      eps: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """`chess::linear` (fp16, weight [K, N] as the reference stores it) then `chess::norm_quant` of its output
+    (model/int8_blocks.py:191-193, 274-288) as one kernel: (out, q, scale). out equals `linear`'s bit for bit; q and scale
+    equal `norm_quant(out, gain, eps)` to within its rounding. N a multiple of 256 up to 1024."""
+    _cuda("linear_norm_quant", x, weight, bias, residual, gain)
+    _dtype("linear_norm_quant", x, torch.float16, "x")
+    K, N = weight.shape
+    x = x.contiguous()
+    M = x.numel() // K
+    out = x.new_empty(*x.shape[:-1], N, dtype=torch.float16)
+    q = x.new_empty(*x.shape[:-1], N, dtype=torch.int8)
+    scale = x.new_empty(x.shape[:-1], dtype=torch.float32)
+    bias = bias.half().contiguous() if bias is not None else None
+    residual = residual.contiguous() if residual is not None else None
+    library().fry_linear_norm_quant(_ptr(x), _ptr(weight.t().contiguous()), _ptr(bias), _ptr(residual), _ptr(out), _ptr(gain.half().contiguous()),
+                                    eps, _ptr(q), _ptr(scale), M, N, K, _stream(x))
+    return out, q, scale
+
+
+@linear_norm_quant.register_fake
+def _(x, weight, bias, residual, gain, eps):
+    shape = (*x.shape[:-1], weight.shape[1])
+    return x.new_empty(shape, dtype=torch.float16), x.new_empty(shape, dtype=torch.int8), x.new_empty(x.shape[:-1], dtype=torch.float32)
+
+
 @torch.library.custom_op("fry::board_embedding", mutates_args=())
 def board_embedding(boards: torch.Tensor, embed: torch.Tensor, position: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
     """`chess::board_embedding` (model/fused_blocks.py:495-507): boards [B, 70] -> [B, 70, D] fp16, the 23 square-feature

@@ -93,6 +93,16 @@ int fry_template_attention(const uint16_t* projected, const uint16_t* paired_tem
 int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, const uint16_t* residual, void* out, int M, int N, int K,
                int out_fp32, void* stream);
 
+/* `chess::linear` (fp16, as fry_linear) feeding `chess::norm_quant` (model/int8_blocks.py:191-193) in one kernel, the pair
+ * `Int8Block.forward` runs for attention-out -> ln2 (model/int8_blocks.py:274-288): out[M, N] fp16 = (x . weight^T + bias)
+ * + residual, then q[M, N] int8 and scale[M] fp32 of RMSNorm(out) * gain. The N / 256 CTAs that share a 128-row block
+ * form a thread-block cluster and sum each row's squares through distributed shared memory. out equals fry_linear's bit
+ * for bit; q and scale equal fry_norm_quant's to within its rounding: the squares are summed in another order, and the
+ * row's absmax is taken as inverse * max|out * gain| (within fp32 rounding of max|(out * inverse) * gain|).
+ * N a multiple of 256 up to 1024, K of 8; x, weight, out, residual, gain and q 16-byte aligned; out may alias residual. */
+int fry_linear_norm_quant(const uint16_t* x, const uint16_t* weight, const uint16_t* bias, const uint16_t* residual, uint16_t* out,
+                          const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int N, int K, void* stream);
+
 /* `chess::board_embedding` / `chess::input_embedding` (model/fused_blocks.py:397-406,495-507, SquareFeatures.indices
  * model/model.py:147-169): boards int64 [B, 70] -> out [B, 70, D] fp16 = embed[token] + position[t] + fp16(sum of the 23
  * square-feature rows of table). embed [81, D], position [70, D], table [1735, D] fp16. A token outside the vocabulary

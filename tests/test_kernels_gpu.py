@@ -135,6 +135,32 @@ def test_int8_linear_normed_refuses_other_widths():
                                torch.ones(64, device="cuda"), None, False)
 
 
+# the attention-out linear with ln2's norm in its epilogue: a cluster of N / 256 CTAs a row block (1 to 4); 17920 rows: 140
+# row blocks, more than the clusters the device holds at once, so clusters take several
+@pytest.mark.parametrize("M, N", [(1, 768), (70, 768), (4480, 768), (17920, 768), (19001, 768), (300, 256), (300, 1024)])
+def test_linear_norm_quant_is_linear_then_norm_quant(M, N):
+    g = torch.Generator().manual_seed(M + N)
+    K = 768
+    x = torch.randn(M, K, generator=g).half().cuda()
+    weight = (torch.randn(K, N, generator=g) / 16).half().cuda()
+    bias = (torch.randn(N, generator=g) / 16).half().cuda()
+    residual = (torch.randn(M, N, generator=g) * 2).half().cuda()
+    gain = (torch.rand(N, generator=g) + 0.5).half().cuda()
+    out, q, scale = ops.linear_norm_quant(x, weight, bias, residual, gain, 1e-5)
+    expected = ops.linear(x, weight, bias, residual)
+    assert torch.equal(out.cpu(), expected.cpu())  # the same epilogue, bit for bit
+    eq, escale = ops.norm_quant(expected, gain, 1e-5)
+    # the squares summed in another order and absmax from max|out * gain|: scales within fp32 rounding, an int8 value one
+    # step apart now and then
+    assert torch.allclose(scale.cpu(), escale.cpu(), rtol=2e-6, atol=0)
+    difference = (q.cpu().int() - eq.cpu().int()).abs()
+    assert difference.max() <= 1 and (difference > 0).float().mean() < 1e-3
+    # and the reference's own criterion (tests/test_int8.py:246-264) against the fp32 RMSNorm of the fp16 output
+    normed = torch.nn.functional.rms_norm(expected.float().cpu(), (N,), gain.float().cpu(), 1e-5)
+    step = normed.abs().amax(-1) / 127
+    assert ((q.cpu().float() * scale.cpu()[:, None] - normed).abs() <= 0.501 * step[:, None] + 1e-6).all()
+
+
 @pytest.mark.parametrize("M, N, K", [(70, 200, 128), (4480, 768, 768)])
 def test_fp16_linear_is_the_oracle(M, N, K):
     g = torch.Generator().manual_seed(N)

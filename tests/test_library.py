@@ -49,6 +49,8 @@ def test_shapes_are_refused_on_the_host_before_any_launch(lib):
         lib.fry_int8_linear(None, None, None, None, None, None, None, None, None, None, 70, 12, 256, 0, None)
     with pytest.raises(FryError, match="K = 768"):
         lib.fry_int8_linear_normed(None, None, 1e-5, None, None, None, None, 70, 864, 512, 0, None)
+    with pytest.raises(FryError, match="multiple of 256"):
+        lib.fry_linear_norm_quant(None, None, None, None, None, None, 1e-5, None, None, 70, 800, 768, None)
     with pytest.raises(FryError, match="template attention"):
         lib.fry_template_attention(None, None, None, None, None, 1, 24, 12, 8, 64, 8, 1e-5, None)
     assert "template attention" in lib.fry_last_error().decode()
