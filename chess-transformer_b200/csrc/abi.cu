@@ -37,6 +37,108 @@ int projection_rows(const FryNetwork* n, int dq) {
     return (n->heads + n->kv_heads) * dq + n->kv_heads * n->dv + n->heads * n->templates_count;
 }
 
+constexpr int kAnswerWidth = 1969;  // 1968 move logits, then the expected score
+
+// The forward on boards (int64 [B, 70]) or on lean lanes' rows (uint8 [B, 508]: tokens, then the answer columns that
+// lean_answers [B, 219] gathers from rows), in the caller's workspace of fry_forward_workspace_bytes.
+int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_rows, int B, float* rows, float* lean_answers,
+                void* workspace, size_t workspace_bytes, void* stream) {
+    if (!n || B < 0) return fail(FRY_ERROR_SHAPE, "fry_forward needs a network and B >= 0");
+    if (B == 0) return check(cudaSuccess, "");
+    if (workspace_bytes < fry_forward_workspace_bytes(n, B))
+        return fail(FRY_ERROR_SHAPE, "fry_forward's workspace is smaller than fry_forward_workspace_bytes");
+    if (!aligned16(workspace)) return fail(FRY_ERROR_SHAPE, "fry_forward needs a 16-byte aligned workspace");
+    const cudaStream_t s = as_stream(stream);
+    const int D = n->d_model, M = B * 70;
+    uint8_t* cursor = static_cast<uint8_t*>(workspace);
+    auto take = [&](size_t bytes) {
+        uint8_t* p = cursor;
+        cursor += round_up(bytes);
+        return p;
+    };
+    int widest = 0;
+    for (int i = 0; i < n->layers; ++i) {
+        const int r = projection_rows(n, n->blocks[i].dq);
+        widest = r > widest ? r : widest;
+    }
+    const int q_width = D > n->down_width ? D : n->down_width;
+    uint16_t* original = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    uint16_t* x = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    uint16_t* attended = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
+    int8_t* q = reinterpret_cast<int8_t*>(take(static_cast<size_t>(M) * q_width));
+    float* scale = reinterpret_cast<float*>(take(static_cast<size_t>(M) * 4));
+    uint16_t* projected = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * widest * 2));
+    uint16_t* hidden = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * n->hidden * 2));
+    const size_t heads_bytes = fry::heads_workspace_bytes(B, D);
+    void* heads_workspace = take(heads_bytes);
+
+    // ln1 and ln2 run as their own kernels. Fused into a neighbouring GEMM they measured slower: in the int8 GEMM's prologue
+    // (fry_int8_linear_normed) no faster at 256 boards and slower at small batches, where each CTA of a row block repeats
+    // the block's norm; in the attention-out GEMM's epilogue (fry_linear_norm_quant) slower at every batch, its clusters
+    // of 3 CTAs taking up to 4 row blocks where single CTAs take 3 tiles, and its cluster exchange adding to each tile
+    std::string detail;
+    cudaError_t status = lean_rows ? fry::board_embedding_lean(lean_rows, n->embed, n->position, n->table, original, B, D, s)
+                                   : fry::board_embedding(boards, n->embed, n->position, n->table, original, B, D, s);
+    if (status != cudaSuccess) return check(status, "fry_forward: embedding");
+    for (int i = 0; i < n->layers; ++i) {
+        const FryBlock& b = n->blocks[i];
+        const std::string where = "fry_forward: block " + std::to_string(i);
+        // ln1 (the first block mixes its own input; later ones get it mixed by the previous down)
+        status = i == 0 ? fry::norm_quant(original, original, b.residual_scale, b.input_scale, b.ln1, n->eps, x, q, scale, M, D, s)
+                        : fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln1, n->eps, nullptr, q, scale, M, D, s);
+        if (status != cudaSuccess) return check(status, where + " ln1");
+        const int rows_p = projection_rows(n, b.dq);
+        fry::GemmArgs projection;
+        projection.x_scale = scale;
+        projection.w_scale = b.projection_scale;
+        projection.bias = b.projection_bias;
+        projection.out = projected;
+        projection.b_constant = true;
+        status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " projection", detail);
+        status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
+                                         n->templates_count, n->eps, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " attention", detail);
+        fry::GemmArgs combine;
+        combine.bias = b.combine_heads_bias;
+        combine.residual = x;
+        combine.out = x;
+        combine.b_constant = true;
+        status = fry::gemm(1, fry::kEpiLinearF16, attended, b.combine_heads, combine, M, D, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " combine_heads", detail);
+        status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
+        if (status != cudaSuccess) return check(status, where + " ln2");
+        fry::GemmArgs gate_up;
+        gate_up.x_scale = scale;
+        gate_up.w_scale = b.gate_up_scale;
+        gate_up.out = hidden;
+        gate_up.b_constant = true;
+        status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " gate_up", detail);
+        status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
+        if (status != cudaSuccess) return check(status, where + " rotate_quant");
+        fry::GemmArgs down;
+        down.x_scale = scale;
+        down.w_scale = b.down_scale;
+        down.residual = x;
+        down.out = x;
+        down.b_constant = true;
+        const bool mixes = i + 1 < n->layers;
+        if (mixes) {
+            down.original = original;
+            down.residual_scale = n->blocks[i + 1].residual_scale;
+            down.input_scale = n->blocks[i + 1].input_scale;
+        }
+        status = fry::gemm(0, mixes ? fry::kEpiMix : fry::kEpiResidual, q, b.down, down, M, D, n->down_width, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " down", detail);
+    }
+    const FryHeads& h = n->head_weights;
+    fry::HeadWeights w{h.ln_gain, h.a_weight, h.a_bias, h.narrow_weight, h.narrow_bias, h.hidden_weight, h.hidden_bias, h.out_weight,
+                       h.out_bias, h.bins};
+    status = fry::heads(x, w, n->eps, rows, heads_workspace, heads_bytes, B, D, s, &detail, lean_rows, lean_answers);
+    return check(status, "fry_forward: heads", detail);
+}
+
 }  // namespace
 
 extern "C" {
@@ -227,99 +329,25 @@ size_t fry_forward_workspace_bytes(const FryNetwork* n, int B) {
 }
 
 int fry_forward(const FryNetwork* n, const int64_t* boards, int B, float* rows, void* workspace, size_t workspace_bytes, void* stream) {
-    if (!n || B < 0) return fail(FRY_ERROR_SHAPE, "fry_forward needs a network and B >= 0");
-    if (B == 0) return check(cudaSuccess, "");
-    if (workspace_bytes < fry_forward_workspace_bytes(n, B))
-        return fail(FRY_ERROR_SHAPE, "fry_forward's workspace is smaller than fry_forward_workspace_bytes");
-    if (!aligned16(workspace)) return fail(FRY_ERROR_SHAPE, "fry_forward needs a 16-byte aligned workspace");
-    const cudaStream_t s = as_stream(stream);
-    const int D = n->d_model, M = B * 70;
-    uint8_t* cursor = static_cast<uint8_t*>(workspace);
-    auto take = [&](size_t bytes) {
-        uint8_t* p = cursor;
-        cursor += round_up(bytes);
-        return p;
-    };
-    int widest = 0;
-    for (int i = 0; i < n->layers; ++i) {
-        const int r = projection_rows(n, n->blocks[i].dq);
-        widest = r > widest ? r : widest;
-    }
-    const int q_width = D > n->down_width ? D : n->down_width;
-    uint16_t* original = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
-    uint16_t* x = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
-    uint16_t* attended = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * D * 2));
-    int8_t* q = reinterpret_cast<int8_t*>(take(static_cast<size_t>(M) * q_width));
-    float* scale = reinterpret_cast<float*>(take(static_cast<size_t>(M) * 4));
-    uint16_t* projected = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * widest * 2));
-    uint16_t* hidden = reinterpret_cast<uint16_t*>(take(static_cast<size_t>(M) * n->hidden * 2));
-    const size_t heads_bytes = fry::heads_workspace_bytes(B, D);
-    void* heads_workspace = take(heads_bytes);
+    return run_forward(n, boards, nullptr, B, rows, nullptr, workspace, workspace_bytes, stream);
+}
 
-    // ln1 and ln2 run as their own kernels. Fused into a neighbouring GEMM they measured slower: in the int8 GEMM's prologue
-    // (fry_int8_linear_normed) no faster at 256 boards and slower at small batches, where each CTA of a row block repeats
-    // the block's norm; in the attention-out GEMM's epilogue (fry_linear_norm_quant) slower at every batch, its clusters
-    // of 3 CTAs taking up to 4 row blocks where single CTAs take 3 tiles, and its cluster exchange adding to each tile
-    std::string detail;
-    cudaError_t status = fry::board_embedding(boards, n->embed, n->position, n->table, original, B, D, s);
-    if (status != cudaSuccess) return check(status, "fry_forward: embedding");
-    for (int i = 0; i < n->layers; ++i) {
-        const FryBlock& b = n->blocks[i];
-        const std::string where = "fry_forward: block " + std::to_string(i);
-        // ln1 (the first block mixes its own input; later ones get it mixed by the previous down)
-        status = i == 0 ? fry::norm_quant(original, original, b.residual_scale, b.input_scale, b.ln1, n->eps, x, q, scale, M, D, s)
-                        : fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln1, n->eps, nullptr, q, scale, M, D, s);
-        if (status != cudaSuccess) return check(status, where + " ln1");
-        const int rows_p = projection_rows(n, b.dq);
-        fry::GemmArgs projection;
-        projection.x_scale = scale;
-        projection.w_scale = b.projection_scale;
-        projection.bias = b.projection_bias;
-        projection.out = projected;
-        projection.b_constant = true;
-        status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " projection", detail);
-        status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
-                                         n->templates_count, n->eps, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " attention", detail);
-        fry::GemmArgs combine;
-        combine.bias = b.combine_heads_bias;
-        combine.residual = x;
-        combine.out = x;
-        combine.b_constant = true;
-        status = fry::gemm(1, fry::kEpiLinearF16, attended, b.combine_heads, combine, M, D, D, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " combine_heads", detail);
-        status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
-        if (status != cudaSuccess) return check(status, where + " ln2");
-        fry::GemmArgs gate_up;
-        gate_up.x_scale = scale;
-        gate_up.w_scale = b.gate_up_scale;
-        gate_up.out = hidden;
-        gate_up.b_constant = true;
-        status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " gate_up", detail);
-        status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
-        if (status != cudaSuccess) return check(status, where + " rotate_quant");
-        fry::GemmArgs down;
-        down.x_scale = scale;
-        down.w_scale = b.down_scale;
-        down.residual = x;
-        down.out = x;
-        down.b_constant = true;
-        const bool mixes = i + 1 < n->layers;
-        if (mixes) {
-            down.original = original;
-            down.residual_scale = n->blocks[i + 1].residual_scale;
-            down.input_scale = n->blocks[i + 1].input_scale;
-        }
-        status = fry::gemm(0, mixes ? fry::kEpiMix : fry::kEpiResidual, q, b.down, down, M, D, n->down_width, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " down", detail);
-    }
-    const FryHeads& h = n->head_weights;
-    fry::HeadWeights w{h.ln_gain, h.a_weight, h.a_bias, h.narrow_weight, h.narrow_bias, h.hidden_weight, h.hidden_bias, h.out_weight,
-                       h.out_bias, h.bins};
-    status = fry::heads(x, w, n->eps, rows, heads_workspace, heads_bytes, B, D, s, &detail);
-    return check(status, "fry_forward: heads", detail);
+size_t fry_forward_lean_workspace_bytes(const FryNetwork* n, int B) {
+    if (!n || B <= 0) return 0;
+    return fry_forward_workspace_bytes(n, B) + round_up(static_cast<size_t>(B) * (kAnswerWidth * 4));
+}
+
+int fry_forward_lean(const FryNetwork* n, const uint8_t* lean_rows, int B, float* answers, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+    if (!n || B < 0) return fail(FRY_ERROR_SHAPE, "fry_forward_lean needs a network and B >= 0");
+    if (B == 0) return check(cudaSuccess, "");
+    if (workspace_bytes < fry_forward_lean_workspace_bytes(n, B))
+        return fail(FRY_ERROR_SHAPE, "fry_forward_lean's workspace is smaller than fry_forward_lean_workspace_bytes");
+    if (!lean_rows || !answers || !aligned16(workspace)) return fail(FRY_ERROR_SHAPE, "fry_forward_lean needs its rows, answers and a 16-byte aligned workspace");
+    // the whole answer rows sit at the end of the workspace, the forward's own scratch before them
+    const size_t forward_bytes = fry_forward_workspace_bytes(n, B);
+    float* rows = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + forward_bytes);
+    return run_forward(n, nullptr, lean_rows, B, rows, answers, workspace, forward_bytes, stream);
 }
 
 }  // extern "C"

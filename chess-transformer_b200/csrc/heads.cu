@@ -215,7 +215,11 @@ __global__ void __launch_bounds__(256) linear_sum_kernel(const float* __restrict
 inline int split_size(int K) { return (K + kEvalSplitsMax - 1) / kEvalSplitsMax < 160 ? 160 : ((K + kEvalSplitsMax - 1) / kEvalSplitsMax + 31) / 32 * 32; }
 
 // One warp per board: the softmax of its value logits times the bin centres (2i + 1) / 2bins, into the row's last column.
-__global__ void __launch_bounds__(256) expected_score_kernel(const float* __restrict__ logits, float* __restrict__ rows, int B, int bins) {
+// With lean lanes, each board's answer also gathers its lane's answer columns of its row (the move logits the policy
+// kernel wrote, the expected score this one writes): lean_answers[b, k] = rows[b, column k], a column outside the row
+// recorded as kBadColumn and answered 0.
+__global__ void __launch_bounds__(256) expected_score_kernel(const float* __restrict__ logits, float* __restrict__ rows, int B, int bins,
+                                                             const uint8_t* __restrict__ lean_rows, float* __restrict__ lean_answers) {
     grid_dependency_start();
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
@@ -231,11 +235,23 @@ __global__ void __launch_bounds__(256) expected_score_kernel(const float* __rest
     }
     total = warp_sum(total);
     weighted = warp_sum(weighted);
-    if (lane == 0) rows[static_cast<size_t>(b) * (kMoves + 1) + kMoves] = __fdiv_rn(weighted, total);
+    const float expected = __fdiv_rn(weighted, total);
+    float* row_out = rows + static_cast<size_t>(b) * (kMoves + 1);
+    if (lane == 0) row_out[kMoves] = expected;
+    if (lean_answers) {
+        __syncwarp();  // the expected score, which padding columns gather, is in the row
+        const uint8_t* columns = lean_rows + static_cast<size_t>(b) * kLeanRow + kHeadTokens;
+        for (int k = lane; k < kLeanColumns; k += 32) {
+            const int column = static_cast<int16_t>(static_cast<uint16_t>(columns[2 * k] | (columns[2 * k + 1] << 8)));
+            const bool ok = column >= 0 && column <= kMoves;
+            if (!ok) record_error(kBadColumn, b);
+            lean_answers[static_cast<size_t>(b) * kLeanColumns + k] = ok ? (column == kMoves ? expected : row_out[column]) : 0.0f;
+        }
+    }
 }
 
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
-                  int D, cudaStream_t stream, std::string* error) {
+                  int D, cudaStream_t stream, std::string* error, const uint8_t* lean_rows, float* lean_answers) {
     if (B <= 0) return cudaSuccess;
     if (workspace_bytes < heads_workspace_bytes(B, D)) {
         if (error) *error = "the heads' workspace is smaller than fry_heads_workspace_bytes";
@@ -287,7 +303,8 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     status = launch_dependent(linear_sum_kernel<false>, dim3((B * w.bins + 255) / 256), dim3(256), 0, stream, partial, w.out_bias, value_logits,
                               B, w.bins, splits2);
     if (status != cudaSuccess) return status;
-    return launch_dependent(expected_score_kernel, dim3((B + 7) / 8), dim3(256), 0, stream, value_logits, rows, B, w.bins);
+    return launch_dependent(expected_score_kernel, dim3((B + 7) / 8), dim3(256), 0, stream, value_logits, rows, B, w.bins, lean_rows,
+                            lean_answers);
 }
 
 }  // namespace fry

@@ -54,6 +54,11 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
                        const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream);
 cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream);
 cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream);
+// Lean lanes (engine/inference.py:94-100,130-135; engine/selfplay_rs/src/lib.rs:330-333): a board is a row of
+// kLeanRow bytes, its 70 token bytes then kLeanColumns int16 answer columns, and its answer those columns of its row.
+constexpr int kLeanColumns = 219, kLeanRow = 70 + 2 * kLeanColumns;
+cudaError_t board_embedding_lean(const uint8_t* lean_rows, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
+                                 uint16_t* out, int B, int D, cudaStream_t stream);
 cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
                             uint16_t* out, int B, int D, cudaStream_t stream);
 
@@ -91,7 +96,8 @@ struct HeadsWorkspace {
 };
 constexpr size_t heads_workspace_bytes_of(size_t B, size_t D) { return HeadsWorkspace(B, D).total; }
 size_t heads_workspace_bytes(int B, int D);
+// lean_rows / lean_answers (optional): each board's answer columns gathered from its row into lean_answers [B, 219]
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
-                  int D, cudaStream_t stream, std::string* error);
+                  int D, cudaStream_t stream, std::string* error, const uint8_t* lean_rows = nullptr, float* lean_answers = nullptr);
 
 }  // namespace fry

@@ -129,7 +129,9 @@ FRY_DEVICE int code_at(const int* codes, int file, int rank) {
 }
 
 // One CTA per (board, 256 columns): the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
-__global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ boards, const uint16_t* __restrict__ embed,
+// A board's tokens: int64 [70] (boards, pitch 70) or the first 70 bytes of a lean lane's row (pitch kLeanRow).
+template <typename Token>
+__global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict__ boards, int pitch, const uint16_t* __restrict__ embed,
                                                         const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
                                                         uint16_t* __restrict__ out, int D) {
     grid_dependency_start();
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restric
     __shared__ int rows[kSquares][kFeatures];
     const int b = blockIdx.x, tid = threadIdx.x;
     for (int t = tid; t < kTokens; t += blockDim.x) {
-        const int64_t token = boards[static_cast<size_t>(b) * kTokens + t];
+        const int64_t token = static_cast<int64_t>(boards[static_cast<size_t>(b) * pitch + t]);
         const bool ok = t < kSquares ? (token >= 0 && token < kPieceCodes) : (token >= 0 && token < kVocab);
         if (!ok) record_error(kBadToken, b);
         codes[t] = ok ? static_cast<int>(token) : 0;
@@ -289,7 +291,16 @@ cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const 
                             uint16_t* out, int B, int D, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
     if (D % 8 != 0) return cudaErrorInvalidValue;
-    return launch_dependent(embedding_kernel, dim3(B, (D + 255) / 256), dim3(256), 0, stream, boards, embed, position, table, out, D);
+    return launch_dependent(embedding_kernel<int64_t>, dim3(B, (D + 255) / 256), dim3(256), 0, stream, boards, kTokens, embed, position,
+                            table, out, D);
+}
+
+cudaError_t board_embedding_lean(const uint8_t* lean_rows, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
+                                 uint16_t* out, int B, int D, cudaStream_t stream) {
+    if (B <= 0) return cudaSuccess;
+    if (D % 8 != 0) return cudaErrorInvalidValue;
+    return launch_dependent(embedding_kernel<uint8_t>, dim3(B, (D + 255) / 256), dim3(256), 0, stream, lean_rows, kLeanRow, embed, position,
+                            table, out, D);
 }
 
 }  // namespace fry

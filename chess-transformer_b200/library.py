@@ -57,6 +57,8 @@ SIGNATURES = {
     "fry_heads_noalloc": ([_ptr, ctypes.POINTER(FryHeads), _c_float, _ptr, _c_int, _c_int, _ptr], _c_int),
     "fry_forward_workspace_bytes": ([ctypes.POINTER(FryNetwork), _c_int], _size),
     "fry_forward": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
+    "fry_forward_lean_workspace_bytes": ([ctypes.POINTER(FryNetwork), _c_int], _size),
+    "fry_forward_lean": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
 }
 
 _lock = threading.Lock()

@@ -19,7 +19,7 @@ import numpy as np
 import torch
 from torch import nn
 
-from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
+from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
 from .library import FryBlock, FryError, FryNetwork, library
 from .ops import heads_struct, pair_templates
 
@@ -188,6 +188,23 @@ class Int8Network(nn.Module):
                           ctypes.cast(blocks, ctypes.POINTER(FryBlock)),
                           heads_struct(t["ln"], t["a_weight"], t["a_bias"], t["narrow_weight"], t["narrow_bias"], t["hidden_weight"],
                                        t["hidden_bias"], t["out_weight"], t["out_bias"]))
+
+    def forward_lean(self, lean_rows: torch.Tensor) -> torch.Tensor:
+        """Lean lanes' rows uint8 [B, LEAN_ROW] cuda (tokens, then int16 answer columns) -> answers fp32 [B, LEAN_COLUMNS]:
+        forward(tokens) gathered at the columns (engine/inference.py:130-135), the gather in the heads' last kernel."""
+        if not lean_rows.is_cuda or lean_rows.device != self.device:
+            raise FryError(f"Int8Network on {self.device} got lean rows on {lean_rows.device}")
+        if lean_rows.dtype != torch.uint8 or lean_rows.dim() != 2 or lean_rows.shape[1] != LEAN_ROW:
+            raise FryError(f"lean rows are uint8 [B, {LEAN_ROW}], got {lean_rows.dtype} {tuple(lean_rows.shape)}")
+        lean_rows = lean_rows.contiguous()
+        B = lean_rows.shape[0]
+        answers = torch.empty(B, LEAN_COLUMNS, device=self.device, dtype=torch.float32)
+        lib = library()
+        size = lib.fry_forward_lean_workspace_bytes(ctypes.byref(self._network), B)
+        workspace = torch.empty(max(size, 1), device=self.device, dtype=torch.uint8)
+        lib.fry_forward_lean(ctypes.byref(self._network), ctypes.c_void_p(lean_rows.data_ptr()), B, ctypes.c_void_p(answers.data_ptr()),
+                             ctypes.c_void_p(workspace.data_ptr()), size, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        return answers
 
     def workspace_bytes(self, boards: int) -> int:
         return library().fry_forward_workspace_bytes(ctypes.byref(self._network), boards)

@@ -1,14 +1,16 @@
 """The batch runtime around the network: CUDA graphs per batch size on lanes of their own stream, fed from pinned host
-buffers. Mirrors the reference's `GraphedBatches` and `Lane` (engine/inference.py:62-225, non-lean lanes): `launch`
-copies a batch of boards in and replays the smallest graph that holds it and returns at once; `collect` copies the answer
-rows out and waits for them. At most `in_flight` batches are out at a time, one a lane.
+buffers. Mirrors the reference's `GraphedBatches` and `Lane` (engine/inference.py:62-225): `launch` copies a batch of
+boards in and replays the smallest graph that holds it and returns at once; `collect` copies the answer rows out and
+waits for them. At most `in_flight` batches are out at a time, one a lane. Lean lanes (lean=True, the Rust round loop's
+format) take rows of tokens and answer columns through `free_lane().rows_array` and `launch_filled`, and `collect` gives
+each board's LEAN_COLUMNS answers (the network's `forward_lean`), a ninth of the bytes of whole rows.
 """
 import numpy as np
 import torch
 from torch import nn
 
 from .boards import START_BOARD
-from .encoding import ANSWER_WIDTH, TOKENS_PER_BOARD
+from .encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
 
 
 def small_graph_sizes(max_batch: int, chunk: int | None = None) -> list[int]:
@@ -22,39 +24,52 @@ def small_graph_sizes(max_batch: int, chunk: int | None = None) -> list[int]:
 
 
 class Lane:
-    """One stream with a graph per size, its own memory pool, and pinned buffers for the boards in and the rows out."""
+    """One stream with a graph per size, its own memory pool, and pinned buffers for the boards in and the rows out. A lean
+    lane takes rows of LEAN_ROW bytes (tokens, then int16 answer columns, all 1968 at first: the expected score's) and
+    answers LEAN_COLUMNS floats a board (engine/inference.py:94-106)."""
 
-    def __init__(self, model: nn.Module, sizes: list[int]):
+    def __init__(self, model: nn.Module, sizes: list[int], lean: bool = False):
         self.stream = torch.cuda.Stream()
         self.device = torch.cuda.current_device()
         self.pending = False
+        self.lean = lean
         largest = sizes[-1]
         # recorded on real boards, as the reference records its lanes
         self.boards = torch.from_numpy(np.tile(START_BOARD, (largest, 1))).long().cuda()
-        self.boards_host = torch.zeros(largest, TOKENS_PER_BOARD, dtype=torch.long, pin_memory=True)
-        self.answers_host = torch.zeros(largest, ANSWER_WIDTH, dtype=torch.float32, pin_memory=True)
+        if lean:
+            self.rows = torch.zeros(largest, LEAN_ROW, dtype=torch.uint8, device="cuda")
+            self.rows[:, :TOKENS_PER_BOARD] = self.boards
+            self.rows[:, TOKENS_PER_BOARD:].view(torch.int16).fill_(ANSWER_WIDTH - 1)
+            self.rows_host = torch.zeros(largest, LEAN_ROW, dtype=torch.uint8, pin_memory=True)
+            self.rows_array = self.rows_host.numpy()
+        else:
+            self.boards_host = torch.zeros(largest, TOKENS_PER_BOARD, dtype=torch.long, pin_memory=True)
+            self.boards_array = self.boards_host.numpy()
+        self.answers_host = torch.zeros(largest, LEAN_COLUMNS if lean else ANSWER_WIDTH, dtype=torch.float32, pin_memory=True)
         self.done = torch.cuda.Event(blocking=True)
+        answer = (lambda size: model.forward_lean(self.rows[:size])) if lean else (lambda size: model(self.boards[:size]))
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream), torch.no_grad():
             for size in sizes:
-                model(self.boards[:size])
+                answer(size)
         torch.cuda.current_stream().wait_stream(self.stream)
         self.pool = torch.cuda.graph_pool_handle()
         self.graphs, self.answers = {}, {}
         for size in reversed(sizes):
             self.graphs[size] = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graphs[size], pool=self.pool, stream=self.stream), torch.no_grad():
-                self.answers[size] = model(self.boards[:size])
+                self.answers[size] = answer(size)
         self.done.record(self.stream)
         self.done.synchronize()
 
 
 class GraphedBatches:
-    """engine/inference.py:148-225: launch(boards uint8/int64 [n, 70]) -> handle; collect(handle) -> float32 [n, 1969]."""
+    """engine/inference.py:148-225: launch(boards uint8/int64 [n, 70]) -> handle; collect(handle) -> float32 [n, 1969]. Lean
+    (lean=True): fill free_lane().rows_array[:n], launch_filled(lane, n), collect(handle) -> float32 [n, 219]."""
 
-    def __init__(self, model: nn.Module, sizes: list[int], in_flight: int = 2, blocking_wait: bool = False):
-        self.model, self.sizes, self.blocking_wait = model, sizes, blocking_wait
-        self.lanes = [Lane(model, sizes) for _ in range(in_flight)]
+    def __init__(self, model: nn.Module, sizes: list[int], in_flight: int = 2, blocking_wait: bool = False, lean: bool = False):
+        self.model, self.sizes, self.blocking_wait, self.lean = model, sizes, blocking_wait, lean
+        self.lanes = [Lane(model, sizes, lean) for _ in range(in_flight)]
 
     def free_lane(self) -> Lane:
         lane = next((lane for lane in self.lanes if not lane.pending), None)
@@ -63,6 +78,8 @@ class GraphedBatches:
         return lane
 
     def launch(self, boards: np.ndarray) -> tuple[Lane, int, int]:
+        if self.lean:
+            raise RuntimeError("lean lanes answer rows with their columns (launch_filled), not boards")
         lane = self.free_lane()
         lane.boards_host[:len(boards)] = torch.from_numpy(np.asarray(boards))
         return self.launch_filled(lane, len(boards))
@@ -71,7 +88,10 @@ class GraphedBatches:
         size = next(size for size in self.sizes if size >= count)
         lane.pending = True
         with torch.cuda.stream(lane.stream):
-            lane.boards[:count].copy_(lane.boards_host[:count], non_blocking=True)
+            if lane.lean:
+                lane.rows[:count].copy_(lane.rows_host[:count], non_blocking=True)
+            else:
+                lane.boards[:count].copy_(lane.boards_host[:count], non_blocking=True)
             lane.graphs[size].replay()
             if self.blocking_wait:
                 lane.done.record(lane.stream)

@@ -31,7 +31,8 @@ const char* fry_last_error(void);
 const char* fry_version(void);
 
 /* Reads the current device's status word: *code 0 if no kernel recorded a fault, else the code (1 a bounded wait timed
- * out, 2 a board token outside the vocabulary) and *where its site. clear != 0 resets it. Synchronous. */
+ * out, 2 a board token outside the vocabulary, 3 a launch shape a kernel does not take, 4 misaligned shared memory, 5 a
+ * lean lane's answer column outside the answer row) and *where its site. clear != 0 resets it. Synchronous. */
 int fry_device_status(int* code, int* where, int clear);
 
 /* ---- block ops: each replaces one torch custom op of the reference ----------------------------------------------- */
@@ -186,6 +187,15 @@ size_t fry_forward_workspace_bytes(const FryNetwork* network, int B);
  * [B, 70] -> rows fp32 [B, 1969] (1968 move logits, then the expected score). */
 int fry_forward(const FryNetwork* network, const int64_t* boards, int B, float* rows, void* workspace, size_t workspace_bytes,
                 void* stream);
+
+/* The forward on lean lanes (engine/inference.py:94-100,130-135, the Rust round loop's wire format): lean_rows uint8
+ * [B, 508], a board's 70 token bytes then 219 int16 (little-endian) answer columns, the legal moves' and, after them,
+ * 1968, the expected score's (engine/selfplay_rs/src/lib.rs:330-333) -> answers fp32 [B, 219], the columns of the board's
+ * answer row, gathered by the heads' last kernel. A column outside [0, 1968] answers 0 and sets the device status
+ * (code 5, where = the board). The workspace holds the forward's scratch and the whole rows. */
+size_t fry_forward_lean_workspace_bytes(const FryNetwork* network, int B);
+int fry_forward_lean(const FryNetwork* network, const uint8_t* lean_rows, int B, float* answers, void* workspace, size_t workspace_bytes,
+                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -119,3 +119,14 @@ def test_int8_model_refuses_fp16_blocks(tmp_path):
         fry_network.int8_model(tmp_path / "model.pt", fp16_blocks=1)
     with pytest.raises(FryError, match="CUDA"):
         fry_network.int8_model(tmp_path / "model.pt", device="cpu")
+
+
+def test_the_lean_row_format_is_the_rust_loops():
+    # engine/selfplay_rs/src/lib.rs:330-333
+    assert (fry_encoding.LEGAL_SLOTS, fry_encoding.LEAN_COLUMNS, fry_encoding.LEAN_ROW) == (218, 219, 508)
+
+
+def test_lean_forward_is_refused_on_the_host_without_a_network(lib):
+    with pytest.raises(FryError, match="needs a network"):
+        lib.fry_forward_lean(None, None, 4, None, None, 0, None)
+    assert lib.fry_forward_lean_workspace_bytes(None, 4) == 0

@@ -7,6 +7,7 @@ import torch
 
 from chess_transformer_b200.boards import random_boards
 from chess_transformer_b200.build import build
+from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
 from chess_transformer_b200.library import library
 from chess_transformer_b200.network import FRY_SETTINGS, Int8Network
 from chess_transformer_b200.runtime import GraphedBatches, small_graph_sizes
@@ -110,3 +111,61 @@ def test_a_token_outside_the_vocabulary_is_reported_not_faulted(fry):
     code, where = lib.device_status(clear=True)
     assert (code, where) == (2, 1) and torch.isfinite(rows).all()
     assert lib.device_status() == (0, 0)
+
+
+def lean_rows(boards: np.ndarray, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """Lean lanes' rows (tokens, then int16 answer columns: a random number of distinct move columns, then the expected
+    score's column as padding, as the Rust loop writes them) and those columns as int64."""
+    rng = np.random.default_rng(seed)
+    rows = np.zeros((len(boards), LEAN_ROW), dtype=np.uint8)
+    rows[:, :TOKENS_PER_BOARD] = boards
+    columns = np.full((len(boards), LEAN_COLUMNS), ANSWER_WIDTH - 1, dtype=np.int16)
+    for b in range(len(boards)):
+        legal = rng.integers(0, LEAN_COLUMNS)
+        columns[b, :legal] = rng.choice(ANSWER_WIDTH - 1, size=legal, replace=False)
+    rows[:, TOKENS_PER_BOARD:] = columns.astype("<i2").view(np.uint8).reshape(len(boards), -1)
+    return rows, columns.astype(np.int64)
+
+
+def test_lean_answers_are_the_rows_gathered_at_their_columns(fry):
+    # engine/inference.py:130-135: a lean lane answers rows.gather(1, columns)
+    network, _ = fry
+    boards = random_boards(37, 8)
+    rows_bytes, columns = lean_rows(boards, 8)
+    with torch.no_grad():
+        whole = network(torch.from_numpy(boards).long().cuda()).cpu()
+        answers = network.forward_lean(torch.from_numpy(rows_bytes).cuda()).cpu()
+    assert answers.shape == (37, LEAN_COLUMNS) and answers.dtype == torch.float32
+    assert torch.equal(answers, whole.gather(1, torch.from_numpy(columns)))
+
+
+def test_lean_graph_lanes_give_the_eager_bits(fry):
+    network, _ = fry
+    boards = random_boards(24, 9)
+    rows_bytes, _ = lean_rows(boards, 9)
+    with torch.no_grad():
+        eager = network.forward_lean(torch.from_numpy(rows_bytes).cuda()).cpu().numpy()
+    batches = GraphedBatches(network, small_graph_sizes(24), in_flight=2, lean=True)
+    with pytest.raises(RuntimeError, match="launch_filled"):
+        batches.launch(boards)
+    lane = batches.free_lane()
+    lane.rows_array[:24] = rows_bytes
+    first = batches.launch_filled(lane, 24)
+    lane = batches.free_lane()
+    lane.rows_array[:10] = rows_bytes[:10]
+    second = batches.launch_filled(lane, 10)
+    assert np.array_equal(batches.collect(first), eager)
+    assert np.array_equal(batches.collect(second), eager[:10])
+
+
+def test_a_lean_column_outside_the_row_is_reported_not_faulted(fry):
+    network, _ = fry
+    lib = library()
+    lib.device_status(clear=True)
+    rows_bytes, _ = lean_rows(random_boards(3, 10), 10)
+    rows_bytes[2, TOKENS_PER_BOARD + 2 * 5:TOKENS_PER_BOARD + 2 * 6] = np.array([ANSWER_WIDTH + 7], dtype="<i2").view(np.uint8)
+    with torch.no_grad():
+        answers = network.forward_lean(torch.from_numpy(rows_bytes).cuda())
+    torch.cuda.synchronize()
+    assert lib.device_status(clear=True) == (5, 2)
+    assert answers[2, 5].item() == 0.0 and torch.isfinite(answers).all()
