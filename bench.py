@@ -28,6 +28,9 @@ sys.path.insert(0, str(ROOT))
 
 BATCH = 256
 LATENCY_BATCH = 64
+# the library's kernels a forward launches: the embedding; per block 2 row norms, projection, attention, attention-out,
+# gate_up, rotate_quant, down (8 x 28); the heads' final norm, f16 GEMM, narrow, policy, 2 x (split, sum), expected score
+LAUNCHES_PER_FORWARD = 1 + 8 * 28 + 9
 FLUSH_BYTES = 256 << 20
 PROFILE_SUMMARY = ROOT / "profiles" / "int8_gemm_traffic.json"
 
@@ -266,6 +269,7 @@ def main() -> None:
     import torch.distributed as dist
     from chess_transformer_b200.boards import random_boards
     from chess_transformer_b200.network import FRY_SETTINGS, Int8Network, quantize, synthetic_state_dict
+    from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
     from chess_transformer_b200.runtime import GraphedBatches
 
     torch.cuda.set_device(local_rank)
@@ -334,6 +338,34 @@ def main() -> None:
         dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
         e2e_seconds = slowest.item()
 
+    # the same through lean lanes, the Rust round loop's format: rows of tokens and answer columns in (30 moves' columns
+    # a board, then the expected score's), 219 answers a board out
+    lean_rows = np.zeros((BATCH, LEAN_ROW), dtype=np.uint8)
+    lean_rows[:, :TOKENS_PER_BOARD] = host_boards
+    columns = np.full((BATCH, LEAN_COLUMNS), ANSWER_WIDTH - 1, dtype="<i2")
+    columns[:, :30] = np.random.default_rng(7 + rank).integers(0, ANSWER_WIDTH - 1, size=(BATCH, 30))
+    lean_rows[:, TOKENS_PER_BOARD:] = columns.view(np.uint8).reshape(BATCH, -1)
+    lean_batches = GraphedBatches(network, [BATCH], in_flight=1, lean=True)
+
+    def lean_step():
+        lane = lean_batches.free_lane()
+        lane.rows_array[:BATCH] = lean_rows
+        lean_batches.collect(lean_batches.launch_filled(lane, BATCH))
+
+    for _ in range(max(3, args.warmup)):
+        lean_step()
+    if world > 1:
+        dist.barrier()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        lean_step()
+    lean_seconds = time.perf_counter() - start
+    if world > 1:
+        slowest = torch.tensor([lean_seconds], device=device)
+        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+        lean_seconds = slowest.item()
+    del lean_batches
+
     extra = {}
     if rank == 0 and not args.no_sweep:
         latencies = []
@@ -366,7 +398,9 @@ def main() -> None:
                 "config": {**workload_config(world), "parallelism": f"replicas x{world}"},
                 "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
                         "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4},
-                "gpu_launches": 231 * args.steps,
+                "e2e_lean": {"value": BATCH * args.steps * world / lean_seconds, "unit": "positions/s",
+                             "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4},
+                "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
                 "forward_int8_tops": round(forward_tops, 1),
                 "roofline": roofline, "clocks": clocks.summary(), **extra}
         if world == 1:
