@@ -83,18 +83,35 @@ int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_
     for (int i = 0; i < n->layers; ++i) {
         const FryBlock& b = n->blocks[i];
         const std::string where = "fry_forward: block " + std::to_string(i);
-        // ln1 (the first block mixes its own input; later ones get it mixed by the previous down)
-        status = i == 0 ? fry::norm_quant(original, original, b.residual_scale, b.input_scale, b.ln1, n->eps, x, q, scale, M, D, s)
-                        : fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln1, n->eps, nullptr, q, scale, M, D, s);
-        if (status != cudaSuccess) return check(status, where + " ln1");
+        const bool fp16 = b.precision == FRY_BLOCK_FP16;
+        // link_input_mixes: a block mixes its own input when first or after a block of the other precision; its down
+        // mixes the next block's when that one is of its own precision
+        const bool mixes_own = i == 0 || n->blocks[i - 1].precision != b.precision;
+        const bool mixes_next = i + 1 < n->layers && n->blocks[i + 1].precision == b.precision;
         const int rows_p = projection_rows(n, b.dq);
         fry::GemmArgs projection;
-        projection.x_scale = scale;
-        projection.w_scale = b.projection_scale;
         projection.bias = b.projection_bias;
         projection.out = projected;
         projection.b_constant = true;
-        status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
+        if (fp16) {
+            // FusedBlock (model/fused_blocks.py:344-354): fp16 norms and linears
+            if (mixes_own) {
+                status = fry::mix_input_f16(i == 0 ? original : x, original, b.residual_scale, b.input_scale, x, M, D, s);
+                if (status != cudaSuccess) return check(status, where + " input mix");
+            }
+            status = fry::rms_norm_f16(x, b.ln1, n->eps, attended, M, D, s);  // attended holds ln1's rows until the attention
+            if (status != cudaSuccess) return check(status, where + " ln1");
+            status = fry::gemm(1, fry::kEpiLinearF16, attended, b.projection, projection, M, rows_p, D, s, &detail);
+        } else {
+            // ln1, mixing the block's own input first where it does
+            status = !mixes_own ? fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln1, n->eps, nullptr, q, scale, M, D, s)
+                                : fry::norm_quant(i == 0 ? original : x, original, b.residual_scale, b.input_scale, b.ln1, n->eps, x, q, scale,
+                                                  M, D, s);
+            if (status != cudaSuccess) return check(status, where + " ln1");
+            projection.x_scale = scale;
+            projection.w_scale = b.projection_scale;
+            status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
+        }
         if (status != cudaSuccess) return check(status, where + " projection", detail);
         status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
                                          n->templates_count, n->eps, s, &detail);
@@ -106,30 +123,38 @@ int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_
         combine.b_constant = true;
         status = fry::gemm(1, fry::kEpiLinearF16, attended, b.combine_heads, combine, M, D, D, s, &detail);
         if (status != cudaSuccess) return check(status, where + " combine_heads", detail);
-        status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
-        if (status != cudaSuccess) return check(status, where + " ln2");
         fry::GemmArgs gate_up;
-        gate_up.x_scale = scale;
-        gate_up.w_scale = b.gate_up_scale;
         gate_up.out = hidden;
         gate_up.b_constant = true;
-        status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
-        if (status != cudaSuccess) return check(status, where + " gate_up", detail);
-        status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
-        if (status != cudaSuccess) return check(status, where + " rotate_quant");
         fry::GemmArgs down;
-        down.x_scale = scale;
-        down.w_scale = b.down_scale;
         down.residual = x;
         down.out = x;
         down.b_constant = true;
-        const bool mixes = i + 1 < n->layers;
-        if (mixes) {
+        if (mixes_next) {
             down.original = original;
             down.residual_scale = n->blocks[i + 1].residual_scale;
             down.input_scale = n->blocks[i + 1].input_scale;
         }
-        status = fry::gemm(0, mixes ? fry::kEpiMix : fry::kEpiResidual, q, b.down, down, M, D, n->down_width, s, &detail);
+        if (fp16) {
+            status = fry::rms_norm_f16(x, b.ln2, n->eps, attended, M, D, s);
+            if (status != cudaSuccess) return check(status, where + " ln2");
+            status = fry::gemm(1, fry::kEpiGatedF16, attended, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
+            if (status != cudaSuccess) return check(status, where + " gate_up", detail);
+            status = fry::gemm(1, mixes_next ? fry::kEpiMixF16 : fry::kEpiLinearF16, hidden, b.down, down, M, D, n->hidden, s, &detail);
+            if (status != cudaSuccess) return check(status, where + " down", detail);
+            continue;
+        }
+        status = fry::norm_quant(x, nullptr, nullptr, nullptr, b.ln2, n->eps, nullptr, q, scale, M, D, s);
+        if (status != cudaSuccess) return check(status, where + " ln2");
+        gate_up.x_scale = scale;
+        gate_up.w_scale = b.gate_up_scale;
+        status = fry::gemm(0, fry::kEpiGated, q, b.gate_up, gate_up, M, n->hidden, D, s, &detail);
+        if (status != cudaSuccess) return check(status, where + " gate_up", detail);
+        status = fry::rotate_quant(hidden, q, scale, M, n->hidden, n->down_width, s);
+        if (status != cudaSuccess) return check(status, where + " rotate_quant");
+        down.x_scale = scale;
+        down.w_scale = b.down_scale;
+        status = fry::gemm(0, mixes_next ? fry::kEpiMix : fry::kEpiResidual, q, b.down, down, M, D, n->down_width, s, &detail);
         if (status != cudaSuccess) return check(status, where + " down", detail);
     }
     const FryHeads& h = n->head_weights;
@@ -272,6 +297,27 @@ int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, cons
     std::string detail;
     return check(fry::gemm(1, out_fp32 ? fry::kEpiLinearF32 : fry::kEpiLinearF16, x, weight, args, M, N, K, as_stream(stream), &detail),
                  "fry_linear", detail);
+}
+
+int fry_linear_full(const uint16_t* x, const uint16_t* weight, const uint16_t* bias, const uint16_t* residual, const uint16_t* original,
+                    const uint16_t* residual_scale, const uint16_t* input_scale, uint16_t* out, int M, int N, int K, int gated, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 8 != 0) return fail(FRY_ERROR_SHAPE, "fry_linear_full takes N and K multiples of 8");
+    if (gated && (residual || original)) return fail(FRY_ERROR_SHAPE, "fry_linear_full's gated form adds no residual and mixes no input");
+    if (original && (!residual || !residual_scale || !input_scale))
+        return fail(FRY_ERROR_SHAPE, "fry_linear_full mixes the next input only with a residual and both scales");
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || (residual && !aligned16(residual)) || (original && !aligned16(original)))
+        return fail(FRY_ERROR_SHAPE, "fry_linear_full needs 16-byte aligned tensors");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.bias = bias;
+    args.residual = residual;
+    args.original = original;
+    args.residual_scale = residual_scale;
+    args.input_scale = input_scale;
+    args.out = out;
+    const int epilogue = gated ? fry::kEpiGatedF16 : original ? fry::kEpiMixF16 : fry::kEpiLinearF16;
+    std::string detail;
+    return check(fry::gemm(1, epilogue, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_linear_full", detail);
 }
 
 int fry_linear_norm_quant(const uint16_t* x, const uint16_t* weight, const uint16_t* bias, const uint16_t* residual, uint16_t* out,

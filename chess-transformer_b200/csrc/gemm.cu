@@ -54,7 +54,9 @@ constexpr int kNormedK = 768, kNormedSlices = kNormedK / kTileKBytes;  // the on
 constexpr int kMaxCluster = 4;  // kEpiLinearNorm: CTAs (column tiles) of a row block, one cluster
 constexpr int kNormBarrier = 2;  // named barrier of the 16 epilogue warps alone
 // fp16 linear epilogues (the bias and the residual optional)
-__host__ __device__ constexpr bool linear16(int epi) { return epi == kEpiLinearF16 || epi == kEpiLinearNorm; }
+__host__ __device__ constexpr bool linear16(int epi) { return epi == kEpiLinearF16 || epi == kEpiLinearNorm || epi == kEpiMixF16; }
+// epilogues that mix the next block's input (residual and original row operands)
+__host__ __device__ constexpr bool mixes(int epi) { return epi == kEpiMix || epi == kEpiMixF16; }
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
@@ -72,7 +74,7 @@ struct GemmShape {
     // fp16 outputs are staged for TMA stores; int32 and fp32 outputs are stored by their threads
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
     // the epilogue's row operands (residual, and original when mixing), loaded into the staging slots
-    static constexpr int kRowTensors = EPI == kEpiMix ? 2 : (EPI == kEpiResidual || linear16(EPI)) ? 1 : 0;
+    static constexpr int kRowTensors = mixes(EPI) ? 2 : (EPI == kEpiResidual || linear16(EPI)) ? 1 : 0;
     // chunks of 16 columns a thread takes in a sub-tile (the 4 warps of a TMEM lane quarter share a sub-tile's chunks)
     static constexpr int kChunksPerSub = SUB / (kChunkCols * kChunkParts) > 0 ? SUB / (kChunkCols * kChunkParts) : 1;
     static constexpr int kSubs = BN / SUB;       // sub-tiles a tile
@@ -119,11 +121,12 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
         float scale = 0.0f, second = 0.0f;
         if constexpr (EPI <= kEpiMix) scale = ok ? p.w_scale[n] : 0.0f;
         if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
-        if constexpr (EPI == kEpiBias || linear16(EPI)) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
+        if constexpr (EPI == kEpiBias || linear16(EPI) || EPI == kEpiGatedF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
         if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
         if constexpr (EPI <= kEpiMix) columns[i] = scale;
         if constexpr (EPI == kEpiLinearNorm) columns[i] = (ok && p.norm_gain) ? h2f_bits(p.norm_gain[n]) : 0.0f;
-        if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32) columns[SECOND + i] = second;
+        if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32 || EPI == kEpiGatedF16)
+            columns[SECOND + i] = second;
     }
 }
 
@@ -132,13 +135,13 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
 template <int EPI, int SUB>
 FRY_DEVICE void load_sub_rows(const CUtensorMap* map_residual, const CUtensorMap* map_original, uint8_t* slot, uint64_t* bar, int m0,
                               int n0, int N) {
-    constexpr int kBoxes = SUB / kBoxCols, kTensors = EPI == kEpiMix ? 2 : 1;
+    constexpr int kBoxes = SUB / kBoxCols, kTensors = mixes(EPI) ? 2 : 1;
     const int in_range = n0 < N ? (N - n0 + kBoxCols - 1) / kBoxCols : 0;
     const int boxes = in_range < kBoxes ? in_range : kBoxes;
     mbar_arrive_expect_tx(bar, boxes * kTensors * kBoxBytes);
     for (int b = 0; b < boxes; ++b) {
         tma_load_2d(slot + b * kBoxBytes, map_residual, bar, n0 + b * kBoxCols, m0);
-        if constexpr (EPI == kEpiMix) tma_load_2d(slot + (kBoxes + b) * kBoxBytes, map_original, bar, n0 + b * kBoxCols, m0);
+        if constexpr (mixes(EPI)) tma_load_2d(slot + (kBoxes + b) * kBoxBytes, map_original, bar, n0 + b * kBoxCols, m0);
     }
 }
 
@@ -178,12 +181,12 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
             }
         return;
     } else {
-        constexpr bool kResidual = EPI == kEpiResidual || EPI == kEpiMix || linear16(EPI);
+        constexpr bool kResidual = EPI == kEpiResidual || mixes(EPI) || linear16(EPI);
         uint4 residual_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, original_words[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if constexpr (kResidual) {
             if (!linear16(EPI) || p.residual != nullptr) residual_words[0] = *staged.at(0), residual_words[1] = *staged.at(1);
         }
-        if constexpr (EPI == kEpiMix) original_words[0] = *original.at(0), original_words[1] = *original.at(1);
+        if constexpr (mixes(EPI)) original_words[0] = *original.at(0), original_words[1] = *original.at(1);
         const uint16_t* res = reinterpret_cast<const uint16_t*>(residual_words);
         const uint16_t* orig = reinterpret_cast<const uint16_t*>(original_words);
         // the chunk's column operands as 4 x float4 each (the chunk starts on a 64-byte boundary of the staged columns)
@@ -194,7 +197,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 const float4 a = reinterpret_cast<const float4*>(scale)[q];
                 scale_v[4 * q] = a.x, scale_v[4 * q + 1] = a.y, scale_v[4 * q + 2] = a.z, scale_v[4 * q + 3] = a.w;
             }
-            if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI)) {
+            if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiGatedF16) {
                 const float4 b = reinterpret_cast<const float4*>(second)[q];
                 second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
             }
@@ -206,14 +209,23 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
             const uint64_t scale2 = pair2(scale_v[e], scale_v[e + 1]), second2 = pair2(second_v[e], second_v[e + 1]);
-            const uint64_t acc2 = pair2(static_cast<float>(static_cast<int32_t>(acc[e])), static_cast<float>(static_cast<int32_t>(acc[e + 1])));
+            // int8: the int32 sums; fp16: the fp32 sums
+            const uint64_t acc2 = EPI <= kEpiMix
+                                      ? pair2(static_cast<float>(static_cast<int32_t>(acc[e])), static_cast<float>(static_cast<int32_t>(acc[e + 1])))
+                                      : pair2(__uint_as_float(acc[e]), __uint_as_float(acc[e + 1]));
             uint64_t value2;
             if constexpr (EPI == kEpiBias) {
                 value2 = fma2(mul2(acc2, xs2), scale2, second2);
-            } else if constexpr (EPI == kEpiGated) {
-                const uint64_t gate2 = mul2(mul2(acc2, xs2), scale2);
-                const uint64_t up2 = mul2(mul2(pair2(static_cast<float>(static_cast<int32_t>(up[e])), static_cast<float>(static_cast<int32_t>(up[e + 1]))), xs2),
-                                          second2);
+            } else if constexpr (EPI == kEpiGated || EPI == kEpiGatedF16) {
+                uint64_t gate2, up2;
+                if constexpr (EPI == kEpiGated) {
+                    gate2 = mul2(mul2(acc2, xs2), scale2);
+                    up2 = mul2(mul2(pair2(static_cast<float>(static_cast<int32_t>(up[e])), static_cast<float>(static_cast<int32_t>(up[e + 1]))), xs2),
+                               second2);
+                } else {  // the bias (zero when there is none) on the gate alone
+                    gate2 = add2(acc2, second2);
+                    up2 = pair2(__uint_as_float(up[e]), __uint_as_float(up[e + 1]));
+                }
                 // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
                 const float2 power = lanes(mul2(gate2, pair2(-1.4426950408889634f, -1.4426950408889634f)));
                 const float2 denominator = lanes(add2(pair2(ex2_approx(power.x), ex2_approx(power.y)), pair2(1.0f, 1.0f)));
@@ -221,16 +233,16 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 value2 = mul2(mul2(gate2, sigmoid2), up2);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
                 value2 = fma2(mul2(acc2, xs2), scale2, pair2(h2f_exact(res[e]), h2f_exact(res[e + 1])));
-                if constexpr (EPI == kEpiMix) {
-                    // the residual sum rounded to fp16, then mixed with the original
-                    const float2 sum = lanes(value2);
-                    const uint32_t stream = pack_half2_rn(sum.x, sum.y);
-                    const uint64_t stream2 = pair2(h2f_exact(static_cast<uint16_t>(stream & 0xffff)), h2f_exact(static_cast<uint16_t>(stream >> 16)));
-                    value2 = fma2(stream2, pair2(rs, rs), mul2(pair2(h2f_exact(orig[e]), h2f_exact(orig[e + 1])), pair2(is, is)));
-                }
-            } else {  // kEpiLinearF16: (acc + bias) + residual
-                value2 = add2(pair2(__uint_as_float(acc[e]), __uint_as_float(acc[e + 1])), second2);
+            } else {  // the fp16 linears: (acc + bias) + residual
+                value2 = add2(acc2, second2);
                 if (p.residual) value2 = add2(value2, pair2(h2f_exact(res[e]), h2f_exact(res[e + 1])));
+            }
+            if constexpr (mixes(EPI)) {
+                // the residual sum rounded to fp16, then mixed with the original
+                const float2 sum = lanes(value2);
+                const uint32_t stream = pack_half2_rn(sum.x, sum.y);
+                const uint64_t stream2 = pair2(h2f_exact(static_cast<uint16_t>(stream & 0xffff)), h2f_exact(static_cast<uint16_t>(stream >> 16)));
+                value2 = fma2(stream2, pair2(rs, rs), mul2(pair2(h2f_exact(orig[e]), h2f_exact(orig[e + 1])), pair2(is, is)));
             }
             const float2 value = lanes(value2);
             values[e] = value.x;
@@ -565,7 +577,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quarter = warp & 3, part = warp >> 2;
         const int row_in_tile = quarter * 32 + lane;
         float rs = 0.0f, is = 0.0f;
-        if constexpr (EPI == kEpiMix) {
+        if constexpr (mixes(EPI)) {
             rs = h2f_bits(*args.residual_scale);
             is = h2f_bits(*args.input_scale);
         }
@@ -760,7 +772,7 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
         if (!make_box_map(&map_out, args.out, N, M, error)) return cudaErrorInvalidValue;
         map_residual = map_original = map_out;
         if (args.residual && !make_box_map(&map_residual, args.residual, N, M, error)) return cudaErrorInvalidValue;
-        if (EPI == kEpiMix && !make_box_map(&map_original, args.original, N, M, error)) return cudaErrorInvalidValue;
+        if (mixes(EPI) && !make_box_map(&map_original, args.original, N, M, error)) return cudaErrorInvalidValue;
     }
     const int row_blocks = (M + kBlockM - 1) / kBlockM, n_blocks = (N + BN - 1) / BN, tiles = row_blocks * n_blocks;
     int device = 0, multiprocessors = 0;
@@ -851,6 +863,13 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 128) return launch<1, 128, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
+            case kEpiGatedF16:
+                if (width >= 128 || tiles(128) >= multiprocessors) return launch<1, 128, true, kEpiGatedF16>(a, b, args, M, N, K, stream, error);
+                return launch<1, 64, true, kEpiGatedF16>(a, b, args, M, N, K, stream, error);
+            case kEpiMixF16:
+                if (width == 256) return launch<1, 192, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<1, 128, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
+                return launch<1, 64, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearNorm:
                 if (N % 256 != 0 || N / 256 > kMaxCluster || !args.norm_q || !args.norm_scale || !args.norm_gain) {
                     if (error) *error = "the norm epilogue takes N a multiple of 256 up to " + std::to_string(256 * kMaxCluster) + " and its outputs";

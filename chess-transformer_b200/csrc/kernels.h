@@ -20,6 +20,9 @@ enum GemmEpilogue : int {
     kEpiLinearF32 = 6,  // fp16: fp32 acc + fp32 bias (optional)
     kEpiLinearNorm = 7, // fp16: as kEpiLinearF16, then norm_quant of each output row into norm_q / norm_scale (a cluster of
                         // the N / 256 CTAs of a row block sums the rows' squares through distributed shared memory)
+    // the fp16 blocks' linears (model/fused_blocks.py:209-225), on fp32 sums:
+    kEpiGatedF16 = 8,   // fp16: fp16((g * sigmoid(g)) * u), weight rows = gate rows then up rows
+    kEpiMixF16 = 9,     // fp16: (acc + bias) + residual rounded to fp16, then fp16(fma(stream, rs, original * is))
 };
 
 struct GemmArgs {
@@ -53,6 +56,10 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
 cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
                        const uint16_t* gain, float eps, uint16_t* mixed, int8_t* q, float* scale, int M, int D, cudaStream_t stream);
 cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream);
+// An fp16 block mixing its own input as torch's fp16 ops do (model/fused_blocks.py:346-347): out = fp16(fp16(rs * x) +
+// fp16(is * original)), elementwise over [M, D]; out may alias x.
+cudaError_t mix_input_f16(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                          uint16_t* out, int M, int D, cudaStream_t stream);
 cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int hidden, int width, cudaStream_t stream);
 // Lean lanes (engine/inference.py:94-100,130-135; engine/selfplay_rs/src/lib.rs:330-333): a board is a row of
 // kLeanRow bytes, its 70 token bytes then kLeanColumns int16 answer columns, and its answer those columns of its row.

@@ -263,6 +263,42 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
     return status;
 }
 
+// 8 fp16 values a thread, grid-stride: the three roundings of torch's fp16 `rs * x + is * original`.
+__global__ void __launch_bounds__(256) mix_input_f16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
+                                                            const uint16_t* __restrict__ residual_scale, const uint16_t* __restrict__ input_scale,
+                                                            uint16_t* out, size_t vectors) {
+    grid_dependency_start();
+    const float rs = h2f_bits(*residual_scale), is = h2f_bits(*input_scale);
+    for (size_t v = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; v < vectors; v += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float a[8], o[8];
+        unpack8(reinterpret_cast<const uint4*>(x)[v], a);
+        unpack8(reinterpret_cast<const uint4*>(original)[v], o);
+        uint32_t words[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            const uint32_t scaled = pack_half2_rn(__fmul_rn(rs, a[i]), __fmul_rn(rs, a[i + 1]));
+            const uint32_t added = pack_half2_rn(__fmul_rn(is, o[i]), __fmul_rn(is, o[i + 1]));
+            words[i / 2] = pack_half2_rn(__fadd_rn(h2f_exact(static_cast<uint16_t>(scaled & 0xffff)), h2f_exact(static_cast<uint16_t>(added & 0xffff))),
+                                         __fadd_rn(h2f_exact(static_cast<uint16_t>(scaled >> 16)), h2f_exact(static_cast<uint16_t>(added >> 16))));
+        }
+        reinterpret_cast<uint4*>(out)[v] = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+}
+
+cudaError_t mix_input_f16(const uint16_t* x, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
+                          uint16_t* out, int M, int D, cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    if (D % 8 != 0) return cudaErrorInvalidValue;
+    const size_t vectors = static_cast<size_t>(M) * D / 8;
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const size_t wanted = (vectors + 255) / 256, most = static_cast<size_t>(multiprocessors) * 8;
+    return launch_dependent(mix_input_f16_kernel, dim3(static_cast<unsigned>(wanted < most ? wanted : most)), dim3(256), 0, stream, x, original,
+                            residual_scale, input_scale, out, vectors);
+}
+
 cudaError_t rms_norm_f16(const uint16_t* x, const uint16_t* gain, float eps, uint16_t* y, int M, int D, cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
     if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;

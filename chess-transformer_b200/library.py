@@ -26,7 +26,9 @@ class FryBlock(ctypes.Structure):
     _fields_ = [("dq", _c_int), ("ln1", _ptr), ("ln2", _ptr), ("residual_scale", _ptr), ("input_scale", _ptr), ("q_gain", _ptr),
                 ("k_gain", _ptr), ("projection", _ptr), ("projection_scale", _ptr), ("projection_bias", _ptr),
                 ("combine_heads", _ptr), ("combine_heads_bias", _ptr), ("gate_up", _ptr), ("gate_up_scale", _ptr), ("down", _ptr),
-                ("down_scale", _ptr)]
+                ("down_scale", _ptr), ("precision", _c_int)]
+
+BLOCK_INT8, BLOCK_FP16 = 0, 1
 
 
 class FryNetwork(ctypes.Structure):
@@ -50,6 +52,7 @@ SIGNATURES = {
     "fry_pair_templates": ([_ptr, _ptr, _c_int, _ptr], _c_int),
     "fry_template_attention": ([_ptr] * 5 + [_c_int] * 6 + [_c_float, _ptr], _c_int),
     "fry_linear": ([_ptr] * 5 + [_c_int] * 4 + [_ptr], _c_int),
+    "fry_linear_full": ([_ptr] * 8 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_linear_norm_quant": ([_ptr] * 6 + [_c_float] + [_ptr] * 2 + [_c_int] * 3 + [_ptr], _c_int),
     "fry_board_embedding": ([_ptr] * 5 + [_c_int, _c_int, _ptr], _c_int),
     "fry_heads_workspace_bytes": ([_c_int, _c_int], _size),

@@ -20,7 +20,7 @@ import torch
 from torch import nn
 
 from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
-from .library import FryBlock, FryError, FryNetwork, library
+from .library import BLOCK_FP16, BLOCK_INT8, FryBlock, FryError, FryNetwork, library
 from .ops import heads_struct, pair_templates
 
 FP16_RESIDUAL_SCALE = 1 / 16      # engine/inference.py:239
@@ -55,6 +55,9 @@ def hadamard(size: int) -> torch.Tensor:
     while matrix.shape[0] < size:
         matrix = torch.cat([torch.cat([matrix, matrix], 1), torch.cat([matrix, -matrix], 1)], 0)
     return matrix
+
+
+FP16_LAST_LAYERS = 1  # engine/quantization.py:46: the blocks at the end that stay fp16
 
 
 def down_inputs(hidden: int) -> int:
@@ -117,7 +120,8 @@ def _pointer(tensor: torch.Tensor) -> int:
 
 
 class Int8Network(nn.Module):
-    """Fry's network with every block in int8, on one GPU. forward(boards [B, 70] int64 cuda) -> rows [B, 1969] fp32."""
+    """Fry's network on one GPU, its blocks int8 where `weights` has them and fp16 otherwise (the reference's int8_model
+    layout). forward(boards [B, 70] int64 cuda) -> rows [B, 1969] fp32."""
 
     def __init__(self, state: dict, settings: dict, weights: dict, device: torch.device | str | None = None):
         super().__init__()
@@ -127,10 +131,8 @@ class Int8Network(nn.Module):
         if device.index is None:
             device = torch.device("cuda", torch.cuda.current_device())
         g = geometry(settings)
-        missing = [layer for layer in range(g["layers"]) if layer not in weights]
-        if missing:
-            raise FryError(f"Int8Network runs every block in int8; no int8 weights for blocks {missing} "
-                           "(the reference keeps those blocks in fp16, which this engine does not run)")
+        # the blocks without int8 weights run in fp16, as the reference's quantize_blocks keeps them (FusedBlock,
+        # model/int8_blocks.py:292-298): the engine's layout keeps the last block and ENGINE_FP16_BLOCKS more in fp16
         self.settings, self.geometry, self.d_model, self.eps = settings, g, g["d"], EPS
         s = FP16_RESIDUAL_SCALE
         half = lambda t: t.detach().to(device=device, dtype=torch.float16).contiguous()
@@ -141,19 +143,28 @@ class Int8Network(nn.Module):
         self.blocks = []
         for i, dq in enumerate(g["dqs"]):
             p = f"encoder.{i}."
-            w = weights[i]
-            width = w["down"][0].shape[1]
             block = {"ln1": half(state[p + "ln1.weight"]), "ln2": half(state[p + "ln2.weight"]),
                      "residual_scale": half(state[p + "residual_scale"]), "input_scale": half(state[p + "input_scale"]),
                      "q_gain": half(state[p + "q_norm.weight"]), "k_gain": half(state[p + "k_norm.weight"]),
-                     "projection": w["projection"][0].to(device).contiguous(), "projection_scale": single(w["projection"][1]),
                      "projection_bias": half(torch.cat([state[p + n + ".bias"] for n in ("Q", "K", "V", "template_mix")])),
                      "combine_heads": half(state[p + "combine_heads.weight"].float() * s),
-                     "combine_heads_bias": half(state[p + "combine_heads.bias"].float() * s),
-                     "gate_up": w["gate_up"][0].to(device).contiguous(), "gate_up_scale": single(w["gate_up"][1]),
-                     "down": w["down"][0].to(device).contiguous(), "down_scale": single(w["down"][1].float() * s)}
-            if width != down_inputs(g["hidden"]):
-                raise FryError(f"block {i}'s down takes {width} inputs, not the padded hidden width {down_inputs(g['hidden'])}")
+                     "combine_heads_bias": half(state[p + "combine_heads.bias"].float() * s)}
+            if i in weights:
+                w = weights[i]
+                width = w["down"][0].shape[1]
+                if width != down_inputs(g["hidden"]):
+                    raise FryError(f"block {i}'s down takes {width} inputs, not the padded hidden width {down_inputs(g['hidden'])}")
+                block.update({"precision": BLOCK_INT8, "projection": w["projection"][0].to(device).contiguous(),
+                              "projection_scale": single(w["projection"][1]), "gate_up": w["gate_up"][0].to(device).contiguous(),
+                              "gate_up_scale": single(w["gate_up"][1]), "down": w["down"][0].to(device).contiguous(),
+                              "down_scale": single(w["down"][1].float() * s)})
+            else:
+                # FusedBlock's weights in nn.Linear's [out, in] layout (the reference keeps them transposed), the down
+                # scaled into the stream's 1/16 before the fp16 rounding as scale_residual_stream does (model/model.py:235-243)
+                block.update({"precision": BLOCK_FP16,
+                              "projection": half(torch.cat([state[p + n + ".weight"] for n in ("Q", "K", "V", "template_mix")])),
+                              "gate_up": half(torch.cat([state[p + "mlp.gate_projection.weight"], state[p + "mlp.up_projection.weight"]])),
+                              "down": half(state[p + "mlp.down_projection.weight"].float() * s)})
             self.blocks.append(block)
         # heads (model/fused_blocks.py:815-824), folded in fp64
         from_w, from_b = state["from_projection.weight"].double(), state["from_projection.bias"].double()
@@ -178,10 +189,11 @@ class Int8Network(nn.Module):
         g, t = self.geometry, self.tensors
         blocks = (FryBlock * len(self.blocks))()
         for i, (dq, b) in enumerate(zip(g["dqs"], self.blocks)):
-            blocks[i] = FryBlock(dq, *(_pointer(b[name]) for name in ("ln1", "ln2", "residual_scale", "input_scale", "q_gain", "k_gain",
-                                                                      "projection", "projection_scale", "projection_bias", "combine_heads",
-                                                                      "combine_heads_bias", "gate_up", "gate_up_scale", "down",
-                                                                      "down_scale")))
+            pointer = lambda name: _pointer(b[name]) if name in b else None
+            blocks[i] = FryBlock(dq, *(pointer(name) for name in ("ln1", "ln2", "residual_scale", "input_scale", "q_gain", "k_gain",
+                                                                  "projection", "projection_scale", "projection_bias", "combine_heads",
+                                                                  "combine_heads_bias", "gate_up", "gate_up_scale", "down", "down_scale")),
+                                 b["precision"])
         self._blocks_array = blocks
         return FryNetwork(g["d"], g["layers"], g["heads"], g["kv_heads"], g["dv"], g["templates"], g["hidden"], down_inputs(g["hidden"]),
                           self.eps, _pointer(t["embed"]), _pointer(t["position"]), _pointer(t["table"]), _pointer(t["templates"]),
@@ -235,12 +247,14 @@ def load_checkpoint(checkpoint_path: Path) -> tuple[dict, dict]:
 
 
 def int8_model(checkpoint_path: Path, fp16_blocks: int = 0, weights: dict | None = None, device: torch.device | str | None = None) -> Int8Network:
-    """`engine.inference.int8_model` (engine/inference.py:267-272) on this engine. `weights` are Int8Weights (the reference's
-    cached GPTQ weights load unchanged); None rounds the checkpoint's weights to nearest. Every block must be int8:
-    fp16_blocks > 0, or weights missing a block, are refused (the reference runs those blocks in fp16)."""
-    if fp16_blocks:
-        raise FryError("this engine runs every block in int8: fp16_blocks must be 0")
+    """`engine.inference.int8_model` (engine/inference.py:267-272) on this engine: the blocks `weights` has run in int8,
+    the others in fp16. `weights` are Int8Weights (the reference's cached GPTQ weights load unchanged, their blocks
+    fixing the layout); None rounds every block but the last (FP16_LAST_LAYERS, engine/quantization.py:46,128) to
+    nearest. Choosing fp16_blocks > 0 more blocks needs the reference's calibration (block_errors,
+    engine/quantization.py:148-172): with weights None it is refused."""
+    if fp16_blocks and weights is None:
+        raise FryError("choosing fp16_blocks needs the reference's calibration: pass its cached weights, which leave those blocks out")
     state, settings = load_checkpoint(Path(checkpoint_path))
     if weights is None:
-        weights = quantize(state, settings)
+        weights = quantize(state, settings, list(range(geometry(settings)["layers"] - FP16_LAST_LAYERS)))
     return Int8Network(state, settings, weights, device)

@@ -199,13 +199,26 @@ def _(projected, templates, q_gain, k_gain, heads, kv_heads, dq, dv, templates_c
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
            gated: bool = False, accumulate_fp32: bool = False, original: torch.Tensor | None = None,
            residual_scale: torch.Tensor | None = None, input_scale: torch.Tensor | None = None) -> torch.Tensor:
-    """`chess::linear` (model/fused_blocks.py:308-313) for fp16 x and weight [K, N] as the reference stores it: fp32
-    accumulation (the reference accumulates fp16 inputs in fp16 unless accumulate_fp32), fp16 out, or fp32 out with
-    accumulate_fp32. The gated and input-mixing forms belong to the fp16 blocks, which this engine does not run."""
-    _cuda("linear", x, weight, bias, residual)
-    if gated or original is not None:
-        raise FryError("fry::linear has no gated or input-mixing epilogue: those serve the reference's fp16 blocks")
+    """`chess::linear` (model/fused_blocks.py:308-313) for fp16 x and weight [K, N] as the reference stores it ([K, 2N],
+    gate columns then up columns, gated): fp32 accumulation (the reference accumulates fp16 inputs in fp16 unless
+    accumulate_fp32), fp16 out, or fp32 out with accumulate_fp32; the gated and input-mixing forms (the fp16 blocks')
+    in fp16."""
+    _cuda("linear", x, weight, bias, residual, original, residual_scale, input_scale)
     _dtype("linear", x, torch.float16, "x")
+    if gated or original is not None:  # the fp16 blocks' forms (fp16 out)
+        if accumulate_fp32:
+            raise FryError("fry::linear gives its gated and input-mixing forms in fp16 only")
+        K, width = weight.shape
+        N = width // 2 if gated else width
+        x = x.contiguous()
+        M = x.numel() // K
+        out = x.new_empty(*x.shape[:-1], N, dtype=torch.float16)
+        bias = bias.half().contiguous() if bias is not None else None
+        residual = residual.contiguous() if residual is not None else None
+        original = original.contiguous() if original is not None else None
+        library().fry_linear_full(_ptr(x), _ptr(weight.t().contiguous()), _ptr(bias), _ptr(residual), _ptr(original), _ptr(residual_scale),
+                                  _ptr(input_scale), _ptr(out), M, N, K, int(gated), _stream(x))
+        return out
     K, N = weight.shape
     x = x.contiguous()
     M = x.numel() // K
@@ -220,7 +233,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 @linear.register_fake
 def _(x, weight, bias=None, residual=None, gated=False, accumulate_fp32=False, original=None, residual_scale=None, input_scale=None):
-    return x.new_empty(*x.shape[:-1], weight.shape[1], dtype=torch.float32 if accumulate_fp32 else x.dtype)
+    return x.new_empty(*x.shape[:-1], weight.shape[1] // 2 if gated else weight.shape[1], dtype=torch.float32 if accumulate_fp32 else x.dtype)
 
 
 @torch.library.custom_op("fry::linear_norm_quant", mutates_args=())

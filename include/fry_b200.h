@@ -94,6 +94,14 @@ int fry_template_attention(const uint16_t* projected, const uint16_t* paired_tem
 int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, const uint16_t* residual, void* out, int M, int N, int K,
                int out_fp32, void* stream);
 
+/* `chess::linear` (model/fused_blocks.py:308-313, epilogue :209-225) with every fp16 form the fp16 blocks use:
+ * out[M, N] fp16 from fp32 sums acc = x . weight^T, then gated != 0: fp16((g * sigmoid(g)) * u), g = acc + bias over
+ * weight rows [0, N), u over rows [N, 2N) (weight [2N, K]); else (acc + bias) + residual, and with original (and both
+ * scales) the sum rounded to fp16 then fp16(fma(stream, *residual_scale, original * *input_scale)). bias, residual and
+ * original may be NULL (original needs residual); out may alias residual. N a multiple of 8, K of 8. */
+int fry_linear_full(const uint16_t* x, const uint16_t* weight, const uint16_t* bias, const uint16_t* residual, const uint16_t* original,
+                    const uint16_t* residual_scale, const uint16_t* input_scale, uint16_t* out, int M, int N, int K, int gated, void* stream);
+
 /* `chess::linear` (fp16, as fry_linear) feeding `chess::norm_quant` (model/int8_blocks.py:191-193) in one kernel, the pair
  * `Int8Block.forward` runs for attention-out -> ln2 (model/int8_blocks.py:274-288): out[M, N] fp16 = (x . weight^T + bias)
  * + residual, then q[M, N] int8 and scale[M] fp32 of RMSNorm(out) * gain. The N / 256 CTAs that share a 128-row block
@@ -146,7 +154,12 @@ int fry_heads_noalloc(const uint16_t* stream_x, const FryHeads* heads, float eps
 
 /* ---- the whole forward ------------------------------------------------------------------------------------------- */
 
-/* One int8 block as `Int8Block` holds it (model/int8_blocks.py:254-272) with the layout of engine/quantization.py:129-139. */
+/* One block: an int8 block as `Int8Block` holds it (model/int8_blocks.py:254-272) with the layout of
+ * engine/quantization.py:129-139, or (precision FRY_BLOCK_FP16) an fp16 block as `FusedBlock` runs it
+ * (model/fused_blocks.py:325-354), whose projection, gate_up and down are fp16 in nn.Linear's [out, in] layout, the down
+ * [D, hidden] times the stream's 1/16, and whose scales are unused. */
+#define FRY_BLOCK_INT8 0
+#define FRY_BLOCK_FP16 1
 typedef struct FryBlock {
     int dq;
     const uint16_t* ln1;                 /* fp16 [D] */
@@ -155,19 +168,21 @@ typedef struct FryBlock {
     const uint16_t* input_scale;         /* fp16 [1] */
     const uint16_t* q_gain;              /* fp16 [dq] */
     const uint16_t* k_gain;              /* fp16 [dq] */
-    const int8_t* projection;            /* int8 [36*dq + 576 (generally heads*dq + kv*dq + kv*dv + heads*templates), D] */
+    const void* projection;              /* int8 (fp16) [36*dq + 576 (generally heads*dq + kv*dq + kv*dv + heads*templates), D] */
     const float* projection_scale;       /* fp32 [rows of projection] */
     const uint16_t* projection_bias;     /* fp16 [rows of projection] */
     const uint16_t* combine_heads;       /* fp16 [D, D], row n = output column n (the reference's [K, N] transposed) */
     const uint16_t* combine_heads_bias;  /* fp16 [D] */
-    const int8_t* gate_up;               /* int8 [2*hidden, D], gate rows then up rows */
+    const void* gate_up;                 /* int8 (fp16) [2*hidden, D], gate rows then up rows */
     const float* gate_up_scale;          /* fp32 [2*hidden] */
-    const int8_t* down;                  /* int8 [D, width], padded and Hadamard-rotated */
+    const void* down;                    /* int8 [D, width], padded and Hadamard-rotated (fp16 [D, hidden]) */
     const float* down_scale;             /* fp32 [D], times the stream's 1/16 */
+    int precision;                       /* FRY_BLOCK_INT8 or FRY_BLOCK_FP16 */
 } FryBlock;
 
-/* The int8 network: FusedTransformer with every block an Int8Block (model/fused_blocks.py:829-878,
- * model/int8_blocks.py:292-298), each down mixing the next block's input (link_input_mixes, model/fused_blocks.py:358-363).
+/* The network: FusedTransformer with its blocks int8 (Int8Block) or fp16 (FusedBlock) (model/fused_blocks.py:829-878,
+ * model/int8_blocks.py:292-298), a down mixing the next block's input when both are of one precision, a block after one
+ * of the other precision mixing its own (link_input_mixes, model/fused_blocks.py:358-363).
  * This struct and the blocks array live in host memory; every tensor pointer in them is a device pointer. */
 typedef struct FryNetwork {
     int d_model, layers, heads, kv_heads, dv, templates_count, hidden, down_width;

@@ -178,6 +178,33 @@ def test_fp16_linear_is_the_oracle(M, N, K):
     assert found32.dtype == torch.float32 and torch.allclose(found32, exact, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("M", [70, 4480, 17920])
+def test_fp16_gated_and_mixing_linears_are_their_fp32_epilogues(M):
+    # the fp16 blocks' forms (model/fused_blocks.py:209-225): the reference's epilogue in fp32 on exact (fp64) sums
+    g = torch.Generator().manual_seed(M)
+    K, hidden, D = 768, 992, 768
+    x = torch.randn(M, K, generator=g).half()
+    gate_up = (torch.randn(K, 2 * hidden, generator=g) / 16).half()
+    bias = (torch.randn(hidden, generator=g) / 4).half()
+    hidden_out = ops.linear(x.cuda(), gate_up.cuda(), bias.cuda(), gated=True).cpu()
+    sums = x.double() @ gate_up.double()
+    gate, up = (sums[:, :hidden] + bias.double()).float(), sums[:, hidden:].float()
+    expected = (gate * torch.sigmoid(gate) * up).half()
+    # fp32 sums in another order and the sigmoid from the 2^x instruction: within an fp16 step and a little absolute slack
+    assert ((hidden_out.float() - expected.float()).abs() <= expected.float().abs() * 2 ** -10 + 1e-4).all()
+
+    h = (torch.randn(M, hidden, generator=g) / 2).half()
+    down = (torch.randn(hidden, D, generator=g) / 32).half()
+    residual, original = torch.randn(M, D, generator=g).half(), torch.randn(M, D, generator=g).half()
+    scales = torch.tensor([0.8, 0.5]).half()
+    mixed = ops.linear(h.cuda(), down.cuda(), None, residual.cuda(), original=original.cuda(), residual_scale=scales[:1].cuda(),
+                       input_scale=scales[1:].cuda()).cpu()
+    stream = ((h.double() @ down.double()).float() + residual.float()).half().float()
+    rs, is_ = scales.float()
+    expected = (rs * stream + is_ * original.float()).half()
+    assert ((mixed.float() - expected.float()).abs() <= expected.float().abs() * 2 ** -9 + 2e-3).all()
+
+
 def test_combine_linear_is_the_references_within_its_fp16_accumulation(golden):
     found = ops.linear(t(golden["combine_x"]), t(golden["combine_w"]), t(golden["combine_b"]), t(golden["combine_residual"])).cpu()
     assert (found.float() - torch.from_numpy(golden["combine_out"]).float()).abs().max() <= 8e-3

@@ -113,9 +113,9 @@ def test_the_synthetic_checkpoint_loads_into_the_oracles_shapes():
     assert all(tuple(state[name].shape) == shape for name, shape in shapes.items())
 
 
-def test_int8_model_refuses_fp16_blocks(tmp_path):
+def test_int8_model_needs_the_references_weights_to_choose_fp16_blocks(tmp_path):
     torch.save({"model_settings": SMALL, "state_dict": om.seeded_state_dict(SMALL, 0)}, tmp_path / "model.pt")
-    with pytest.raises(FryError, match="int8"):
+    with pytest.raises(FryError, match="calibration"):
         fry_network.int8_model(tmp_path / "model.pt", fp16_blocks=1)
     with pytest.raises(FryError, match="CUDA"):
         fry_network.int8_model(tmp_path / "model.pt", device="cpu")

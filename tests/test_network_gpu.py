@@ -58,6 +58,23 @@ def test_the_network_computes_what_the_fp32_model_does(golden):
     assert torch.allclose(rows[:, -1], om.expected_score(values), atol=5e-3)
 
 
+def test_the_references_layout_with_an_fp16_last_block_is_its_int8_model(golden):
+    # engine/inference.py:265-272: every block int8 but the last, which runs as the fp16 FusedBlock
+    # (model/fused_blocks.py:325-354); the reference's fp16 linears accumulate in fp16, these in fp32
+    state = om.seeded_state_dict(SMALL, 10)
+    layers = SMALL["num_layers"]
+    weights = {layer: w for layer, w in oi.int8_weights(state, SMALL).items() if layer < layers - 1}
+    network = Int8Network(state, SMALL, weights)
+    assert [b["precision"] for b in network.blocks] == [0] * (layers - 1) + [1]
+    boards = torch.from_numpy(golden["fp32_boards"][:4]).long()
+    with torch.no_grad():
+        rows = network(boards.cuda()).cpu()
+    logits = torch.from_numpy(golden["int8_small_layout_logits"])
+    values = torch.from_numpy(golden["int8_small_layout_values"])
+    assert (rows[:, :-1] - logits).abs().max() <= LOGIT_TOLERANCE
+    assert (rows[:, -1] - om.expected_score(values)).abs().max() <= SCORE_TOLERANCE
+
+
 @pytest.fixture(scope="module")
 def fry():
     return network_and_oracle(FRY_SETTINGS, 1, std=0.02, template_std=0.02, table_std=0.02)
@@ -169,3 +186,20 @@ def test_a_lean_column_outside_the_row_is_reported_not_faulted(fry):
     torch.cuda.synchronize()
     assert lib.device_status(clear=True) == (5, 2)
     assert answers[2, 5].item() == 0.0 and torch.isfinite(answers).all()
+
+
+def test_fry_with_fp16_blocks_inside_and_last_runs_the_transitions(fry):
+    # the engine's 26 + 2 layout: an fp16 block between int8 ones (each mixing its own input, link_input_mixes) and the
+    # last; the fp16 blocks are the more exact, so the answers stay within int8's noise of the all-int8 network's
+    network, _ = fry
+    state = om.seeded_state_dict(FRY_SETTINGS, 1, std=0.02, template_std=0.02, table_std=0.02)
+    weights = {layer: w for layer, w in oi.int8_weights(state, FRY_SETTINGS).items() if layer not in (13, 27)}
+    mixed = Int8Network(state, FRY_SETTINGS, weights)
+    assert [i for i, b in enumerate(mixed.blocks) if b["precision"] == 1] == [13, 27]
+    boards = torch.from_numpy(random_boards(8, 12)).long().cuda()
+    with torch.no_grad():
+        ours, int8 = mixed(boards).cpu(), network(boards).cpu()
+        alone = mixed(boards[[5]]).cpu()
+    assert torch.isfinite(ours).all()
+    assert (ours[:, :-1] - int8[:, :-1]).abs().max() <= 0.1 and (ours[:, -1] - int8[:, -1]).abs().max() <= 0.02
+    assert torch.equal(alone, ours[[5]])  # an answer does not depend on its batch here either
