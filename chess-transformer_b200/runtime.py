@@ -46,6 +46,7 @@ class Lane:
             self.boards_host = torch.zeros(largest, TOKENS_PER_BOARD, dtype=torch.long, pin_memory=True)
             self.boards_array = self.boards_host.numpy()
         self.answers_host = torch.zeros(largest, LEAN_COLUMNS if lean else ANSWER_WIDTH, dtype=torch.float32, pin_memory=True)
+        self.answers_array = self.answers_host.numpy()
         self.done = torch.cuda.Event(blocking=True)
         answer = (lambda size: model.forward_lean(self.rows[:size])) if lean else (lambda size: model(self.boards[:size]))
         self.stream.wait_stream(torch.cuda.current_stream())
@@ -59,8 +60,16 @@ class Lane:
             self.graphs[size] = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graphs[size], pool=self.pool, stream=self.stream), torch.no_grad():
                 self.answers[size] = answer(size)
-        self.done.record(self.stream)
+        self.done.record(self.stream)  # the event's handle exists from its first record
         self.done.synchronize()
+
+    def handles(self) -> dict:
+        """The raw handles a caller outside Python replays the lane with (engine/inference.py:138-142): the device, the
+        stream and done event, the rows' pinned and device buffers, the answers' pinned buffer, and for each size its graph's
+        executable and answers on the device."""
+        return {"device": self.device, "stream": self.stream.cuda_stream, "done": self.done.cuda_event,
+                "rows_host": self.rows_host.data_ptr(), "rows": self.rows.data_ptr(), "answers_host": self.answers_host.data_ptr(),
+                "graphs": {size: (graph.raw_cuda_graph_exec(), self.answers[size].data_ptr()) for size, graph in self.graphs.items()}}
 
 
 class GraphedBatches:
@@ -70,6 +79,14 @@ class GraphedBatches:
     def __init__(self, model: nn.Module, sizes: list[int], in_flight: int = 2, blocking_wait: bool = False, lean: bool = False):
         self.model, self.sizes, self.blocking_wait, self.lean = model, sizes, blocking_wait, lean
         self.lanes = [Lane(model, sizes, lean) for _ in range(in_flight)]
+        self.handles = {id(lane): lane.handles() for lane in self.lanes} if lean else {}
+
+    def rust_network(self) -> dict:
+        """engine/inference.py:207-211: what the Rust round loop (Searches) replays the lean lanes with, no Python between
+        rounds; it calls the CUDA runtime by these handles as it does the reference's lanes."""
+        if not self.lean:
+            raise ValueError("Searches' round loop needs lean lanes")
+        return {"blocking_wait": self.blocking_wait, "lanes": [self.handles[id(lane)] for lane in self.lanes]}
 
     def free_lane(self) -> Lane:
         lane = next((lane for lane in self.lanes if not lane.pending), None)

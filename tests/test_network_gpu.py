@@ -203,3 +203,29 @@ def test_fry_with_fp16_blocks_inside_and_last_runs_the_transitions(fry):
     assert torch.isfinite(ours).all()
     assert (ours[:, :-1] - int8[:, :-1]).abs().max() <= 0.1 and (ours[:, -1] - int8[:, -1]).abs().max() <= 0.02
     assert torch.equal(alone, ours[[5]])  # an answer does not depend on its batch here either
+
+
+def test_lean_lanes_replay_by_their_raw_handles_as_the_rust_loop_does(fry):
+    # the Rust round loop's calls (engine/inference.py:175-205 spells them out in Python): copy the rows in, launch the
+    # size's graph executable on the lane's stream, record done, copy the answers out, all by raw handle through cudart
+    import ctypes, os
+    network, _ = fry
+    boards = random_boards(16, 13)
+    rows_bytes, _ = lean_rows(boards, 13)
+    batches = GraphedBatches(network, [8, 16], in_flight=1, lean=True)
+    lane = batches.free_lane()
+    lane.rows_array[:16] = rows_bytes
+    expected = batches.collect(batches.launch_filled(lane, 16)).copy()
+    handles = batches.rust_network()["lanes"][0]
+    cudart = ctypes.CDLL(f"libcudart.so.{torch.version.cuda.split('.')[0]}", mode=os.RTLD_NOLOAD | os.RTLD_LAZY)
+    memcpy, launch, record, sync = cudart.cudaMemcpyAsync, cudart.cudaGraphLaunch, cudart.cudaEventRecord, cudart.cudaStreamSynchronize
+    memcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    launch.argtypes, record.argtypes, sync.argtypes = [ctypes.c_void_p] * 2, [ctypes.c_void_p] * 2, [ctypes.c_void_p]
+    lane.answers_array[:] = 0
+    executable, answers = handles["graphs"][16]
+    assert memcpy(handles["rows"], handles["rows_host"], 16 * LEAN_ROW, 1, handles["stream"]) == 0
+    assert launch(executable, handles["stream"]) == 0
+    assert record(handles["done"], handles["stream"]) == 0
+    assert memcpy(handles["answers_host"], answers, 16 * LEAN_COLUMNS * 4, 2, handles["stream"]) == 0
+    assert sync(handles["stream"]) == 0
+    assert np.array_equal(lane.answers_array[:16], expected)
