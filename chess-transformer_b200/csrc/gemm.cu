@@ -85,7 +85,8 @@ struct GemmShape {
     // one slot holds a sub-tile's row operands (the output overwrites the first) or, without row operands, its output;
     // there are two, so the next sub-tile's operands load, and the last one's stores drain, while one is worked on
     static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kBoxes * kBoxBytes : 0;
-    static constexpr int kSlots = 2;
+    // the mix's two row operands a sub-tile take three slots, so their loads run two sub-tiles ahead of the one staged
+    static constexpr int kSlots = mixes(EPI) ? 3 : 2;
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
     // (the mix and residual epilogues use the scales alone, the fp16 linears the bias alone: one array)
@@ -387,8 +388,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* empty = full + S::kStages;
     uint64_t* tmem_full = empty + S::kStages;   // [2]: an accumulator is ready for the epilogue
     uint64_t* tmem_empty = tmem_full + 2;       // [2]: the epilogue has read an accumulator out
-    uint64_t* rows_full = tmem_empty + 2;       // [2]: a slot's row operands have landed
-    uint64_t* a_ready = rows_full + 2;          // a normed A's block is in place (all epilogue warps)
+    uint64_t* rows_full = tmem_empty + 2;       // [kSlots]: a slot's row operands have landed
+    uint64_t* a_ready = rows_full + 3;          // a normed A's block is in place (all epilogue warps)
     uint64_t* xready = a_ready + 1;             // [2]: every rank's row partials of a tile have arrived (kEpiLinearNorm)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xready + 2);
 
@@ -433,8 +434,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
             mbar_init(&tmem_empty[b], kEpilogueWarps);
-            mbar_init(&rows_full[b], 1);
         }
+        for (int b = 0; b < S::kSlots; ++b) mbar_init(&rows_full[b], 1);
         mbar_init(a_ready, kEpilogueWarps);
         for (int b = 0; b < 2; ++b) mbar_init(&xready[b], EPI == kEpiLinearNorm ? n_blocks * 4 : 1);  // 4 warps a rank
         fence_barrier_init();
@@ -531,9 +532,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     } else if (warp == kStoreWarp) {
-        // the staged sub-tiles' TMA traffic: after sub-tile j's barrier, its stores from slot j % 2; once they have read
-        // the slot, the row operands of sub-tile j + 2 into it (those of sub-tiles 0 and 1 first). Waiting for the reads
-        // before the next barrier also frees the slot for sub-tile j + 2's outputs.
+        // the staged sub-tiles' TMA traffic: after sub-tile j's barrier, its stores from slot j % kSlots; once they have
+        // read the slot, the row operands of sub-tile j + kSlots into it (those of the first kSlots sub-tiles first).
+        // Waiting for the reads before the next barrier also frees the slot for sub-tile j + kSlots's outputs.
         if constexpr (S::kStaged) {
             const bool has_rows = S::kRowTensors > 0 && (!linear16(EPI) || args.residual != nullptr);
             const bool issuer = lane == 0;
@@ -542,16 +543,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 load_sub_rows<EPI, SUB>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
                                         (tile / n_blocks) * kBlockM, column0(tile) + sub * SUB, N);
             };
-            int ahead_tile = first_tile, ahead_sub = 0;  // the sub-tile two ahead of the one being stored
-            load_rows(ahead_tile, ahead_sub, 0);
-            advance(ahead_tile, ahead_sub);
-            load_rows(ahead_tile, ahead_sub, 1);
-            advance(ahead_tile, ahead_sub);
+            int ahead_tile = first_tile, ahead_sub = 0;  // the sub-tile kSlots ahead of the one being stored
+            for (int slot = 0; slot < S::kSlots; ++slot) {
+                load_rows(ahead_tile, ahead_sub, slot);
+                advance(ahead_tile, ahead_sub);
+            }
             epilogue_sync();  // the first tile's column operands are staged
             int j = 0;
             for (int tile = first_tile; tile < tiles; tile = next_tile(tile)) {
                 for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
-                    const int slot = j & 1;
+                    const int slot = j % S::kSlots;
                     __syncwarp();
                     epilogue_sync();  // sub-tile j is staged
                     if (issuer) {
@@ -631,10 +632,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float squares = 0.0f, largest = 0.0f;
 #pragma unroll(EPI == kEpiLinearNorm ? S::kSubs : 1)
             for (int sub = 0; sub < S::kSubs; ++sub, ++j) {
-                // sub-tile j stages into slot j % 2, which the stores of sub-tile j - 2 had read before the barrier that ended
+                // sub-tile j stages into slot j % kSlots, which the stores of sub-tile j - kSlots had read before the barrier that ended
                 // sub-tile j - 1; every thread waits for the row operands, alive or not, so none is in flight when the CTA exits
-                const int slot = j & 1;
-                if (has_rows && !mbar_wait(&rows_full[slot], (j >> 1) & 1, 14)) alive = false;
+                const int slot = j % S::kSlots;
+                if (has_rows && !mbar_wait(&rows_full[slot], (j / S::kSlots) & 1, 14)) alive = false;
                 uint8_t* staged_sub = io + slot * S::kSlotBytes;
                 if (alive) {
                     tc_fence_after();
