@@ -72,18 +72,28 @@ class ClockSampler:
         self.samples, self.max_mhz, self.source = [], None, None
         self.stop = threading.Event()
         self.thread = self.process = self.file = None
+        self.nvml = self.handle = None
 
-    def _poll(self, nvml, handle):
+    def _read(self, nvml, handle):
         reasons = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown, "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
                    "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown, "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+        try:
+            mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+            mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+            self.samples.append((float(mhz), sorted(name for name, bit in reasons.items() if mask & bit)))
+        except Exception:
+            pass
+
+    def _poll(self, nvml, handle):
         while not self.stop.is_set():
-            try:
-                mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
-                mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                self.samples.append((float(mhz), sorted(name for name, bit in reasons.items() if mask & bit)))
-            except Exception:
-                pass
+            self._read(nvml, handle)
             self.stop.wait(0.005)
+
+    def sample_now(self) -> None:
+        """One reading from the calling thread (the timed loop calls it after enqueueing each step, while the GPU runs the
+        steps before): the polling thread may get few turns while the loop holds the interpreter."""
+        if self.nvml is not None:
+            self._read(self.nvml, self.handle)
 
     def __enter__(self):
         try:
@@ -93,9 +103,10 @@ class ClockSampler:
             index = int(visible.split(",")[self.device_index]) if visible and visible.split(",")[0].isdigit() else self.device_index
             handle = nvml.nvmlDeviceGetHandleByIndex(index)
             self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+            self.nvml, self.handle = nvml, handle
             self.thread = threading.Thread(target=self._poll, args=(nvml, handle), daemon=True)
             self.thread.start()
-            self.source = "nvml, every 5 ms"
+            self.source = "nvml, every 5 ms and once a step as it is enqueued"
         except Exception:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             try:
@@ -312,6 +323,7 @@ def main() -> None:
             start.record(stream)
             graph.replay()
             end.record(stream)
+            clocks.sample_now()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
