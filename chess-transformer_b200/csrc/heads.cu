@@ -7,7 +7,8 @@
 //   logit[f, t] = a_f . y_t + s_f, gathered to the 1968 moves, promotions plus their piece's logit at the landing square;
 //   value = Linear(GELU(Linear(GELU(board-down) flattened))) ; score = softmax(value) . bin centres.
 //
-// Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel (also the eval head's GELU'd inputs),
+// Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel (split-fp16 mma.sync, N = hi + lo / 2048;
+// also the eval head's GELU'd inputs),
 // policy_kernel (per board: the 64x64 logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay
 // fp32-exact), the eval head's two layers as split-K partial products (linear_split_kernel) summed in a fixed order by
 // linear_sum_kernel, expected_score_kernel (softmax times the bin centres). fp32 arithmetic throughout, where the
@@ -24,67 +25,13 @@ constexpr int kHeadTokens = 70, kHeadSquares = 64, kNarrow = 21, kNarrowStride =
 constexpr int kEvalInputs = kHeadTokens * kDown;  // the eval head's first layer takes 70 x 16 GELU'd board-down units
 constexpr float kLoScale = 2048.0f;
 constexpr int kSplitTile = 32;  // linear_split_kernel: 32 boards x 32 outputs a CTA, K in steps of 32
+// narrow_kernel: the 21 outputs padded to 3 mma tiles of 8; 8 tiles of 16 rows a CTA, the columns in kNarrowParts parts
+constexpr int kNarrowTile = 24, kNarrowTiles = 8, kNarrowParts = 2, kNarrowLoads = 12;
+constexpr int kPolicyAhead = 4;  // policy_kernel: steps of 16 columns loading ahead of the MMAs
 
 FRY_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
 size_t heads_workspace_bytes(int B, int D) { return heads_workspace_bytes_of(B, D); }
-
-// The warp's 32 lanes each hold 32 partial sums v[0..31]; afterwards lane j holds the total of v[j] over the lanes
-// (halving exchanges: 31 shuffles where 32 separate reductions take 160).
-FRY_DEVICE float reduce_scatter32(float (&v)[32], int lane) {
-#pragma unroll
-    for (int width = 16; width >= 1; width >>= 1) {
-        const bool upper = (lane & width) != 0;
-#pragma unroll
-        for (int i = 0; i < width; ++i) {
-            // keep v[i] (lower lanes) or v[i + width] (upper lanes); send the other half to the partner
-            const float send = upper ? v[i] : v[i + width];
-            const float keep = upper ? v[i + width] : v[i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, width));
-        }
-    }
-    return v[0];
-}
-
-// narrow[m, 0..20] = y[m] . N^T + n_bias for two rows a warp at a time, 8 warps a CTA, the weights staged in shared
-// memory; eval_in[b, t * 16 + i] = GELU(narrow[b * 70 + t, 5 + i]), the eval head's inputs, once per board.
-__global__ void __launch_bounds__(256) narrow_kernel(const uint16_t* __restrict__ y, const float* __restrict__ weight,
-                                                     const float* __restrict__ bias, float* __restrict__ narrow,
-                                                     float* __restrict__ eval_in, int M, int D) {
-    grid_dependency_start();
-    extern __shared__ float narrow_weights[];  // [21][D]
-    for (int i = threadIdx.x; i < kNarrow * D; i += blockDim.x) narrow_weights[i] = weight[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = (blockIdx.x * 8 + warp) * 2; m < M; m += gridDim.x * 16) {
-        const bool second = m + 1 < M;
-        float acc[2][32];
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[r][j] = 0.0f;
-        for (int k = lane; k < D; k += 32) {
-            const float v0 = h2f_bits(y[static_cast<size_t>(m) * D + k]);
-            const float v1 = second ? h2f_bits(y[static_cast<size_t>(m + 1) * D + k]) : 0.0f;
-#pragma unroll
-            for (int j = 0; j < kNarrow; ++j) {
-                const float w = narrow_weights[j * D + k];
-                acc[0][j] = __fmaf_rn(v0, w, acc[0][j]);
-                acc[1][j] = __fmaf_rn(v1, w, acc[1][j]);
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int row = m + r;
-            const float total = reduce_scatter32(acc[r], lane);  // lane j: output j
-            if (row < M && lane < kNarrow) {
-                const float value = __fadd_rn(total, bias[lane]);
-                narrow[static_cast<size_t>(row) * kNarrowStride + lane] = value;
-                if (lane >= 5) eval_in[static_cast<size_t>(row / kHeadTokens) * kEvalInputs + (row % kHeadTokens) * kDown + lane - 5] = gelu(value);
-            }
-        }
-    }
-}
 
 FRY_DEVICE void mma_f16_heads(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -98,6 +45,120 @@ FRY_DEVICE void split_pair(float2 v, uint32_t& hi, uint32_t& lo) {
     const __half l1 = __float2half_rn(__fmul_rn(__fsub_rn(v.y, __half2float(h1)), kLoScale));
     hi = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
     lo = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+}
+
+// narrow[m, 0..20] = y[m] . N^T + n_bias on the tensor cores: N (fp32) split into fp16 halves N = hi + lo / 2048 in shared
+// memory, [24][D + 8] each (rows 21..23 zero; the 8-element pad puts a fragment's 32 lanes on 32 banks), and y times both
+// halves by split-fp16 mma.sync (y is fp16, so every product is fp32-exact, as in policy_kernel). A CTA takes 8 tiles of
+// 16 rows; warp w works on tile w % 8 over the (w / 8)-th of kNarrowParts parts of the columns, and the parts' sums are
+// added in order through shared memory. eval_in[b, t * 16 + i] = GELU(narrow[b * 70 + t, 5 + i]), the eval head's
+// inputs, once per board. The weights are the network's constants and are split before the wait on the kernel ahead.
+__global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kernel(const uint16_t* __restrict__ y,
+                                                                                  const float* __restrict__ weight,
+                                                                                  const float* __restrict__ bias, float* __restrict__ narrow,
+                                                                                  float* __restrict__ eval_in, int M, int D) {
+    extern __shared__ __align__(16) uint16_t narrow_split[];
+    const int pitch = D + 8, quads = kNarrowTile * D / 4, per_row = D / 4;
+    uint16_t* w_hi = narrow_split;
+    uint16_t* w_lo = narrow_split + kNarrowTile * pitch;
+    float* part_sums = reinterpret_cast<float*>(narrow_split + 2 * kNarrowTile * pitch);  // [parts - 1][tiles][32][13]
+    for (int base = threadIdx.x; base < quads; base += blockDim.x * kNarrowLoads) {
+        float4 v[kNarrowLoads];
+#pragma unroll
+        for (int u = 0; u < kNarrowLoads; ++u) {
+            const int i = base + u * blockDim.x, j = i / per_row;
+            v[u] = (i < quads && j < kNarrow) ? __ldg(reinterpret_cast<const float4*>(weight + static_cast<size_t>(i) * 4))
+                                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < kNarrowLoads; ++u) {
+            const int i = base + u * blockDim.x, j = i / per_row, k = (i % per_row) * 4;
+            if (i < quads) {
+                uint32_t hi01, lo01, hi23, lo23;
+                split_pair(make_float2(v[u].x, v[u].y), hi01, lo01);
+                split_pair(make_float2(v[u].z, v[u].w), hi23, lo23);
+                *reinterpret_cast<uint2*>(w_hi + j * pitch + k) = make_uint2(hi01, hi23);
+                *reinterpret_cast<uint2*>(w_lo + j * pitch + k) = make_uint2(lo01, lo23);
+            }
+        }
+    }
+    grid_dependency_start();
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int tile = warp % kNarrowTiles, part = warp / kNarrowTiles, first = (blockIdx.x * kNarrowTiles + tile) * 16;
+    const int steps = D / 16, k_begin = steps * part / kNarrowParts * 16, k_end = steps * (part + 1) / kNarrowParts * 16;
+    // rows past M compute on row M - 1 and are not written
+    const uint16_t* rows[2] = {y + static_cast<size_t>(min(first + g, M - 1)) * D + 2 * t,
+                               y + static_cast<size_t>(min(first + g + 8, M - 1)) * D + 2 * t};
+    float hi[3][4], lo[3][4];
+#pragma unroll
+    for (int n = 0; n < 3; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
+    uint32_t a_next[kPolicyAhead][4];
+    auto fetch = [&](int slot, int k) {
+        a_next[slot][0] = *reinterpret_cast<const uint32_t*>(rows[0] + k);
+        a_next[slot][1] = *reinterpret_cast<const uint32_t*>(rows[1] + k);
+        a_next[slot][2] = *reinterpret_cast<const uint32_t*>(rows[0] + k + 8);
+        a_next[slot][3] = *reinterpret_cast<const uint32_t*>(rows[1] + k + 8);
+    };
+    const bool active = first < M;
+    if (active) {
+#pragma unroll
+        for (int slot = 0; slot < kPolicyAhead; ++slot)
+            if (k_begin + slot * 16 < k_end) fetch(slot, k_begin + slot * 16);
+        const uint16_t* b_hi = w_hi + g * pitch + 2 * t;
+        const uint16_t* b_lo = w_lo + g * pitch + 2 * t;
+        for (int k0 = k_begin; k0 < k_end; k0 += 16 * kPolicyAhead) {
+#pragma unroll
+            for (int slot = 0; slot < kPolicyAhead; ++slot) {
+                const int k = k0 + slot * 16;
+                if (k < k_end) {
+                    const uint32_t a[4] = {a_next[slot][0], a_next[slot][1], a_next[slot][2], a_next[slot][3]};
+                    if (k + 16 * kPolicyAhead < k_end) fetch(slot, k + 16 * kPolicyAhead);
+#pragma unroll
+                    for (int n = 0; n < 3; ++n) {
+                        const uint16_t* h = b_hi + n * 8 * pitch + k;
+                        const uint16_t* l = b_lo + n * 8 * pitch + k;
+                        mma_f16_heads(hi[n], a, *reinterpret_cast<const uint32_t*>(h), *reinterpret_cast<const uint32_t*>(h + 8));
+                        mma_f16_heads(lo[n], a, *reinterpret_cast<const uint32_t*>(l), *reinterpret_cast<const uint32_t*>(l + 8));
+                    }
+                }
+            }
+        }
+    }
+    float sums[3][4];
+#pragma unroll
+    for (int n = 0; n < 3; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sums[n][e] = __fadd_rn(hi[n][e], __fdiv_rn(lo[n][e], kLoScale));
+    if (kNarrowParts > 1) {
+        if (part > 0) {
+            float* mine = part_sums + ((part - 1) * kNarrowTiles + tile) * 32 * 13 + lane * 13;
+#pragma unroll
+            for (int i = 0; i < 12; ++i) mine[i] = sums[i >> 2][i & 3];
+        }
+        __syncthreads();
+        if (part > 0) return;
+#pragma unroll
+        for (int p = 1; p < kNarrowParts; ++p) {
+            const float* theirs = part_sums + ((p - 1) * kNarrowTiles + tile) * 32 * 13 + lane * 13;
+#pragma unroll
+            for (int i = 0; i < 12; ++i) sums[i >> 2][i & 3] = __fadd_rn(sums[i >> 2][i & 3], theirs[i]);
+        }
+    }
+    if (!active) return;
+#pragma unroll
+    for (int n = 0; n < 3; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int m = first + g + (e >> 1) * 8, j = n * 8 + 2 * t + (e & 1);
+            if (m < M && j < kNarrow) {
+                const float value = __fadd_rn(sums[n][e], bias[j]);
+                narrow[static_cast<size_t>(m) * kNarrowStride + j] = value;
+                if (j >= 5) eval_in[static_cast<size_t>(m / kHeadTokens) * kEvalInputs + (m % kHeadTokens) * kDown + j - 5] = gelu(value);
+            }
+        }
 }
 
 // One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits.
@@ -114,33 +175,41 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 #pragma unroll
         for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
     const float* a_rows[2] = {a + (board + m_tile * 16 + g) * D, a + (board + m_tile * 16 + g + 8) * D};
-    // the operands of step k + 16 load while step k's MMAs run
-    float2 a_next[4];
-    uint32_t y_next[4][2];
-    auto fetch = [&](int k) {
-        a_next[0] = *reinterpret_cast<const float2*>(a_rows[0] + k + 2 * t);
-        a_next[1] = *reinterpret_cast<const float2*>(a_rows[1] + k + 2 * t);
-        a_next[2] = *reinterpret_cast<const float2*>(a_rows[0] + k + 8 + 2 * t);
-        a_next[3] = *reinterpret_cast<const float2*>(a_rows[1] + k + 8 + 2 * t);
+    // the operands of the next kPolicyAhead steps of 16 load while this step's MMAs run; slot s holds steps s mod kPolicyAhead
+    float2 a_next[kPolicyAhead][4];
+    uint32_t y_next[kPolicyAhead][4][2];
+    auto fetch = [&](int slot, int k) {
+        a_next[slot][0] = *reinterpret_cast<const float2*>(a_rows[0] + k + 2 * t);
+        a_next[slot][1] = *reinterpret_cast<const float2*>(a_rows[1] + k + 2 * t);
+        a_next[slot][2] = *reinterpret_cast<const float2*>(a_rows[0] + k + 8 + 2 * t);
+        a_next[slot][3] = *reinterpret_cast<const float2*>(a_rows[1] + k + 8 + 2 * t);
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
             const uint16_t* y_row = y + (board + (n_first + n) * 8 + g) * D + k + 2 * t;
-            y_next[n][0] = *reinterpret_cast<const uint32_t*>(y_row);
-            y_next[n][1] = *reinterpret_cast<const uint32_t*>(y_row + 8);
+            y_next[slot][n][0] = *reinterpret_cast<const uint32_t*>(y_row);
+            y_next[slot][n][1] = *reinterpret_cast<const uint32_t*>(y_row + 8);
         }
     };
-    fetch(0);
-    for (int k = 0; k < D; k += 16) {
-        uint32_t ah[4], al[4], yb[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) split_pair(a_next[i], ah[i], al[i]);
+    for (int slot = 0; slot < kPolicyAhead; ++slot)
+        if (slot * 16 < D) fetch(slot, slot * 16);
+    for (int k0 = 0; k0 < D; k0 += 16 * kPolicyAhead) {
 #pragma unroll
-        for (int n = 0; n < 4; ++n) yb[n][0] = y_next[n][0], yb[n][1] = y_next[n][1];
-        if (k + 16 < D) fetch(k + 16);
+        for (int slot = 0; slot < kPolicyAhead; ++slot) {
+            const int k = k0 + slot * 16;
+            if (k < D) {
+                uint32_t ah[4], al[4], yb[4][2];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-            mma_f16_heads(hi[n], ah, yb[n][0], yb[n][1]);
-            mma_f16_heads(lo[n], al, yb[n][0], yb[n][1]);
+                for (int i = 0; i < 4; ++i) split_pair(a_next[slot][i], ah[i], al[i]);
+#pragma unroll
+                for (int n = 0; n < 4; ++n) yb[n][0] = y_next[slot][n][0], yb[n][1] = y_next[slot][n][1];
+                if (k + 16 * kPolicyAhead < D) fetch(slot, k + 16 * kPolicyAhead);
+#pragma unroll
+                for (int n = 0; n < 4; ++n) {
+                    mma_f16_heads(hi[n], ah, yb[n][0], yb[n][1]);
+                    mma_f16_heads(lo[n], al, yb[n][0], yb[n][1]);
+                }
+            }
         }
     }
 #pragma unroll
@@ -261,6 +330,10 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
         if (error) *error = "the heads take d_model a multiple of 16 up to 1024 and 2 to 256 value bins";
         return cudaErrorInvalidValue;
     }
+    if (reinterpret_cast<uintptr_t>(w.narrow_weight) % 16 != 0) {
+        if (error) *error = "the heads take the narrow weight 16-byte aligned";
+        return cudaErrorInvalidValue;
+    }
     const int M = B * kHeadTokens;
     const HeadsWorkspace layout(B, D);
     uint8_t* base = static_cast<uint8_t*>(workspace);
@@ -279,12 +352,11 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     args.out = a;
     status = gemm(1, kEpiLinearF32, y, w.a_weight, args, M, D, D, stream, error);
     if (status != cudaSuccess) return status;
-    const size_t narrow_smem = static_cast<size_t>(kNarrow) * D * sizeof(float);
+    const size_t narrow_smem = 2ull * kNarrowTile * (D + 8) * sizeof(uint16_t) + (kNarrowParts - 1) * kNarrowTiles * 32 * 13 * sizeof(float);
     status = ensure_smem(reinterpret_cast<const void*>(narrow_kernel), static_cast<int>(narrow_smem));
     if (status != cudaSuccess) return status;
-    const int narrow_blocks = (M + 15) / 16 < 148 * 3 ? (M + 15) / 16 : 148 * 3;
-    status = launch_dependent(narrow_kernel, dim3(narrow_blocks), dim3(256), narrow_smem, stream, y, w.narrow_weight, w.narrow_bias, narrow,
-                              eval_in, M, D);
+    status = launch_dependent(narrow_kernel, dim3((M + kNarrowTiles * 16 - 1) / (kNarrowTiles * 16)), dim3(kNarrowTiles * kNarrowParts * 32),
+                              narrow_smem, stream, y, w.narrow_weight, w.narrow_bias, narrow, eval_in, M, D);
     if (status != cudaSuccess) return status;
     status = launch_dependent(policy_kernel, dim3(B), dim3(256), 0, stream, a, y, narrow, rows, D);
     if (status != cudaSuccess) return status;
