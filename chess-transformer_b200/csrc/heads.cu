@@ -27,7 +27,10 @@ constexpr float kLoScale = 2048.0f;
 constexpr int kSplitTile = 32;  // linear_split_kernel: 32 boards x 32 outputs a CTA, K in steps of 32
 // narrow_kernel: the 21 outputs padded to 3 mma tiles of 8; 8 tiles of 16 rows a CTA, the columns in kNarrowParts parts
 constexpr int kNarrowTile = 24, kNarrowTiles = 8, kNarrowParts = 2, kNarrowLoads = 12;
-constexpr int kPolicyAhead = 4;  // policy_kernel: steps of 16 columns loading ahead of the MMAs
+constexpr int kNarrowAhead = 4;  // narrow_kernel: steps of 16 columns loading ahead of the MMAs
+// policy_kernel: chunks of 64 columns in a ring of 3 stages; row pitches padded by 8 elements (conflict-free fragment loads)
+constexpr int kPolicyChunk = 64, kPolicyStages = 3, kPolicyAPitch = kPolicyChunk + 8, kPolicyYPitch = kPolicyChunk + 8;
+static_assert(kHeadSquares * (kHeadSquares + 1) <= kPolicyStages * kHeadSquares * kPolicyAPitch, "the logits fit in the a chunks");
 
 FRY_DEVICE float gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kerne
     for (int n = 0; n < 3; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
-    uint32_t a_next[kPolicyAhead][4];
+    uint32_t a_next[kNarrowAhead][4];
     auto fetch = [&](int slot, int k) {
         a_next[slot][0] = *reinterpret_cast<const uint32_t*>(rows[0] + k);
         a_next[slot][1] = *reinterpret_cast<const uint32_t*>(rows[1] + k);
@@ -105,17 +108,17 @@ __global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kerne
     const bool active = first < M;
     if (active) {
 #pragma unroll
-        for (int slot = 0; slot < kPolicyAhead; ++slot)
+        for (int slot = 0; slot < kNarrowAhead; ++slot)
             if (k_begin + slot * 16 < k_end) fetch(slot, k_begin + slot * 16);
         const uint16_t* b_hi = w_hi + g * pitch + 2 * t;
         const uint16_t* b_lo = w_lo + g * pitch + 2 * t;
-        for (int k0 = k_begin; k0 < k_end; k0 += 16 * kPolicyAhead) {
+        for (int k0 = k_begin; k0 < k_end; k0 += 16 * kNarrowAhead) {
 #pragma unroll
-            for (int slot = 0; slot < kPolicyAhead; ++slot) {
+            for (int slot = 0; slot < kNarrowAhead; ++slot) {
                 const int k = k0 + slot * 16;
                 if (k < k_end) {
                     const uint32_t a[4] = {a_next[slot][0], a_next[slot][1], a_next[slot][2], a_next[slot][3]};
-                    if (k + 16 * kPolicyAhead < k_end) fetch(slot, k + 16 * kPolicyAhead);
+                    if (k + 16 * kNarrowAhead < k_end) fetch(slot, k + 16 * kNarrowAhead);
 #pragma unroll
                     for (int n = 0; n < 3; ++n) {
                         const uint16_t* h = b_hi + n * 8 * pitch + k;
@@ -161,57 +164,81 @@ __global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kerne
         }
 }
 
-// One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits.
+FRY_DEVICE void cp_async16(void* shared, const void* global) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(shared))), "l"(global)
+                 : "memory");
+}
+FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int PENDING>
+FRY_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory"); }
+
+// One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits. The board's 64 square rows of a
+// (fp32) and y (fp16) stream through shared memory in chunks of kPolicyChunk columns, kPolicyStages deep, by 16-byte cp.async
+// (whole 128-byte lines per 8 lanes); each warp takes its 16 x 32 tile of L from fragments read out of shared memory,
+// the padded pitches putting each fragment load on distinct banks.
 __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a, const uint16_t* __restrict__ y,
                                                      const float* __restrict__ narrow, float* __restrict__ rows, int D) {
+    extern __shared__ __align__(16) float policy_smem[];  // a chunks, then y chunks; the logits reuse the a chunks at the end
+    auto a_chunks = reinterpret_cast<float(*)[kHeadSquares * kPolicyAPitch]>(policy_smem);
+    auto y_chunks = reinterpret_cast<uint16_t(*)[kHeadSquares * kPolicyYPitch]>(policy_smem + kPolicyStages * kHeadSquares * kPolicyAPitch);
+    auto logits = reinterpret_cast<float(*)[kHeadSquares + 1]>(policy_smem);
     grid_dependency_start();
-    __shared__ float logits[kHeadSquares][kHeadSquares + 1];
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int m_tile = warp >> 1, n_first = (warp & 1) * 4;
     const size_t board = static_cast<size_t>(b) * kHeadTokens;
+    const int chunks = (D + kPolicyChunk - 1) / kPolicyChunk;
+    auto load_chunk = [&](int chunk) {
+        const int stage = chunk % kPolicyStages, k0 = chunk * kPolicyChunk;
+        constexpr int a_pieces = kPolicyChunk / 4, y_pieces = kPolicyChunk / 8;  // 16-byte pieces of a row
+#pragma unroll
+        for (int i = threadIdx.x; i < kHeadSquares * a_pieces; i += 256) {
+            const int r = i / a_pieces, piece = i % a_pieces, k = k0 + piece * 4;
+            if (k < D) cp_async16(&a_chunks[stage][r * kPolicyAPitch + piece * 4], a + (board + r) * D + k);
+        }
+#pragma unroll
+        for (int i = threadIdx.x; i < kHeadSquares * y_pieces; i += 256) {
+            const int r = i / y_pieces, piece = i % y_pieces, k = k0 + piece * 8;
+            if (k < D) cp_async16(&y_chunks[stage][r * kPolicyYPitch + piece * 8], y + (board + r) * D + k);
+        }
+    };
+#pragma unroll
+    for (int chunk = 0; chunk < kPolicyStages - 1; ++chunk) {
+        if (chunk < chunks) load_chunk(chunk);
+        cp_async_commit();
+    }
     float hi[4][4], lo[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
-    const float* a_rows[2] = {a + (board + m_tile * 16 + g) * D, a + (board + m_tile * 16 + g + 8) * D};
-    // the operands of the next kPolicyAhead steps of 16 load while this step's MMAs run; slot s holds steps s mod kPolicyAhead
-    float2 a_next[kPolicyAhead][4];
-    uint32_t y_next[kPolicyAhead][4][2];
-    auto fetch = [&](int slot, int k) {
-        a_next[slot][0] = *reinterpret_cast<const float2*>(a_rows[0] + k + 2 * t);
-        a_next[slot][1] = *reinterpret_cast<const float2*>(a_rows[1] + k + 2 * t);
-        a_next[slot][2] = *reinterpret_cast<const float2*>(a_rows[0] + k + 8 + 2 * t);
-        a_next[slot][3] = *reinterpret_cast<const float2*>(a_rows[1] + k + 8 + 2 * t);
+    for (int chunk = 0; chunk < chunks; ++chunk) {
+        cp_async_wait<kPolicyStages - 2>();
+        __syncthreads();  // the chunk is in; and every warp is done with the stage the next load overwrites
+        if (chunk + kPolicyStages - 1 < chunks) load_chunk(chunk + kPolicyStages - 1);
+        cp_async_commit();
+        const float* as = a_chunks[chunk % kPolicyStages] + (m_tile * 16 + g) * kPolicyAPitch + 2 * t;
+        const uint16_t* ys = y_chunks[chunk % kPolicyStages] + (n_first * 8 + g) * kPolicyYPitch + 2 * t;
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-            const uint16_t* y_row = y + (board + (n_first + n) * 8 + g) * D + k + 2 * t;
-            y_next[slot][n][0] = *reinterpret_cast<const uint32_t*>(y_row);
-            y_next[slot][n][1] = *reinterpret_cast<const uint32_t*>(y_row + 8);
-        }
-    };
+        for (int kk = 0; kk < kPolicyChunk; kk += 16) {
+            if (chunk * kPolicyChunk + kk < D) {
+                const float2 a_pairs[4] = {*reinterpret_cast<const float2*>(as + kk), *reinterpret_cast<const float2*>(as + 8 * kPolicyAPitch + kk),
+                                           *reinterpret_cast<const float2*>(as + kk + 8),
+                                           *reinterpret_cast<const float2*>(as + 8 * kPolicyAPitch + kk + 8)};
+                uint32_t ah[4], al[4];
 #pragma unroll
-    for (int slot = 0; slot < kPolicyAhead; ++slot)
-        if (slot * 16 < D) fetch(slot, slot * 16);
-    for (int k0 = 0; k0 < D; k0 += 16 * kPolicyAhead) {
-#pragma unroll
-        for (int slot = 0; slot < kPolicyAhead; ++slot) {
-            const int k = k0 + slot * 16;
-            if (k < D) {
-                uint32_t ah[4], al[4], yb[4][2];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) split_pair(a_next[slot][i], ah[i], al[i]);
-#pragma unroll
-                for (int n = 0; n < 4; ++n) yb[n][0] = y_next[slot][n][0], yb[n][1] = y_next[slot][n][1];
-                if (k + 16 * kPolicyAhead < D) fetch(slot, k + 16 * kPolicyAhead);
+                for (int i = 0; i < 4; ++i) split_pair(a_pairs[i], ah[i], al[i]);
 #pragma unroll
                 for (int n = 0; n < 4; ++n) {
-                    mma_f16_heads(hi[n], ah, yb[n][0], yb[n][1]);
-                    mma_f16_heads(lo[n], al, yb[n][0], yb[n][1]);
+                    const uint16_t* yn = ys + n * 8 * kPolicyYPitch + kk;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(yn), b1 = *reinterpret_cast<const uint32_t*>(yn + 8);
+                    mma_f16_heads(hi[n], ah, b0, b1);
+                    mma_f16_heads(lo[n], al, b0, b1);
                 }
             }
         }
     }
+    cp_async_wait<0>();
+    __syncthreads();  // every warp is done reading the chunks the logits overwrite
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -358,7 +385,10 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     status = launch_dependent(narrow_kernel, dim3((M + kNarrowTiles * 16 - 1) / (kNarrowTiles * 16)), dim3(kNarrowTiles * kNarrowParts * 32),
                               narrow_smem, stream, y, w.narrow_weight, w.narrow_bias, narrow, eval_in, M, D);
     if (status != cudaSuccess) return status;
-    status = launch_dependent(policy_kernel, dim3(B), dim3(256), 0, stream, a, y, narrow, rows, D);
+    const size_t policy_smem = kPolicyStages * kHeadSquares * (kPolicyAPitch * sizeof(float) + kPolicyYPitch * sizeof(uint16_t));
+    status = ensure_smem(reinterpret_cast<const void*>(policy_kernel), static_cast<int>(policy_smem));
+    if (status != cudaSuccess) return status;
+    status = launch_dependent(policy_kernel, dim3(B), dim3(256), policy_smem, stream, a, y, narrow, rows, D);
     if (status != cudaSuccess) return status;
     // the eval head: hidden = GELU(W1 . eval_in + b1), logits = W2 . hidden + b2, each as split-K partial products
     const int split1 = split_size(kEvalInputs), splits1 = (kEvalInputs + split1 - 1) / split1;
