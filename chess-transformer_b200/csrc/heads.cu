@@ -24,7 +24,8 @@ namespace fry {
 constexpr int kHeadTokens = 70, kHeadSquares = 64, kNarrow = 21, kNarrowStride = 24, kDown = 16, kMoves = 1968;
 constexpr int kEvalInputs = kHeadTokens * kDown;  // the eval head's first layer takes 70 x 16 GELU'd board-down units
 constexpr float kLoScale = 2048.0f;
-constexpr int kSplitTile = 32;  // linear_split_kernel: 32 boards x 32 outputs a CTA, K in steps of 32
+constexpr int kLinearTile = 64, kLinearStep = 16;  // linear_split_kernel: 64 boards x 64 outputs a CTA, K in steps of 16
+constexpr int kEvalSplits = 8;  // the eval head's layers: K in 8 splits, whatever the batch
 // narrow_kernel: the 21 outputs padded to 3 mma tiles of 8; 8 tiles of 16 rows a CTA, the columns in kNarrowParts parts
 constexpr int kNarrowTile = 24, kNarrowTiles = 8, kNarrowParts = 2, kNarrowLoads = 12;
 constexpr int kNarrowAhead = 4;  // narrow_kernel: steps of 16 columns loading ahead of the MMAs
@@ -258,39 +259,67 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 }
 
 // One split of an fp32 linear layer: partial[split, b, u] = sum over inputs i of split's K range of W[u, i] * x[b, i], for
-// x [B, K] and W [N, K] row-major; a CTA takes 32 boards x 32 outputs of one split, 2 x 2 a thread.
+// x [B, K] and W [N, K] row-major (K a multiple of 4, both 16-byte aligned). A CTA takes 64 boards x 64 outputs of one
+// split, 4 x 4 a thread, K in steps of 16 through shared memory (transposed, two buffers): each thread loads one float4
+// of x and of W a step, the next step's while this one's FMAs run. Each output's sum runs over its split's inputs in
+// order, whatever the batch.
 __global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ x, const float* __restrict__ weight,
                                                            float* __restrict__ partial, int B, int K, int N, int k_split) {
     grid_dependency_start();
-    __shared__ float xs[kSplitTile][kSplitTile + 1];
-    __shared__ float ws[kSplitTile][kSplitTile + 1];
+    __shared__ __align__(16) float xs[2][kLinearStep][kLinearTile + 4];
+    __shared__ __align__(16) float ws[2][kLinearStep][kLinearTile + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int b0 = blockIdx.y * kSplitTile, u0 = blockIdx.x * kSplitTile;
+    const int b0 = blockIdx.y * kLinearTile, u0 = blockIdx.x * kLinearTile;
     const int k_begin = blockIdx.z * k_split, k_end = min(K, k_begin + k_split);
-    float acc[2][2] = {};
-    for (int k0 = k_begin; k0 < k_end; k0 += kSplitTile) {
-        for (int i = threadIdx.x; i < kSplitTile * kSplitTile; i += 256) {
-            const int kk = i % kSplitTile, row = i / kSplitTile, input = k0 + kk;
-            const int board = b0 + row, unit = u0 + row;
-            xs[kk][row] = (board < B && input < k_end) ? x[static_cast<size_t>(board) * K + input] : 0.0f;
-            ws[kk][row] = (unit < N && input < k_end) ? weight[static_cast<size_t>(unit) * K + input] : 0.0f;
+    const int load_row = threadIdx.x >> 2, load_quad = threadIdx.x & 3, board = b0 + load_row, unit = u0 + load_row;
+    const float* x_row = x + static_cast<size_t>(min(board, B - 1)) * K + load_quad * 4;
+    const float* w_row = weight + static_cast<size_t>(min(unit, N - 1)) * K + load_quad * 4;
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 xv, wv;
+    auto fetch = [&](int k0) {
+        const bool in = k0 + load_quad * 4 < k_end;
+        xv = in && board < B ? *reinterpret_cast<const float4*>(x_row + k0) : zero;
+        wv = in && unit < N ? __ldg(reinterpret_cast<const float4*>(w_row + k0)) : zero;
+    };
+    auto stash = [&](int buffer) {
+        float* xc = &xs[buffer][load_quad * 4][load_row];
+        float* wc = &ws[buffer][load_quad * 4][load_row];
+        xc[0] = xv.x, xc[kLinearTile + 4] = xv.y, xc[2 * (kLinearTile + 4)] = xv.z, xc[3 * (kLinearTile + 4)] = xv.w;
+        wc[0] = wv.x, wc[kLinearTile + 4] = wv.y, wc[2 * (kLinearTile + 4)] = wv.z, wc[3 * (kLinearTile + 4)] = wv.w;
+    };
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    fetch(k_begin);
+    stash(0);
+    __syncthreads();
+    int buffer = 0;
+    for (int k0 = k_begin; k0 < k_end; k0 += kLinearStep) {
+        const bool more = k0 + kLinearStep < k_end;
+        if (more) fetch(k0 + kLinearStep);
+#pragma unroll
+        for (int kk = 0; kk < kLinearStep; ++kk) {
+            const float4 a = *reinterpret_cast<const float4*>(&xs[buffer][kk][ty * 4]);
+            const float4 w = *reinterpret_cast<const float4*>(&ws[buffer][kk][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, wv4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], wv4[j], acc[i][j]);
         }
+        if (more) stash(buffer ^ 1);
         __syncthreads();
-#pragma unroll 8
-        for (int kk = 0; kk < kSplitTile; ++kk)
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j) acc[i][j] = __fmaf_rn(xs[kk][ty * 2 + i], ws[kk][tx * 2 + j], acc[i][j]);
-        __syncthreads();
+        buffer ^= 1;
     }
     float* out = partial + static_cast<size_t>(blockIdx.z) * B * N;
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int board = b0 + ty * 2 + i, unit = u0 + tx * 2 + j;
-            if (board < B && unit < N) out[static_cast<size_t>(board) * N + unit] = acc[i][j];
+        for (int j = 0; j < 4; ++j) {
+            const int b = b0 + ty * 4 + i, u = u0 + tx * 4 + j;
+            if (b < B && u < N) out[static_cast<size_t>(b) * N + u] = acc[i][j];
         }
 }
 
@@ -307,8 +336,9 @@ __global__ void __launch_bounds__(256) linear_sum_kernel(const float* __restrict
     out[index] = GELU ? gelu(value) : value;
 }
 
-// Splits of K for the eval head's layers: about 160 inputs a CTA, whole 32-input steps.
-inline int split_size(int K) { return (K + kEvalSplitsMax - 1) / kEvalSplitsMax < 160 ? 160 : ((K + kEvalSplitsMax - 1) / kEvalSplitsMax + 31) / 32 * 32; }
+// Splits of K for the eval head's layers: kEvalSplits of whole steps of 16 (a board's sums do not depend on its batch).
+inline int split_size(int K) { return ((K + kEvalSplits - 1) / kEvalSplits + kLinearStep - 1) / kLinearStep * kLinearStep; }
+static_assert(kEvalSplits <= kEvalSplitsMax, "the workspace holds kEvalSplitsMax splits");
 
 // One warp per board: the softmax of its value logits times the bin centres (2i + 1) / 2bins, into the row's last column.
 // With lean lanes, each board's answer also gathers its lane's answer columns of its row (the move logits the policy
@@ -357,8 +387,9 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
         if (error) *error = "the heads take d_model a multiple of 16 up to 1024 and 2 to 256 value bins";
         return cudaErrorInvalidValue;
     }
-    if (reinterpret_cast<uintptr_t>(w.narrow_weight) % 16 != 0) {
-        if (error) *error = "the heads take the narrow weight 16-byte aligned";
+    if (reinterpret_cast<uintptr_t>(w.narrow_weight) % 16 != 0 || reinterpret_cast<uintptr_t>(w.hidden_weight) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(w.out_weight) % 16 != 0) {
+        if (error) *error = "the heads take the narrow and eval-head weights 16-byte aligned";
         return cudaErrorInvalidValue;
     }
     const int M = B * kHeadTokens;
@@ -392,14 +423,14 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
     if (status != cudaSuccess) return status;
     // the eval head: hidden = GELU(W1 . eval_in + b1), logits = W2 . hidden + b2, each as split-K partial products
     const int split1 = split_size(kEvalInputs), splits1 = (kEvalInputs + split1 - 1) / split1;
-    status = launch_dependent(linear_split_kernel, dim3((D + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits1),
+    status = launch_dependent(linear_split_kernel, dim3((D + kLinearTile - 1) / kLinearTile, (B + kLinearTile - 1) / kLinearTile, splits1),
                               dim3(256), 0, stream, eval_in, w.hidden_weight, partial, B, kEvalInputs, D, split1);
     if (status != cudaSuccess) return status;
     status = launch_dependent(linear_sum_kernel<true>, dim3((B * D + 255) / 256), dim3(256), 0, stream, partial, w.hidden_bias, hidden, B, D,
                               splits1);
     if (status != cudaSuccess) return status;
     const int split2 = split_size(D), splits2 = (D + split2 - 1) / split2;
-    status = launch_dependent(linear_split_kernel, dim3((w.bins + kSplitTile - 1) / kSplitTile, (B + kSplitTile - 1) / kSplitTile, splits2),
+    status = launch_dependent(linear_split_kernel, dim3((w.bins + kLinearTile - 1) / kLinearTile, (B + kLinearTile - 1) / kLinearTile, splits2),
                               dim3(256), 0, stream, hidden, w.out_weight, partial, B, D, w.bins, split2);
     if (status != cudaSuccess) return status;
     status = launch_dependent(linear_sum_kernel<false>, dim3((B * w.bins + 255) / 256), dim3(256), 0, stream, partial, w.out_bias, value_logits,
