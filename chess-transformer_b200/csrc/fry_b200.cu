@@ -6,3 +6,4 @@
 #include "heads.cu"
 #include "abi.cu"
 #include "noalloc.cu"
+#include "lanes.cu"

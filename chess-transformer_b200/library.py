@@ -38,6 +38,13 @@ class FryNetwork(ctypes.Structure):
                 ("head_weights", FryHeads)]
 
 
+class FryLaneHandles(ctypes.Structure):
+    _fields_ = [("device", _c_int), ("stream", _ptr), ("done", _ptr), ("rows_host", _ptr), ("rows", _ptr), ("answers_host", _ptr),
+                ("answers", _ptr)]
+
+
+ERROR_SHAPE, ERROR_CUDA, ERROR_STATE = 1, 2, 3
+
 # name -> (argument types, result type); every int-returning entry point is checked
 SIGNATURES = {
     "fry_last_error": ([], ctypes.c_char_p),
@@ -62,6 +69,14 @@ SIGNATURES = {
     "fry_forward": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
     "fry_forward_lean_workspace_bytes": ([ctypes.POINTER(FryNetwork), _c_int], _size),
     "fry_forward_lean": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
+    "fry_lanes_create": ([ctypes.POINTER(FryNetwork), ctypes.POINTER(_c_int), _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_ptr)], _c_int),
+    "fry_lanes_destroy": ([_ptr], _c_int),
+    "fry_lanes_free_lane": ([_ptr, ctypes.POINTER(_c_int)], _c_int),
+    "fry_lanes_handles": ([_ptr, _c_int, ctypes.POINTER(FryLaneHandles)], _c_int),
+    "fry_lanes_graph": ([_ptr, _c_int, _c_int, ctypes.POINTER(_ptr)], _c_int),
+    "fry_lanes_launch": ([_ptr, _c_int, _c_int, ctypes.POINTER(_c_int)], _c_int),
+    "fry_lanes_collect": ([_ptr, _c_int, ctypes.POINTER(_c_int)], _c_int),
+    "fry_lanes_settle": ([_ptr], _c_int),
 }
 
 _lock = threading.Lock()

@@ -212,6 +212,51 @@ size_t fry_forward_lean_workspace_bytes(const FryNetwork* network, int B);
 int fry_forward_lean(const FryNetwork* network, const uint8_t* lean_rows, int B, float* answers, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ---- lanes: the batch runtime in C++ ------------------------------------------------------------------------------
+ * `GraphedBatches` and `Lane` (engine/inference.py:85-225) with the CUDA runtime calls of engine/cuda_runtime.py, and no
+ * Python between batches. A FryLanes holds `in_flight` lanes on the device current at creation. Each lane has its own
+ * stream, one CUDA graph of the forward per batch size in `sizes` (ascending), pinned host buffers for the boards in and
+ * the answers out, and a done event. fry_lanes_launch copies a batch's boards in, replays the smallest graph that holds
+ * it and returns; fry_lanes_collect copies its answers out and waits for them. At most one batch is out a lane.
+ * A lean FryLanes (lean != 0) takes rows of FRY_LEAN_ROW bytes (70 token bytes, then FRY_LEAN_COLUMNS int16 answer
+ * columns) and answers FRY_LEAN_COLUMNS floats a board, as fry_forward_lean; otherwise it takes boards int64 [n, 70]
+ * and answers rows fp32 [n, 1969], as fry_forward. The graphs read the network's weights where they were at
+ * fry_lanes_create: keep them in place while the FryLanes lives. A call out of order (a launch on a lane whose batch is
+ * out, a collect of a lane with none, no free lane) returns FRY_ERROR_STATE, as the reference raises RuntimeError. */
+#define FRY_ERROR_STATE 3   /* a lane call out of order */
+#define FRY_LEAN_ROW 508
+#define FRY_LEAN_COLUMNS 219
+typedef struct FryLanes FryLanes;
+
+/* The raw handles of a lane, as `Lane.handles()` gives them (engine/inference.py:138-142): every size's graph writes
+ * the lane's one answers buffer. Pointers are host-pinned (`*_host`) or device memory. */
+typedef struct FryLaneHandles {
+    int device;
+    void* stream;        /* cudaStream_t */
+    void* done;          /* cudaEvent_t, recorded after each launch */
+    void* rows_host;     /* pinned: the boards in (int64 [largest, 70], or lean rows uint8 [largest, 508]) */
+    void* rows;          /* device: the same */
+    float* answers_host; /* pinned: the answers out ([largest, 1969], or lean [largest, 219]) */
+    float* answers;      /* device: the same */
+} FryLaneHandles;
+
+int fry_lanes_create(const FryNetwork* network, const int* sizes, int sizes_count, int in_flight, int lean, int blocking_wait,
+                     FryLanes** lanes);
+int fry_lanes_destroy(FryLanes* lanes);
+/* The first lane with no batch out (`GraphedBatches.free_lane`), or FRY_ERROR_STATE. */
+int fry_lanes_free_lane(const FryLanes* lanes, int* lane);
+int fry_lanes_handles(const FryLanes* lanes, int lane, FryLaneHandles* handles);
+/* The graph executable (cudaGraphExec_t) of sizes[size_index] on a lane, for callers that replay it themselves. */
+int fry_lanes_graph(const FryLanes* lanes, int lane, int size_index, void** graph_exec);
+/* Copies `count` boards from the lane's pinned rows_host in, replays the smallest graph of at least `count` boards and
+ * records the done event (`launch_filled`); *size is the graph's size. Returns at once. */
+int fry_lanes_launch(FryLanes* lanes, int lane, int count, int* size);
+/* Waits for the lane's batch (on the done event when blocking_wait, else on the stream) and copies its `count` answers
+ * into answers_host (`collect`); *count is the batch's. */
+int fry_lanes_collect(FryLanes* lanes, int lane, int* count);
+/* Waits for every lane's batch and marks them collected without copying (`settle`). */
+int fry_lanes_settle(FryLanes* lanes);
+
 #ifdef __cplusplus
 }
 #endif

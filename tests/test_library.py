@@ -130,3 +130,23 @@ def test_lean_forward_is_refused_on_the_host_without_a_network(lib):
     with pytest.raises(FryError, match="needs a network"):
         lib.fry_forward_lean(None, None, 4, None, None, 0, None)
     assert lib.fry_forward_lean_workspace_bytes(None, 4) == 0
+
+
+def test_lane_calls_are_refused_on_the_host_before_any_cuda_call(lib):
+    # fry_lanes_*: the batch runtime's argument checks come before its first CUDA call, so they run without a GPU
+    import ctypes
+    from chess_transformer_b200.library import ERROR_SHAPE, FryNetwork
+    network, handle = FryNetwork(), ctypes.c_void_p()
+    sizes = lambda *s: (ctypes.c_int * len(s))(*s)
+    with pytest.raises(FryError, match="ascending"):
+        lib.fry_lanes_create(ctypes.byref(network), sizes(1, 8, 4), 3, 2, 0, 0, ctypes.byref(handle))
+    with pytest.raises(FryError, match="ascending"):
+        lib.fry_lanes_create(ctypes.byref(network), sizes(0, 4), 2, 2, 1, 0, ctypes.byref(handle))
+    with pytest.raises(FryError, match="at least one size and one lane"):
+        lib.fry_lanes_create(ctypes.byref(network), sizes(1, 2), 2, 0, 0, 0, ctypes.byref(handle))
+    assert handle.value is None
+    raw = lib.handle
+    assert raw.fry_lanes_free_lane(None, None) == ERROR_SHAPE and "needs lanes" in raw.fry_last_error().decode()
+    assert raw.fry_lanes_launch(None, 0, 1, None) == ERROR_SHAPE and "no such lane" in raw.fry_last_error().decode()
+    assert raw.fry_lanes_collect(None, 0, None) == ERROR_SHAPE
+    assert raw.fry_lanes_destroy(None) == 0

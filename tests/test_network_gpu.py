@@ -10,7 +10,7 @@ from chess_transformer_b200.build import build
 from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
 from chess_transformer_b200.library import library
 from chess_transformer_b200.network import FRY_SETTINGS, Int8Network
-from chess_transformer_b200.runtime import GraphedBatches, small_graph_sizes
+from chess_transformer_b200.runtime import GraphedBatches, NativeBatches, small_graph_sizes
 from oracle import int8 as oi, model as om
 from tests.conftest import SMALL, TINY
 
@@ -229,3 +229,72 @@ def test_lean_lanes_replay_by_their_raw_handles_as_the_rust_loop_does(fry):
     assert memcpy(handles["answers_host"], answers, 16 * LEAN_COLUMNS * 4, 2, handles["stream"]) == 0
     assert sync(handles["stream"]) == 0
     assert np.array_equal(lane.answers_array[:16], expected)
+
+
+def test_native_lanes_give_the_eager_bits(fry):
+    # the C++ lane runtime (fry_lanes_*): the eager forward's bits, two batches out and collected in either order, and the
+    # reference's refusals (engine/inference.py:167-171: RuntimeError with every lane busy)
+    network, _ = fry
+    boards = random_boards(24, 14)
+    with torch.no_grad():
+        eager = network(torch.from_numpy(boards).long().cuda()).cpu().numpy()
+    batches = NativeBatches(network, small_graph_sizes(24), in_flight=2)
+    try:
+        first = batches.launch(boards[:10])
+        second = batches.launch(boards)
+        with pytest.raises(RuntimeError, match="more batches in flight than lanes"):
+            batches.launch(boards[:3])
+        assert np.array_equal(batches.collect(second), eager)
+        assert np.array_equal(batches.collect(first), eager[:10])
+        with pytest.raises(RuntimeError, match="no batch out"):
+            batches.collect(first)
+        with pytest.raises(RuntimeError, match="1 to 24 boards"):
+            batches.launch_filled(batches.free_lane(), 25)
+        for _ in range(20):
+            assert np.array_equal(batches.collect(batches.launch(boards[:17])), eager[:17])
+        batches.launch(boards[:5])
+        batches.settle()
+        assert all(not lane.pending for lane in batches.lanes)
+    finally:
+        batches.close()
+
+
+def test_native_lean_lanes_give_the_eager_bits_and_replay_by_raw_handle(fry):
+    # lean C++ lanes with blocking waits; then the Rust round loop's own calls on one of them, by raw handle through
+    # torch's cudart (engine/inference.py:175-205): rows in, the size's graph, done, answers out
+    import ctypes, os
+    network, _ = fry
+    boards = random_boards(24, 15)
+    rows_bytes, _ = lean_rows(boards, 15)
+    with torch.no_grad():
+        eager = network.forward_lean(torch.from_numpy(rows_bytes).cuda()).cpu().numpy()
+    batches = NativeBatches(network, [8, 16, 24], in_flight=2, blocking_wait=True, lean=True)
+    try:
+        with pytest.raises(RuntimeError, match="launch_filled"):
+            batches.launch(boards)
+        lane = batches.free_lane()
+        lane.rows_array[:24] = rows_bytes
+        first = batches.launch_filled(lane, 24)
+        lane = batches.free_lane()
+        lane.rows_array[:10] = rows_bytes[:10]
+        second = batches.launch_filled(lane, 10)
+        assert (first[1], second[1]) == (24, 16)
+        assert np.array_equal(batches.collect(second), eager[:10])
+        assert np.array_equal(batches.collect(first), eager)
+        handles = batches.rust_network()["lanes"][1]
+        cudart = ctypes.CDLL(f"libcudart.so.{torch.version.cuda.split('.')[0]}", mode=os.RTLD_NOLOAD | os.RTLD_LAZY)
+        memcpy, launch, record, sync = cudart.cudaMemcpyAsync, cudart.cudaGraphLaunch, cudart.cudaEventRecord, cudart.cudaStreamSynchronize
+        memcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+        launch.argtypes, record.argtypes, sync.argtypes = [ctypes.c_void_p] * 2, [ctypes.c_void_p] * 2, [ctypes.c_void_p]
+        lane = batches.lanes[1]
+        lane.rows_array[:16] = rows_bytes[8:]
+        lane.answers_array[:] = 0
+        executable, answers = handles["graphs"][16]
+        assert memcpy(handles["rows"], handles["rows_host"], 16 * LEAN_ROW, 1, handles["stream"]) == 0
+        assert launch(executable, handles["stream"]) == 0
+        assert record(handles["done"], handles["stream"]) == 0
+        assert memcpy(handles["answers_host"], answers, 16 * LEAN_COLUMNS * 4, 2, handles["stream"]) == 0
+        assert sync(handles["stream"]) == 0
+        assert np.array_equal(lane.answers_array[:16], eager[8:])
+    finally:
+        batches.close()
