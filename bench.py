@@ -281,7 +281,7 @@ def main() -> None:
     from chess_transformer_b200.boards import random_boards
     from chess_transformer_b200.network import FRY_SETTINGS, Int8Network, quantize, synthetic_state_dict
     from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
-    from chess_transformer_b200.runtime import GraphedBatches
+    from chess_transformer_b200.runtime import GraphedBatches, NativeBatches
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -378,6 +378,28 @@ def main() -> None:
         lean_seconds = slowest.item()
     del lean_batches
 
+    # the same lean steps through the library's C++ lanes (fry_lanes_*): one C-ABI call to launch, one to collect
+    native = NativeBatches(network, [BATCH], in_flight=1, lean=True)
+
+    def native_step():
+        lane = native.free_lane()
+        lane.rows_array[:BATCH] = lean_rows
+        native.collect(native.launch_filled(lane, BATCH))
+
+    for _ in range(max(3, args.warmup)):
+        native_step()
+    if world > 1:
+        dist.barrier()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        native_step()
+    native_seconds = time.perf_counter() - start
+    if world > 1:
+        slowest = torch.tensor([native_seconds], device=device)
+        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+        native_seconds = slowest.item()
+    native.close()
+
     extra = {}
     if rank == 0 and not args.no_sweep:
         latencies = []
@@ -412,6 +434,9 @@ def main() -> None:
                         "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4},
                 "e2e_lean": {"value": BATCH * args.steps * world / lean_seconds, "unit": "positions/s",
                              "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4},
+                "e2e_lean_native": {"value": BATCH * args.steps * world / native_seconds, "unit": "positions/s",
+                                    "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4,
+                                    "runtime": "fry_lanes_* (C++ lanes, one C-ABI call to launch and one to collect)"},
                 "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
                 "forward_int8_tops": round(forward_tops, 1),
                 "roofline": roofline, "clocks": clocks.summary(), **extra}
