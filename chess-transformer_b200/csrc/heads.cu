@@ -7,12 +7,11 @@
 //   logit[f, t] = a_f . y_t + s_f, gathered to the 1968 moves, promotions plus their piece's logit at the landing square;
 //   value = Linear(GELU(Linear(GELU(board-down) flattened))) ; score = softmax(value) . bin centres.
 //
-// Kernels: rms_norm (rows.cu), the tcgen05 f16 GEMM for a (gemm.cu), narrow_kernel (split-fp16 mma.sync, N = hi + lo / 2048;
-// also the eval head's GELU'd inputs),
-// policy_kernel (per board: the 64x64 logits from split-fp16 mma.sync, a = hi + lo / 2048 so the products stay
-// fp32-exact), the eval head's two layers as split-K partial products (linear_split_kernel) summed in a fixed order by
-// linear_sum_kernel, expected_score_kernel (softmax times the bin centres). fp32 arithmetic throughout, where the
-// reference uses tf32 matmuls.
+// Kernels: rms_norm (rows.cu); the tcgen05 f16 GEMM for a (gemm.cu); narrow_kernel (split-fp16 mma.sync, N = hi + lo /
+// 2048, and the eval head's GELU'd inputs); policy_kernel (per board, the 64x64 logits by split-fp16 mma.sync, a = hi +
+// lo / 2048, so the products stay fp32-exact); the eval head's two layers as split-K partial products
+// (linear_split_kernel) summed in a fixed order by linear_sum_kernel; expected_score_kernel (softmax times the bin
+// centres). fp32 arithmetic throughout, where the reference uses tf32 matmuls.
 #include <string>
 
 #include "common.cuh"
