@@ -396,4 +396,18 @@ int fry_forward_lean(const FryNetwork* n, const uint8_t* lean_rows, int B, float
     return run_forward(n, nullptr, lean_rows, B, rows, answers, workspace, forward_bytes, stream);
 }
 
+size_t fry_gptq_workspace_bytes(int N, int K) { return N > 0 && K > 0 ? fry::GptqWorkspace(N, K).total : 0; }
+
+int fry_gptq(const double* weight, const double* hessian, int N, int K, int8_t* q, float* scale, void* workspace,
+             size_t workspace_bytes, void* stream) {
+    if (!weight || !hessian || !q || !scale || !workspace)
+        return fail(FRY_ERROR_SHAPE, "fry_gptq needs its weight, hessian, outputs and workspace");
+    if (!aligned16(workspace) || reinterpret_cast<uintptr_t>(weight) % 8 != 0 || reinterpret_cast<uintptr_t>(hessian) % 8 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_gptq needs fp64-aligned inputs and a 16-byte aligned workspace");
+    std::string detail;
+    const cudaError_t status = fry::gptq(weight, hessian, N, K, q, scale, workspace, workspace_bytes, as_stream(stream), &detail);
+    if (status == cudaErrorInvalidValue && !detail.empty()) return fail(FRY_ERROR_SHAPE, detail);
+    return check(status, "fry_gptq");
+}
+
 }  // extern "C"

@@ -24,6 +24,7 @@ enum DeviceError : int {
     kBadShape = 3,         // a launch got a shape its kernel does not take
     kMisaligned = 4,       // dynamic shared memory did not start on the 1024-byte boundary a kernel lays out from
     kBadColumn = 5,        // a lean lane's answer column outside the answer row
+    kNotPositiveDefinite = 6,  // a GPTQ Cholesky factorization met a pivot that is not positive (where: the column)
 };
 
 // Set by kernels on a failure they can detect; read and cleared by fry_device_status(). The library is one

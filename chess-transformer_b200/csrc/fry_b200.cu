@@ -4,6 +4,7 @@
 #include "rows.cu"
 #include "attention.cu"
 #include "heads.cu"
+#include "gptq.cu"
 #include "abi.cu"
 #include "noalloc.cu"
 #include "lanes.cu"

@@ -107,4 +107,13 @@ size_t heads_workspace_bytes(int B, int D);
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
                   int D, cudaStream_t stream, std::string* error, const uint8_t* lean_rows = nullptr, float* lean_answers = nullptr);
 
+// GPTQ (engine/quantization.py:76-99): weight fp64 [N, K], hessian fp64 [K, K] -> q int8 [N, K], scale fp32 [N]. The
+// workspace holds fp64 copies of both ([K, K] twice, [N, K]), a block's errors [N, 128], the fp64 scales and the dead flags.
+struct GptqWorkspace {
+    size_t hessian, inverse, weight, errors, scale, dead, total;
+    GptqWorkspace(size_t N, size_t K);
+};
+cudaError_t gptq(const double* weight, const double* hessian, int N, int K, int8_t* q, float* scale, void* workspace,
+                 size_t workspace_bytes, cudaStream_t stream, std::string* error);
+
 }  // namespace fry

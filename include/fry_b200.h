@@ -32,7 +32,8 @@ const char* fry_version(void);
 
 /* Reads the current device's status word: *code 0 if no kernel recorded a fault, else the code (1 a bounded wait timed
  * out, 2 a board token outside the vocabulary, 3 a launch shape a kernel does not take, 4 misaligned shared memory, 5 a
- * lean lane's answer column outside the answer row) and *where its site. clear != 0 resets it. Synchronous. */
+ * lean lane's answer column outside the answer row, 6 a GPTQ Hessian that is not positive definite) and *where its
+ * site. clear != 0 resets it. Synchronous. */
 int fry_device_status(int* code, int* where, int clear);
 
 /* ---- block ops: each replaces one torch custom op of the reference ----------------------------------------------- */
@@ -211,6 +212,17 @@ int fry_forward(const FryNetwork* network, const int64_t* boards, int B, float* 
 size_t fry_forward_lean_workspace_bytes(const FryNetwork* network, int B);
 int fry_forward_lean(const FryNetwork* network, const uint8_t* lean_rows, int B, float* answers, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/* ---- GPTQ: the offline rounding of a block's weights to Int8Weights ---------------------------------------------------
+ * `gptq` (engine/quantization.py:76-99, Frantar et al. 2022) in fp64: weight [N, K] and the input Hessian [K, K] (both
+ * fp64, device) -> q int8 [N, K] and scale fp32 [N], as the reference returns them. Inputs whose Hessian diagonal is zero
+ * get zero weights; the diagonal is dampened by 0.01 of its mean; columns are rounded half to even in blocks of 128,
+ * each column's error spread over the later ones through the inverse Hessian's upper Cholesky factor. A Hessian that is
+ * not positive definite is recorded in the device status (code 6, where = the column), as the reference's
+ * torch.linalg.cholesky raises. Enqueue only; 0 < N <= 262144, 0 < K <= 4096. */
+size_t fry_gptq_workspace_bytes(int N, int K);
+int fry_gptq(const double* weight, const double* hessian, int N, int K, int8_t* q, float* scale, void* workspace,
+             size_t workspace_bytes, void* stream);
 
 /* ---- lanes: the batch runtime in C++ ------------------------------------------------------------------------------
  * `GraphedBatches` and `Lane` (engine/inference.py:85-225) with the CUDA runtime calls of engine/cuda_runtime.py, and no
