@@ -410,4 +410,13 @@ int fry_gptq(const double* weight, const double* hessian, int N, int K, int8_t* 
     return check(status, "fry_gptq");
 }
 
+int fry_hessian_accumulate(const double* x, int rows, int K, double* hessian, void* stream) {
+    if ((rows > 0 && !x) || !hessian || reinterpret_cast<uintptr_t>(x) % 8 != 0 || reinterpret_cast<uintptr_t>(hessian) % 8 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_hessian_accumulate needs fp64-aligned x and hessian");
+    std::string detail;
+    const cudaError_t status = fry::hessian_accumulate(x, rows, K, hessian, as_stream(stream), &detail);
+    if (status == cudaErrorInvalidValue && !detail.empty()) return fail(FRY_ERROR_SHAPE, detail);
+    return check(status, "fry_hessian_accumulate");
+}
+
 }  // extern "C"

@@ -163,6 +163,52 @@ __global__ void gptq_trailing_kernel(double* __restrict__ W, const double* __res
     W[at] = __dsub_rn(W[at], s);
 }
 
+// H [K, K] += x^T x for x [rows, K] fp64 (the input sums of engine/quantization.py:103-119): a CTA a 32 x 32 tile of H
+// on or below the diagonal, 16 x 16 threads of 2 x 2 outputs, rows in steps of 32 through shared memory. Each output sums
+// its rows in order, is added to H, and is mirrored above the diagonal, so H stays exactly symmetric.
+__global__ void __launch_bounds__(256) hessian_accumulate_kernel(const double* __restrict__ x, double* __restrict__ H, int rows, int K) {
+    if (blockIdx.y < blockIdx.x) return;
+    __shared__ double xa[32][33], xb[32][33];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4, a0 = blockIdx.y * 32, b0 = blockIdx.x * 32;
+    double acc[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+    for (int r0 = 0; r0 < rows; r0 += 32) {
+        for (int i = threadIdx.x; i < 32 * 32; i += blockDim.x) {
+            const int rr = i >> 5, cc = i & 31, r = r0 + rr;
+            xa[rr][cc] = r < rows && a0 + cc < K ? x[static_cast<size_t>(r) * K + a0 + cc] : 0.0;
+            xb[rr][cc] = r < rows && b0 + cc < K ? x[static_cast<size_t>(r) * K + b0 + cc] : 0.0;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int rr = 0; rr < 32; ++rr)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 2; ++j) acc[i][j] = __fma_rn(xa[rr][ty * 2 + i], xb[rr][tx * 2 + j], acc[i][j]);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int a = a0 + ty * 2 + i, b = b0 + tx * 2 + j;
+            if (a >= K || b >= K) continue;
+            const size_t at = static_cast<size_t>(a) * K + b;
+            H[at] = __dadd_rn(H[at], acc[i][j]);
+            if (a0 != b0) H[static_cast<size_t>(b) * K + a] = H[at];
+        }
+}
+
+cudaError_t hessian_accumulate(const double* x, int rows, int K, double* H, cudaStream_t stream, std::string* error) {
+    if (rows < 0 || K <= 0 || K > kGptqMaxK) {
+        if (error) *error = "fry_hessian_accumulate takes rows >= 0 and 0 < K <= " + std::to_string(kGptqMaxK);
+        return cudaErrorInvalidValue;
+    }
+    if (rows == 0) return cudaSuccess;
+    const int tiles = (K + 31) / 32;
+    hessian_accumulate_kernel<<<dim3(tiles, tiles), 256, 0, stream>>>(x, H, rows, K);
+    return cudaGetLastError();
+}
+
 // A = L L^T in place (lower triangle), one column at a time.
 cudaError_t cholesky_lower(double* A, int K, cudaStream_t stream) {
     const dim3 tile(32, 8);

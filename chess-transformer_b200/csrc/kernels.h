@@ -115,5 +115,7 @@ struct GptqWorkspace {
 };
 cudaError_t gptq(const double* weight, const double* hessian, int N, int K, int8_t* q, float* scale, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream, std::string* error);
+// H [K, K] += x^T x, x [rows, K], fp64 (the input sums GPTQ's Hessians are made of)
+cudaError_t hessian_accumulate(const double* x, int rows, int K, double* H, cudaStream_t stream, std::string* error);
 
 }  // namespace fry

@@ -71,6 +71,7 @@ SIGNATURES = {
     "fry_forward_lean": ([ctypes.POINTER(FryNetwork), _ptr, _c_int, _ptr, _ptr, _size, _ptr], _c_int),
     "fry_gptq_workspace_bytes": ([_c_int, _c_int], _size),
     "fry_gptq": ([_ptr, _ptr, _c_int, _c_int, _ptr, _ptr, _ptr, _size, _ptr], _c_int),
+    "fry_hessian_accumulate": ([_ptr, _c_int, _c_int, _ptr, _ptr], _c_int),
     "fry_lanes_create": ([ctypes.POINTER(FryNetwork), ctypes.POINTER(_c_int), _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_ptr)], _c_int),
     "fry_lanes_destroy": ([_ptr], _c_int),
     "fry_lanes_free_lane": ([_ptr, ctypes.POINTER(_c_int)], _c_int),

@@ -1,12 +1,14 @@
-"""GPTQ on the device: the drop-in for the reference's `gptq` (engine/quantization.py:76-99), which
-`compute_int8_weights` (:104-140) calls for every int8 matmul of every block. One C-ABI call (fry_gptq) runs it in fp64
-on the weight's GPU; the answer is the reference's (int8 [N, K], fp32 scale [N]) on that device.
+"""GPTQ on the device: drop-ins for the reference's `gptq` (engine/quantization.py:76-99), `input_hessians` (:103-119)
+and `compute_int8_weights` (:122-140). fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate
+sums the inputs x^T x that its Hessian is made of; the answers are the reference's Int8Weights.
 """
 import ctypes
 
 import torch
+from torch import nn
 
 from .library import FryError, library
+from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, down_inputs, geometry, hadamard
 
 NOT_POSITIVE_DEFINITE = 6  # the device status code fry_gptq records
 
@@ -38,3 +40,61 @@ def gptq(weight: torch.Tensor, hessian: torch.Tensor) -> tuple[torch.Tensor, tor
             lib.device_status(clear=True)
             raise FryError(f"gptq: the dampened Hessian is not positive definite (Cholesky pivot {where})")
     return integers, scale
+
+
+@torch.no_grad()
+def input_hessians(model: nn.Module, boards: torch.Tensor, batch: int = 128) -> list[dict[str, torch.Tensor]]:
+    """engine/quantization.py:103-119: per block of `model` (the reference's ChessTransformer, or any module with its
+    `encoder` blocks and their Q, mlp.gate_projection and mlp.down_projection), the fp64 sum over the boards' tokens of
+    x^T x for the inputs x of its projection, gate_up and down matmuls, summed on the GPU by fry_hessian_accumulate."""
+    lib = library()
+    device = next(model.parameters()).device
+    device = device if device.type == "cuda" else torch.device("cuda")
+    hessians = [{} for _ in model.encoder]
+    hooks = []
+    for block, sums in zip(model.encoder, hessians):
+        for name, layer in (("projection", block.Q), ("gate_up", block.mlp.gate_projection), ("down", block.mlp.down_projection)):
+            def add(module, inputs, name=name, sums=sums):
+                x = inputs[0].reshape(-1, inputs[0].shape[-1]).to(device=device, dtype=torch.float64).contiguous()
+                if name not in sums:
+                    sums[name] = torch.zeros(x.shape[1], x.shape[1], dtype=torch.float64, device=device)
+                lib.fry_hessian_accumulate(ctypes.c_void_p(x.data_ptr()), x.shape[0], x.shape[1], ctypes.c_void_p(sums[name].data_ptr()),
+                                           ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+            hooks.append(layer.register_forward_pre_hook(add))
+    try:
+        for start in range(0, len(boards), batch):
+            model(boards[start:start + batch].to(next(model.parameters()).device))
+    finally:
+        for hook in hooks:
+            hook.remove()
+    torch.cuda.synchronize(device)
+    return hessians
+
+
+def gptq_inputs(state: dict, settings: dict, layer: int, sums: dict[str, torch.Tensor]) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+    """engine/quantization.py:129-139: a block's (weight, hessian) pairs as gptq takes them, fp64 on the sums' device:
+    projection = Q|K|V|template mix rows with the projection's sums; gate_up = gate rows then up rows with gate_up's; down
+    zero-padded to a multiple of 128 inputs and rotated, weight = pad(W) R / 32 and hessian = R^T pad(H) R, R the
+    block-diagonal 32 x 32 Hadamard matrix."""
+    g = geometry(settings)
+    device = sums["down"].device
+    p = f"encoder.{layer}."
+    w = lambda name: state[p + name].to(device=device, dtype=torch.float64)
+    projection = torch.cat([w(n + ".weight") for n in ("Q", "K", "V", "template_mix")])
+    gate_up = torch.cat([w("mlp.gate_projection.weight"), w("mlp.up_projection.weight")])
+    width = down_inputs(g["hidden"])
+    padding = width - g["hidden"]
+    rotation = torch.block_diag(*[hadamard(HADAMARD_BLOCK)] * (width // HADAMARD_BLOCK)).to(device=device, dtype=torch.float64)
+    padded = nn.functional.pad(sums["down"].double(), (0, padding, 0, padding))
+    down = nn.functional.pad(w("mlp.down_projection.weight"), (0, padding)) @ rotation / HADAMARD_BLOCK
+    return {"projection": (projection, sums["projection"].double()), "gate_up": (gate_up, sums["gate_up"].double()),
+            "down": (down, rotation.t() @ padded @ rotation)}
+
+
+def compute_int8_weights(state: dict, settings: dict, hessians: list[dict[str, torch.Tensor]], layers: list[int] | None = None) -> dict:
+    """engine/quantization.py:122-140: Int8Weights {layer: {"projection"|"gate_up"|"down": (int8 [N, K], fp32 [N])}} of a
+    state dict (named as the reference's ChessTransformer names its weights) from input_hessians' sums, every block but
+    the last FP16_LAST_LAYERS by default, each matmul rounded by GPTQ on the device."""
+    layers = range(len(hessians) - FP16_LAST_LAYERS) if layers is None else layers
+    return {layer: {name: gptq(weight, hessian) for name, (weight, hessian) in gptq_inputs(state, settings, layer, hessians[layer]).items()}
+            for layer in layers}

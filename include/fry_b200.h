@@ -223,6 +223,9 @@ int fry_forward_lean(const FryNetwork* network, const uint8_t* lean_rows, int B,
 size_t fry_gptq_workspace_bytes(int N, int K);
 int fry_gptq(const double* weight, const double* hessian, int N, int K, int8_t* q, float* scale, void* workspace,
              size_t workspace_bytes, void* stream);
+/* The Hessians GPTQ takes (`input_hessians`, engine/quantization.py:103-119): hessian [K, K] += x^T x for a matmul's
+ * inputs x [rows, K], fp64 on the device. The sum is exactly symmetric. Enqueue only; 0 < K <= 4096. */
+int fry_hessian_accumulate(const double* x, int rows, int K, double* hessian, void* stream);
 
 /* ---- lanes: the batch runtime in C++ ------------------------------------------------------------------------------
  * `GraphedBatches` and `Lane` (engine/inference.py:85-225) with the CUDA runtime calls of engine/cuda_runtime.py, and no

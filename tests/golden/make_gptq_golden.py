@@ -9,7 +9,8 @@ It sets up the reference's modules as make_golden.py does, then runs `compute_in
 (weight, hessian) that each call of the reference's `gptq` receives for block 0: the projection (K 128, one column
 block) and the down matmul (padded from 320 inputs to 384 and rotated: three column blocks, 64 inputs with no
 curvature). The recorded inputs are rounded to fp32 to halve the file, and the reference's `gptq` is run again on those
-rounded values, so the stored outputs are exactly the reference's for the stored inputs.
+rounded values, so the stored outputs are exactly the reference's for the stored inputs. Block 0's raw sums from
+`input_hessians` (before the down's padding and rotation) are stored too, rounded to fp32, for the layout step.
 """
 import sys
 from pathlib import Path
@@ -32,13 +33,16 @@ def main() -> None:
         return real(weight, hessian)
 
     mg.ref_quantization.gptq = recorded
+    boards = torch.from_numpy(mg.golden_boards(64, 21)).long()
     try:
         model = mg.reference_model(mg.SMALL, 10).half_except_heads(torch.float64)
-        mg.ref_quantization.compute_int8_weights(model, torch.from_numpy(mg.golden_boards(64, 21)).long())
+        mg.ref_quantization.compute_int8_weights(model, boards)
+        # the sums compute_int8_weights starts from (input_hessians, :103-119), block 0's
+        raw = mg.ref_quantization.input_hessians(model, boards)[0]
     finally:
         mg.ref_quantization.gptq = real
     # block 0's calls, in compute_int8_weights' order: projection, gate_up, down
-    out = {}
+    out = {f"raw_{name}_hessian": raw[name].float().numpy() for name in ("projection", "gate_up", "down")}
     for name, (weight, hessian) in (("projection", calls[0]), ("down", calls[2])):
         weight32, hessian32 = weight.float(), hessian.float()
         integers, scale = real(weight32.double(), hessian32.double())

@@ -49,3 +49,22 @@ def test_gptq_is_refused_on_the_host_before_any_cuda_call():
     with pytest.raises(FryError, match="needs its weight"):
         lib.fry_gptq(None, buffer, 8, 128, buffer, buffer, buffer, 1 << 40, None)
     assert lib.fry_gptq_workspace_bytes(0, 128) == 0 and lib.fry_gptq_workspace_bytes(768, 1024) >= (2 * 1024 * 1024 + 768 * 1024) * 8
+
+
+def test_the_layout_gptq_takes_is_the_references():
+    # engine/quantization.py:129-139: from block 0's raw sums (input_hessians, :103-119) to the (weight, hessian) pairs the
+    # reference's gptq received: the projection's rows Q|K|V|template mix with its sums, the down's padded and rotated pair
+    import torch
+    from chess_transformer_b200.quantization import gptq_inputs
+    from oracle import model as om
+    from tests.conftest import SMALL
+    golden = np.load(GOLDEN)
+    sums = {name: torch.from_numpy(golden[f"raw_{name}_hessian"]).double() for name in ("projection", "gate_up", "down")}
+    pairs = gptq_inputs(om.seeded_state_dict(SMALL, 10), SMALL, 0, sums)
+    assert torch.equal(pairs["projection"][0].float(), torch.from_numpy(golden["projection_weight"]))
+    assert torch.equal(pairs["projection"][1].float(), torch.from_numpy(golden["projection_hessian"]))
+    assert torch.allclose(pairs["down"][0].float(), torch.from_numpy(golden["down_weight"]), rtol=1e-6, atol=0)
+    recorded = torch.from_numpy(golden["down_hessian"]).double()
+    # the recorded pair was rotated from the fp64 sums; these are the sums rounded to fp32 first
+    assert torch.allclose(pairs["down"][1], recorded, rtol=1e-5, atol=1e-6 * recorded.abs().max().item())
+    assert pairs["gate_up"][0].shape == (2 * SMALL["mlp_hidden"], SMALL["d_model"])

@@ -59,3 +59,83 @@ def test_a_hessian_that_is_not_positive_definite_raises_as_the_references_choles
     with pytest.raises(FryError, match="not positive definite"):
         gptq(torch.randn(16, 64, dtype=torch.float64).cuda(), hessian.cuda())
     assert lib.device_status() == before
+
+
+def test_hessian_accumulate_sums_x_transpose_x_exactly_symmetric():
+    lib = library()
+    rng = np.random.default_rng(7)
+    first, second = rng.standard_normal((700, 384)), rng.standard_normal((70, 384)) * 3
+    hessian = torch.zeros(384, 384, dtype=torch.float64, device="cuda")
+    for x in (first, second):
+        xs = torch.from_numpy(x).cuda()
+        lib.fry_hessian_accumulate(xs.data_ptr(), xs.shape[0], xs.shape[1], hessian.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    found = hessian.cpu().numpy()
+    assert np.array_equal(found, found.T)
+    assert np.allclose(found, first.T @ first + second.T @ second, rtol=1e-12, atol=1e-10)
+
+
+def test_input_hessians_sum_each_matmuls_inputs():
+    # engine/quantization.py:103-119 on a module with the reference's block structure: the sums of x^T x over the inputs
+    # of each block's Q, gate_projection and down_projection
+    from torch import nn
+    from chess_transformer_b200.quantization import input_hessians
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.Q = nn.Linear(64, 64, bias=False)
+            self.mlp = nn.Module()
+            self.mlp.gate_projection, self.mlp.up_projection = nn.Linear(64, 96, bias=False), nn.Linear(64, 96, bias=False)
+            self.mlp.down_projection = nn.Linear(96, 64, bias=False)
+
+        def forward(self, x):
+            x = x + self.Q(x).tanh()
+            return x + self.mlp.down_projection(nn.functional.silu(self.mlp.gate_projection(x)) * self.mlp.up_projection(x))
+
+    class Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Embedding(20, 64)
+            self.encoder = nn.ModuleList([Block(), Block()])
+
+        def forward(self, boards):
+            x = self.embed(boards)
+            for block in self.encoder:
+                x = block(x)
+            return x
+
+    torch.manual_seed(3)
+    model = Model().double().cuda()
+    boards = torch.randint(0, 20, (300, 70), device="cuda")
+    found = input_hessians(model, boards, batch=128)
+    expected = [{} for _ in model.encoder]
+    hooks = [layer.register_forward_pre_hook(lambda module, inputs, sums=sums, name=name: sums.__setitem__(
+                 name, sums.get(name, 0) + inputs[0].reshape(-1, inputs[0].shape[-1]).t() @ inputs[0].reshape(-1, inputs[0].shape[-1])))
+             for block, sums in zip(model.encoder, expected)
+             for name, layer in (("projection", block.Q), ("gate_up", block.mlp.gate_projection), ("down", block.mlp.down_projection))]
+    with torch.no_grad():
+        for start in range(0, 300, 128):
+            model(boards[start:start + 128])
+    for hook in hooks:
+        hook.remove()
+    for got, want in zip(found, expected):
+        for name in ("projection", "gate_up", "down"):
+            assert torch.allclose(got[name], want[name], rtol=1e-11, atol=1e-9)
+
+
+def test_compute_int8_weights_from_the_references_sums_is_the_references():
+    # engine/quantization.py:122-140 from block 0's raw sums: the projection's pair is the reference's to the bit, so its
+    # int8 weights are too; the down's Hessian is rotated here from the sums rounded to fp32, so a weight on a rounding
+    # boundary may land one step apart
+    from chess_transformer_b200.quantization import compute_int8_weights
+    from oracle import model as om
+    from tests.conftest import SMALL
+    golden = np.load(GOLDEN)
+    sums = {name: torch.from_numpy(golden[f"raw_{name}_hessian"]).double().cuda() for name in ("projection", "gate_up", "down")}
+    weights = compute_int8_weights(om.seeded_state_dict(SMALL, 10), SMALL, [sums], layers=[0])
+    assert set(weights) == {0} and set(weights[0]) == {"projection", "gate_up", "down"}
+    assert np.array_equal(weights[0]["projection"][0].cpu().numpy(), golden["projection_int8"])
+    assert np.array_equal(weights[0]["projection"][1].cpu().numpy(), golden["projection_scale"])
+    down = weights[0]["down"][0].cpu().numpy()
+    assert (down == golden["down_int8"]).mean() >= 0.999 and np.abs(down.astype(int) - golden["down_int8"]).max() <= 1
+    assert np.array_equal(weights[0]["down"][1].cpu().numpy(), golden["down_scale"])
