@@ -8,7 +8,7 @@ import torch
 from torch import nn
 
 from .library import FryError, library
-from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, down_inputs, geometry, hadamard
+from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, down_inputs, hadamard
 
 NOT_POSITIVE_DEFINITE = 6  # the device status code fry_gptq records
 
@@ -71,19 +71,19 @@ def input_hessians(model: nn.Module, boards: torch.Tensor, batch: int = 128) -> 
     return hessians
 
 
-def gptq_inputs(state: dict, settings: dict, layer: int, sums: dict[str, torch.Tensor]) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+def gptq_inputs(state: dict, layer: int, sums: dict[str, torch.Tensor]) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
     """engine/quantization.py:129-139: a block's (weight, hessian) pairs as gptq takes them, fp64 on the sums' device:
     projection = Q|K|V|template mix rows with the projection's sums; gate_up = gate rows then up rows with gate_up's; down
     zero-padded to a multiple of 128 inputs and rotated, weight = pad(W) R / 32 and hessian = R^T pad(H) R, R the
-    block-diagonal 32 x 32 Hadamard matrix."""
-    g = geometry(settings)
+    block-diagonal 32 x 32 Hadamard matrix. `state` is named as the reference's ChessTransformer names its weights."""
     device = sums["down"].device
     p = f"encoder.{layer}."
     w = lambda name: state[p + name].to(device=device, dtype=torch.float64)
     projection = torch.cat([w(n + ".weight") for n in ("Q", "K", "V", "template_mix")])
     gate_up = torch.cat([w("mlp.gate_projection.weight"), w("mlp.up_projection.weight")])
-    width = down_inputs(g["hidden"])
-    padding = width - g["hidden"]
+    hidden = state[p + "mlp.down_projection.weight"].shape[1]
+    width = down_inputs(hidden)
+    padding = width - hidden
     rotation = torch.block_diag(*[hadamard(HADAMARD_BLOCK)] * (width // HADAMARD_BLOCK)).to(device=device, dtype=torch.float64)
     padded = nn.functional.pad(sums["down"].double(), (0, padding, 0, padding))
     down = nn.functional.pad(w("mlp.down_projection.weight"), (0, padding)) @ rotation / HADAMARD_BLOCK
@@ -91,10 +91,17 @@ def gptq_inputs(state: dict, settings: dict, layer: int, sums: dict[str, torch.T
             "down": (down, rotation.t() @ padded @ rotation)}
 
 
-def compute_int8_weights(state: dict, settings: dict, hessians: list[dict[str, torch.Tensor]], layers: list[int] | None = None) -> dict:
-    """engine/quantization.py:122-140: Int8Weights {layer: {"projection"|"gate_up"|"down": (int8 [N, K], fp32 [N])}} of a
-    state dict (named as the reference's ChessTransformer names its weights) from input_hessians' sums, every block but
-    the last FP16_LAST_LAYERS by default, each matmul rounded by GPTQ on the device."""
+def int8_weights_from_sums(state: dict, hessians: list[dict[str, torch.Tensor]], layers: list[int] | None = None) -> dict:
+    """Int8Weights {layer: {"projection"|"gate_up"|"down": (int8 [N, K], fp32 [N])}} of a state dict from input_hessians'
+    sums, every block but the last FP16_LAST_LAYERS by default (engine/quantization.py:126), each matmul rounded by GPTQ
+    on the device."""
     layers = range(len(hessians) - FP16_LAST_LAYERS) if layers is None else layers
-    return {layer: {name: gptq(weight, hessian) for name, (weight, hessian) in gptq_inputs(state, settings, layer, hessians[layer]).items()}
+    return {layer: {name: gptq(weight, hessian) for name, (weight, hessian) in gptq_inputs(state, layer, hessians[layer]).items()}
             for layer in layers}
+
+
+@torch.no_grad()
+def compute_int8_weights(model: nn.Module, boards: torch.Tensor) -> dict:
+    """engine/quantization.py:122-140, same signature: the Int8Weights of `model` (the reference's ChessTransformer,
+    loaded as int8_weights loads it, :200-201) calibrated on `boards`, every block but the last."""
+    return int8_weights_from_sums(model.state_dict(), input_hessians(model, boards))

@@ -60,7 +60,7 @@ def test_the_layout_gptq_takes_is_the_references():
     from tests.conftest import SMALL
     golden = np.load(GOLDEN)
     sums = {name: torch.from_numpy(golden[f"raw_{name}_hessian"]).double() for name in ("projection", "gate_up", "down")}
-    pairs = gptq_inputs(om.seeded_state_dict(SMALL, 10), SMALL, 0, sums)
+    pairs = gptq_inputs(om.seeded_state_dict(SMALL, 10), 0, sums)
     assert torch.equal(pairs["projection"][0].float(), torch.from_numpy(golden["projection_weight"]))
     assert torch.equal(pairs["projection"][1].float(), torch.from_numpy(golden["projection_hessian"]))
     assert torch.allclose(pairs["down"][0].float(), torch.from_numpy(golden["down_weight"]), rtol=1e-6, atol=0)

@@ -123,16 +123,16 @@ def test_input_hessians_sum_each_matmuls_inputs():
             assert torch.allclose(got[name], want[name], rtol=1e-11, atol=1e-9)
 
 
-def test_compute_int8_weights_from_the_references_sums_is_the_references():
+def test_int8_weights_from_the_references_sums_are_the_references():
     # engine/quantization.py:122-140 from block 0's raw sums: the projection's pair is the reference's to the bit, so its
     # int8 weights are too; the down's Hessian is rotated here from the sums rounded to fp32, so a weight on a rounding
     # boundary may land one step apart
-    from chess_transformer_b200.quantization import compute_int8_weights
+    from chess_transformer_b200.quantization import int8_weights_from_sums
     from oracle import model as om
     from tests.conftest import SMALL
     golden = np.load(GOLDEN)
     sums = {name: torch.from_numpy(golden[f"raw_{name}_hessian"]).double().cuda() for name in ("projection", "gate_up", "down")}
-    weights = compute_int8_weights(om.seeded_state_dict(SMALL, 10), SMALL, [sums], layers=[0])
+    weights = int8_weights_from_sums(om.seeded_state_dict(SMALL, 10), [sums], layers=[0])
     assert set(weights) == {0} and set(weights[0]) == {"projection", "gate_up", "down"}
     assert np.array_equal(weights[0]["projection"][0].cpu().numpy(), golden["projection_int8"])
     assert np.array_equal(weights[0]["projection"][1].cpu().numpy(), golden["projection_scale"])
