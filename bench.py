@@ -28,6 +28,7 @@ sys.path.insert(0, str(ROOT))
 
 BATCH = 256
 LATENCY_BATCH = 64
+E2E_LANES = 2  # batches in flight in the end-to-end runs (GraphedBatches' default, engine/inference.py:149)
 # the library's kernels a forward launches: the embedding; per block 2 row norms, projection, attention, attention-out,
 # gate_up, rotate_quant, down (8 x 28); the heads' final norm, f16 GEMM, narrow, policy, 2 x (split, sum), expected score
 LAUNCHES_PER_FORWARD = 1 + 8 * 28 + 9
@@ -334,21 +335,33 @@ def main() -> None:
         dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
         seconds = slowest.item()
 
-    # end to end through the runtime: pinned host boards in, graph replay, answer rows out, every step
+    # end to end through the runtime: pinned host boards in, graph replay, answer rows out, every step; two lanes, each
+    # step launched before the previous one is collected, as the reference's search keeps its lanes in flight
+    # (engine/inference.py:144-146)
+    def pipelined_seconds(launch, collect) -> float:
+        def run(count: int) -> None:
+            pending = launch()
+            for _ in range(count - 1):
+                following = launch()
+                collect(pending)
+                pending = following
+            collect(pending)
+
+        run(max(3, args.warmup))
+        if world > 1:
+            dist.barrier()
+        start = time.perf_counter()
+        run(args.steps)
+        elapsed = time.perf_counter() - start
+        if world > 1:
+            slowest = torch.tensor([elapsed], device=device)
+            dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+            elapsed = slowest.item()
+        return elapsed
+
     host_boards = random_boards(BATCH, 99 + rank)
-    batches = GraphedBatches(network, [LATENCY_BATCH, BATCH], in_flight=1)
-    for _ in range(max(3, args.warmup)):
-        batches.collect(batches.launch(host_boards))
-    if world > 1:
-        dist.barrier()
-    start = time.perf_counter()
-    for _ in range(args.steps):
-        batches.collect(batches.launch(host_boards))
-    e2e_seconds = time.perf_counter() - start
-    if world > 1:
-        slowest = torch.tensor([e2e_seconds], device=device)
-        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
-        e2e_seconds = slowest.item()
+    batches = GraphedBatches(network, [LATENCY_BATCH, BATCH], in_flight=E2E_LANES)
+    e2e_seconds = pipelined_seconds(lambda: batches.launch(host_boards), batches.collect)
 
     # the same through lean lanes, the Rust round loop's format: rows of tokens and answer columns in (30 moves' columns
     # a board, then the expected score's), 219 answers a board out
@@ -357,47 +370,19 @@ def main() -> None:
     columns = np.full((BATCH, LEAN_COLUMNS), ANSWER_WIDTH - 1, dtype="<i2")
     columns[:, :30] = np.random.default_rng(7 + rank).integers(0, ANSWER_WIDTH - 1, size=(BATCH, 30))
     lean_rows[:, TOKENS_PER_BOARD:] = columns.view(np.uint8).reshape(BATCH, -1)
-    lean_batches = GraphedBatches(network, [BATCH], in_flight=1, lean=True)
 
-    def lean_step():
-        lane = lean_batches.free_lane()
+    def lean_launch(runtime):
+        lane = runtime.free_lane()
         lane.rows_array[:BATCH] = lean_rows
-        lean_batches.collect(lean_batches.launch_filled(lane, BATCH))
+        return runtime.launch_filled(lane, BATCH)
 
-    for _ in range(max(3, args.warmup)):
-        lean_step()
-    if world > 1:
-        dist.barrier()
-    start = time.perf_counter()
-    for _ in range(args.steps):
-        lean_step()
-    lean_seconds = time.perf_counter() - start
-    if world > 1:
-        slowest = torch.tensor([lean_seconds], device=device)
-        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
-        lean_seconds = slowest.item()
+    lean_batches = GraphedBatches(network, [BATCH], in_flight=E2E_LANES, lean=True)
+    lean_seconds = pipelined_seconds(lambda: lean_launch(lean_batches), lean_batches.collect)
     del lean_batches
 
     # the same lean steps through the library's C++ lanes (fry_lanes_*): one C-ABI call to launch, one to collect
-    native = NativeBatches(network, [BATCH], in_flight=1, lean=True)
-
-    def native_step():
-        lane = native.free_lane()
-        lane.rows_array[:BATCH] = lean_rows
-        native.collect(native.launch_filled(lane, BATCH))
-
-    for _ in range(max(3, args.warmup)):
-        native_step()
-    if world > 1:
-        dist.barrier()
-    start = time.perf_counter()
-    for _ in range(args.steps):
-        native_step()
-    native_seconds = time.perf_counter() - start
-    if world > 1:
-        slowest = torch.tensor([native_seconds], device=device)
-        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
-        native_seconds = slowest.item()
+    native = NativeBatches(network, [BATCH], in_flight=E2E_LANES, lean=True)
+    native_seconds = pipelined_seconds(lambda: lean_launch(native), native.collect)
     native.close()
 
     extra = {}
@@ -431,7 +416,7 @@ def main() -> None:
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
                 "config": {**workload_config(world), "parallelism": f"replicas x{world}"},
                 "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
-                        "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4},
+                        "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4, "lanes": E2E_LANES},
                 "e2e_lean": {"value": BATCH * args.steps * world / lean_seconds, "unit": "positions/s",
                              "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4},
                 "e2e_lean_native": {"value": BATCH * args.steps * world / native_seconds, "unit": "positions/s",
