@@ -416,7 +416,9 @@ def main() -> None:
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
                 "config": {**workload_config(world), "parallelism": f"replicas x{world}"},
                 "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
-                        "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4, "lanes": E2E_LANES},
+                        "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4, "lanes": E2E_LANES,
+                        "note": "lanes on their own streams, a step launched before the previous one is collected; "
+                                "no L2 flush between steps, unlike value"},
                 "e2e_lean": {"value": BATCH * args.steps * world / lean_seconds, "unit": "positions/s",
                              "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4},
                 "e2e_lean_native": {"value": BATCH * args.steps * world / native_seconds, "unit": "positions/s",
