@@ -24,6 +24,7 @@ constexpr int kHeadTokens = 70, kHeadSquares = 64, kNarrow = 21, kNarrowStride =
 constexpr int kEvalInputs = kHeadTokens * kDown;  // the eval head's first layer takes 70 x 16 GELU'd board-down units
 constexpr float kLoScale = 2048.0f;
 constexpr int kLinearTile = 64, kLinearStep = 16;  // linear_split_kernel: 64 boards x 64 outputs a CTA, K in steps of 16
+static_assert(kLinearTile * kLinearStep == 4 * 256, "linear_split_kernel: one float4 of x and of W a thread a step");
 constexpr int kEvalSplits = 8;  // the eval head's layers: K in 8 splits, whatever the batch
 // narrow_kernel: the 21 outputs padded to 3 mma tiles of 8; 8 tiles of 16 rows a CTA, the columns in kNarrowParts parts
 constexpr int kNarrowTile = 24, kNarrowTiles = 8, kNarrowParts = 2, kNarrowLoads = 12;
