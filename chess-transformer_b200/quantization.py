@@ -1,5 +1,5 @@
-"""GPTQ on the device: drop-ins for the reference's `gptq` (engine/quantization.py:76-99), `input_hessians` (:103-119)
-and `compute_int8_weights` (:122-140). fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate
+"""GPTQ on the device: drop-ins for the reference's `gptq` (engine/quantization.py:76-99), `input_hessians` (:103-119),
+`compute_int8_weights` (:122-140) and `block_errors` (:144-169), the ranking that picks the blocks kept in fp16. fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate
 sums the inputs x^T x that its Hessian is made of; the answers are the reference's Int8Weights.
 """
 import ctypes
@@ -8,7 +8,7 @@ import torch
 from torch import nn
 
 from .library import FryError, library
-from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, down_inputs, hadamard
+from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, Int8Network, down_inputs, hadamard
 
 NOT_POSITIVE_DEFINITE = 6  # the device status code fry_gptq records
 
@@ -105,3 +105,27 @@ def compute_int8_weights(model: nn.Module, boards: torch.Tensor) -> dict:
     """engine/quantization.py:122-140, same signature: the Int8Weights of `model` (the reference's ChessTransformer,
     loaded as int8_weights loads it, :200-201) calibrated on `boards`, every block but the last."""
     return int8_weights_from_sums(model.state_dict(), input_hessians(model, boards))
+
+
+@torch.no_grad()
+def block_errors(state: dict, settings: dict, weights: dict, boards: torch.Tensor, legal: torch.Tensor, batch: int = 256) -> dict[int, float]:
+    """engine/quantization.py:144-169: per block of `weights`, the mean over the boards of the total variation between
+    the policy (softmax over each board's legal moves, fp64) of the fp16 network and of the fp16 network with only that
+    block in int8. Both networks run through fry_forward (Int8Network with the one block's weights, or none). boards int64
+    [n, 70] and legal bool [n, 1968] are the calibration positions and their legal moves, which the reference reads from
+    its PGN through python-chess."""
+    device = torch.device("cuda", torch.cuda.current_device())
+    boards, legal = boards.to(device), legal.to(device=device, dtype=torch.bool)
+
+    def priors(int8_layers: list[int]) -> torch.Tensor:
+        network = Int8Network(state, settings, {layer: weights[layer] for layer in int8_layers}, device)
+        logits = torch.cat([network(boards[start:start + batch])[:, :-1] for start in range(0, len(boards), batch)])
+        return torch.softmax(logits.double().masked_fill(~legal, -torch.inf), dim=-1)
+
+    fp16 = priors([])
+    return {layer: 0.5 * (priors([layer]) - fp16).abs().sum(dim=-1).mean().item() for layer in weights}
+
+
+def fp16_choice(errors: dict[int, float], fp16_blocks: int) -> list[int]:
+    """engine/quantization.py:196-198: the fp16_blocks blocks of the largest block_errors, which stay fp16."""
+    return sorted(errors, key=errors.get, reverse=True)[:fp16_blocks]

@@ -68,3 +68,10 @@ def test_the_layout_gptq_takes_is_the_references():
     # the recorded pair was rotated from the fp64 sums; these are the sums rounded to fp32 first
     assert torch.allclose(pairs["down"][1], recorded, rtol=1e-5, atol=1e-6 * recorded.abs().max().item())
     assert pairs["gate_up"][0].shape == (2 * SMALL["mlp_hidden"], SMALL["d_model"])
+
+
+def test_the_fp16_choice_keeps_the_blocks_of_the_largest_errors():
+    # engine/quantization.py:196-198
+    from chess_transformer_b200.quantization import fp16_choice
+    errors = {0: 0.01, 1: 0.04, 2: 0.02, 3: 0.03}
+    assert fp16_choice(errors, 1) == [1] and fp16_choice(errors, 2) == [1, 3] and fp16_choice(errors, 0) == []
