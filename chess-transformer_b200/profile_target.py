@@ -3,7 +3,7 @@ that `ncu --profile-from-start off` captures exactly that work. Warm-up runs hap
 
     ncu --profile-from-start off --metrics gpu__time_duration.sum --clock-control none --csv \\
         python chess-transformer_b200/profile_target.py --batch 256 --forwards 1
-    ncu --profile-from-start off --set full --clock-control none -k regex:gemm_kernel -c 1 -o gpurun_out/gemm \\
+    ncu --profile-from-start off --set full --clock-control none -k regex:gemm_kernel -c 1 -o gemm \\
         python chess-transformer_b200/profile_target.py --gemm gate_up --batch 256
     ncu --profile-from-start off --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \\
         -k regex:gemm_kernel --csv python chess-transformer_b200/profile_target.py --gemm all --batch 256

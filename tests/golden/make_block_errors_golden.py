@@ -2,7 +2,7 @@
 on the SMALL network (seed 10, weights of std 0.1 and the policy's from-projection 8 times wider, so that one block's
 rounding moves the priors measurably) with its round-to-nearest int8 weights for blocks 0 and 1 (the last stays fp16).
 
-Run in the build container, where the reference is checked out (default /root/reference, or the path in FRY_REFERENCE):
+Run in the build container, where the reference is checked out (FRY_REFERENCE, as make_golden.py reads it):
 
     python tests/golden/make_block_errors_golden.py
 

@@ -1,7 +1,7 @@
 """Writes the golden fixtures under tests/golden/ from the reference's own code.
 
-Run in the build container, where the reference is checked out (default
-/root/reference, or the path in FRY_REFERENCE):
+Run in the build container, where the reference is checked out (the path in
+FRY_REFERENCE, or the default REFERENCE below):
 
     python tests/golden/make_golden.py
 

@@ -1,6 +1,6 @@
 """Writes tests/golden/gptq_golden.npz from the reference's own GPTQ (engine/quantization.py:76-99,104-140).
 
-Run in the build container, where the reference is checked out (default /root/reference, or the path in FRY_REFERENCE):
+Run in the build container, where the reference is checked out (FRY_REFERENCE, as make_golden.py reads it):
 
     python tests/golden/make_gptq_golden.py
 
