@@ -1,6 +1,7 @@
 """GPTQ on the device: drop-ins for the reference's `gptq` (engine/quantization.py:76-99), `input_hessians` (:103-119),
-`compute_int8_weights` (:122-140) and `block_errors` (:144-169), the ranking that picks the blocks kept in fp16. fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate
-sums the inputs x^T x that its Hessian is made of; the answers are the reference's Int8Weights.
+`compute_int8_weights` (:122-140) and `block_errors` (:144-169), the ranking that picks the blocks kept in fp16.
+fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate sums the inputs x^T x that its Hessian
+is made of; the answers are the reference's Int8Weights.
 """
 import ctypes
 
