@@ -14,7 +14,7 @@ from torch import nn
 
 from .boards import START_BOARD
 from .encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
-from .library import FryLaneHandles, library
+from .library import FryError, FryLaneHandles, library
 
 
 def small_graph_sizes(max_batch: int, chunk: int | None = None) -> list[int]:
@@ -168,6 +168,10 @@ class NativeBatches:
             handles = FryLaneHandles()
             self._lib.fry_lanes_handles(self._lanes, index, ctypes.byref(handles))
             self.lanes.append(NativeLane(index, handles, self.sizes[-1], lean))
+        if self.lanes[0].handles.device != torch.cuda.current_device():
+            device = self.lanes[0].handles.device
+            self.close()
+            raise FryError(f"the lanes were made on device {device}, not on torch's current device {torch.cuda.current_device()}")
 
     def free_lane(self) -> NativeLane:
         index = ctypes.c_int()
