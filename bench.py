@@ -143,6 +143,18 @@ class ClockSampler:
                 "source": self.source}
 
 
+def slowest_over_ranks(seconds: float, device) -> float:
+    """The job's time: the largest of the ranks' times (an all_reduce MAX over the process group, on `device`), or the
+    rank's own when it runs alone. Every rank calls it at the same point."""
+    import torch
+    import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
+        return seconds
+    slowest = torch.tensor([seconds], dtype=torch.float64, device=device)
+    dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
+    return slowest.item()
+
+
 def reference_arm(args, rank: int) -> None:
     """The reference's CPU path on the host cores: fp32 forward of a bounded sample of boards a step."""
     if rank != 0:
@@ -329,11 +341,7 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    seconds = sum(start.elapsed_time(end) for start, end in events) / 1000
-    if world > 1:
-        slowest = torch.tensor([seconds], device=device)
-        dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
-        seconds = slowest.item()
+    seconds = slowest_over_ranks(sum(start.elapsed_time(end) for start, end in events) / 1000, device)
 
     # end to end through the runtime: pinned host boards in, graph replay, answer rows out, every step; two lanes, each
     # step launched before the previous one is collected, as the reference's search keeps its lanes in flight
@@ -352,12 +360,7 @@ def main() -> None:
             dist.barrier()
         start = time.perf_counter()
         run(args.steps)
-        elapsed = time.perf_counter() - start
-        if world > 1:
-            slowest = torch.tensor([elapsed], device=device)
-            dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
-            elapsed = slowest.item()
-        return elapsed
+        return slowest_over_ranks(time.perf_counter() - start, device)
 
     host_boards = random_boards(BATCH, 99 + rank)
     batches = GraphedBatches(network, [LATENCY_BATCH, BATCH], in_flight=E2E_LANES)
