@@ -24,7 +24,8 @@ extern "C" {
 #define FRY_ERROR_SHAPE 1   /* a shape or alignment the kernels do not take */
 #define FRY_ERROR_CUDA 2    /* a CUDA runtime or driver call failed */
 
-/* The calling thread's last error message ("" after a success). */
+/* The calling thread's last error message ("" after a success). The string stays valid until the thread's next call
+ * into the library: read it after the call that failed, not in the same expression. */
 const char* fry_last_error(void);
 
 /* The library version string. */

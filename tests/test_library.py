@@ -150,3 +150,37 @@ def test_lane_calls_are_refused_on_the_host_before_any_cuda_call(lib):
     assert raw.fry_lanes_launch(None, 0, 1, None) == ERROR_SHAPE and "no such lane" in raw.fry_last_error().decode()
     assert raw.fry_lanes_collect(None, 0, None) == ERROR_SHAPE
     assert raw.fry_lanes_destroy(None) == 0
+
+
+def test_the_header_is_plain_c_and_a_c_program_links_the_library(lib, tmp_path):
+    # a host written in C (or bound through any C FFI) sees exactly include/fry_b200.h: it compiles as C11, and its
+    # refusals come back through the C ABI before any CUDA call, so this runs without a GPU
+    source = tmp_path / "host.c"
+    source.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "fry_b200.h"
+
+int main(void) {
+    int sizes[2] = {8, 4};
+    FryNetwork network;
+    FryLanes* lanes = NULL;
+    memset(&network, 0, sizeof network);
+    int status;
+    printf("%s\n", fry_version());
+    status = fry_lanes_create(&network, sizes, 2, 1, 1, 0, &lanes);
+    printf("%d %s\n", status, fry_last_error());
+    status = fry_gptq(NULL, NULL, 8, 128, NULL, NULL, NULL, 0, NULL);
+    printf("%d %s\n", status, fry_last_error());
+    printf("%d %d\n", FRY_LEAN_ROW, FRY_LEAN_COLUMNS);
+    return lanes != NULL;
+}
+""")
+    binary = tmp_path / "host"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", str(HEADER.parent), str(source), "-o", str(binary),
+                    "-L", str(LIBRARY_PATH.parent), "-lfry_b200", f"-Wl,-rpath,{LIBRARY_PATH.parent}"], check=True)
+    out = subprocess.run([str(binary)], capture_output=True, text=True, check=True).stdout.splitlines()
+    assert out[0].startswith("fry_b200")
+    assert out[1].startswith("1 ") and "ascending" in out[1]
+    assert out[2].startswith("1 ") and "needs its weight" in out[2]
+    assert out[3] == "508 219"
