@@ -1,10 +1,13 @@
 /* fry_b200: the C ABI of the B200 (sm_100a) int8 inference engine for Fry's network (GilliamWong/chess-transformer).
  *
  * Every pointer argument is a device pointer unless stated otherwise; fp16 tensors are passed as uint16_t bit patterns;
- * every array is dense row-major. `stream` is a cudaStream_t (NULL: the legacy default stream). Work is only enqueued:
- * nothing here synchronises the stream, allocates device memory or changes a pointer between calls, so every entry point
- * may be captured in a CUDA graph. Each returns 0 on success or a nonzero code; fry_last_error() gives the calling
- * thread's last message. Shapes a kernel does not take are refused on the host with FRY_ERROR_SHAPE before anything is
+ * every array is dense row-major. `stream` is a cudaStream_t (NULL: the legacy default stream). The block ops, the heads,
+ * the forward and GPTQ only enqueue work: they do not synchronise the stream, allocate device memory or keep a pointer
+ * between calls (the caller provides the scratch that the *_workspace_bytes functions size), so the block ops, the heads
+ * and the forward can be recorded into CUDA graphs, as GraphedBatches and the lanes record the forward. The lanes
+ * (fry_lanes_*) own their memory, streams and graphs, and fry_lanes_create, _collect and _settle wait on the GPU; so
+ * does fry_device_status. Each returns 0 on success or a nonzero code; fry_last_error() gives the calling thread's last
+ * message. Shapes a kernel does not take are refused on the host with FRY_ERROR_SHAPE before anything is
  * enqueued (the reference raises ValueError for these, model/int8_blocks.py:111-112, model/fused_blocks.py:116-117).
  *
  * Faults the kernels can detect (a wait that timed out, a board token outside the vocabulary) are recorded in a device
