@@ -5,12 +5,15 @@
 
 A step is one forward of 256 synthetic positions (seeded legal-looking boards, independent seeds per GPU) through the
 full 28-block int8 network with random-init weights (no checkpoint ships here), replayed as a CUDA graph. Each GPU runs
-its own replica (no collective on the data path; NCCL only for the barrier and the max of the timings). L2 is flushed
-between timed steps by writing a 256 MiB buffer outside the timed events. Rank 0 prints one JSON line.
+its own replica: no collective on the data path and no NCCL at all (a gloo group on the host carries the barrier and the
+max of the ranks' timings). L2 is flushed between timed steps by writing a 256 MiB buffer outside the timed events.
+The end-to-end numbers go through the library's C++ lanes (fry_lanes_*, runtime.NativeBatches). Rank 0 prints one JSON
+line.
 
 --impl reference times the reference's own CPU implementation of the path, the fp32 ChessTransformer forward run through
-cpu_batches (engine/inference.py:274-278), as restated by the CPU oracle (oracle/model.py), on all host cores, one bounded
-sample of boards a step.
+cpu_batches (engine/inference.py:274-278), as restated by the CPU oracle (oracle/model.py), on all host cores: each step
+one forward of the metric's 256 boards, or of a bounded sample of them when K + W such forwards would not end within
+about three minutes.
 """
 import argparse
 import json
@@ -28,7 +31,9 @@ sys.path.insert(0, str(ROOT))
 
 BATCH = 256
 LATENCY_BATCH = 64
-E2E_LANES = 2  # batches in flight in the end-to-end runs (GraphedBatches' default, engine/inference.py:149)
+E2E_LANES = 2  # batches in flight in the end-to-end runs (the reference runtime's default, engine/inference.py:149)
+CPU_SWEEP_BATCHES = (1, 16, 64, 256)  # the reference CPU path's batch sweep
+REFERENCE_ARM_SECONDS = 180.0  # the reference arm's whole run stays within about this
 # the library's kernels a forward launches: the embedding; per block 2 row norms, projection, attention, attention-out,
 # gate_up, rotate_quant, down (8 x 28); the heads' final norm, f16 GEMM, narrow, policy, 2 x (split, sum), expected score
 LAUNCHES_PER_FORWARD = 1 + 8 * 28 + 9
@@ -143,20 +148,45 @@ class ClockSampler:
                 "source": self.source}
 
 
-def slowest_over_ranks(seconds: float, device) -> float:
-    """The job's time: the largest of the ranks' times (an all_reduce MAX over the process group, on `device`), or the
-    rank's own when it runs alone. Every rank calls it at the same point."""
+def slowest_over_ranks(seconds: float) -> float:
+    """The job's time: the largest of the ranks' times (an all_reduce MAX over the host-side gloo group), or the rank's
+    own when it runs alone. Every rank calls it at the same point."""
     import torch
     import torch.distributed as dist
     if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
         return seconds
-    slowest = torch.tensor([seconds], dtype=torch.float64, device=device)
+    slowest = torch.tensor([seconds], dtype=torch.float64)
     dist.all_reduce(slowest, op=dist.ReduceOp.MAX)
     return slowest.item()
 
 
+def host_cpu() -> str:
+    """The host's CPU model, as /proc/cpuinfo names it."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_forward_seconds(torch, state: dict, settings: dict, boards, minimum_seconds: float, minimum_repeats: int) -> tuple[float, int]:
+    """Mean seconds of the reference CPU path's fp32 forward (the oracle's restatement) on `boards`, after one untimed
+    forward, over at least minimum_repeats forwards and minimum_seconds."""
+    from oracle.model import fp32_forward
+    with torch.no_grad():
+        fp32_forward(state, settings, boards)
+        start, repeats = time.perf_counter(), 0
+        while repeats < minimum_repeats or time.perf_counter() - start < minimum_seconds:
+            fp32_forward(state, settings, boards)
+            repeats += 1
+    return (time.perf_counter() - start) / repeats, repeats
+
+
 def reference_arm(args, rank: int) -> None:
-    """The reference's CPU path on the host cores: fp32 forward of a bounded sample of boards a step."""
+    """The reference's CPU path on the host cores: the fp32 forward of the metric's 256 boards a step, or of the largest
+    halving of them whose K + W steps end within REFERENCE_ARM_SECONDS."""
     if rank != 0:
         return
     import torch
@@ -165,10 +195,17 @@ def reference_arm(args, rank: int) -> None:
     from chess_transformer_b200.network import FRY_SETTINGS, synthetic_state_dict
     torch.set_num_threads(os.cpu_count() or 1)
     state = synthetic_state_dict(FRY_SETTINGS, 0)
-    sample = 16
-    boards = torch.from_numpy(random_boards(sample, 0)).long()
+    sample = BATCH
     with torch.no_grad():
-        for _ in range(args.warmup):
+        while True:
+            boards = torch.from_numpy(random_boards(sample, 0)).long()
+            probe = time.perf_counter()
+            fp32_forward(state, FRY_SETTINGS, boards)
+            probe = time.perf_counter() - probe
+            if sample == 1 or probe * (args.steps + args.warmup) <= REFERENCE_ARM_SECONDS:
+                break
+            sample //= 2
+        for _ in range(max(0, args.warmup - 1)):
             fp32_forward(state, FRY_SETTINGS, boards)
         start = time.perf_counter()
         for _ in range(args.steps):
@@ -180,37 +217,36 @@ def reference_arm(args, rank: int) -> None:
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {**workload_config(1), "parallelism": "host cores",
-                       "sample": f"{sample} boards a step (bounded CPU sample of the batch of 256)"},
+                       "sample": f"{sample} of the batch's {BATCH} boards a step" + ("" if sample == BATCH else " (bounded CPU sample)")},
             "cpu_baseline": {"value": value, "unit": "positions/s", "cores": cores, "kind": "port",
                              "sample": f"{sample} boards x {args.steps} steps, fp32 ChessTransformer forward (oracle/model.py) "
-                                       f"on {cores} threads, {os.cpu_count()} host cores"},
+                                       f"on {cores} threads, {os.cpu_count()} host cores ({host_cpu()})"},
             "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def cpu_baseline() -> dict:
-    """The oracle port of the reference's CPU path on this host's cores, a ~10-20 s sample."""
+    """The oracle port of the reference's CPU path on this host's cores at each of CPU_SWEEP_BATCHES (a few seconds a
+    batch); the value is the metric's batch, 256."""
     import torch
-    from oracle.model import fp32_forward
     from chess_transformer_b200.boards import random_boards
     from chess_transformer_b200.network import FRY_SETTINGS, synthetic_state_dict
     threads = torch.get_num_threads()
     torch.set_num_threads(os.cpu_count() or 1)
     state = synthetic_state_dict(FRY_SETTINGS, 0)
-    sample = 8
-    boards = torch.from_numpy(random_boards(sample, 1)).long()
-    with torch.no_grad():
-        fp32_forward(state, FRY_SETTINGS, boards)
-        start, repeats = time.perf_counter(), 0
-        while time.perf_counter() - start < 10 or repeats < 2:
-            fp32_forward(state, FRY_SETTINGS, boards)
-            repeats += 1
-        elapsed = time.perf_counter() - start
+    sweep, repeats_at = {}, {}
+    for batch in CPU_SWEEP_BATCHES:
+        boards = torch.from_numpy(random_boards(batch, 1)).long()
+        seconds, repeats = cpu_forward_seconds(torch, state, FRY_SETTINGS, boards, 3.0, 2)
+        sweep[str(batch)] = {"ms_per_forward": round(1000 * seconds, 2), "positions_per_s": round(batch / seconds, 2)}
+        repeats_at[batch] = repeats
     cores = torch.get_num_threads()
     torch.set_num_threads(threads)
-    return {"value": sample * repeats / elapsed, "unit": "positions/s", "cores": cores, "kind": "port",
-            "sample": f"{sample} boards x {repeats} forwards, fp32 ChessTransformer forward (oracle/model.py, the reference's "
-                      f"cpu_batches path) on {cores} threads of {os.cpu_count()} host cores"}
+    return {"value": sweep[str(BATCH)]["positions_per_s"], "unit": "positions/s", "cores": cores, "kind": "port",
+            "cpu": host_cpu(), "batch_sweep": sweep,
+            "sample": f"the fp32 ChessTransformer forward (oracle/model.py, the reference's cpu_batches path) of "
+                      f"{BATCH} boards x {repeats_at[BATCH]} forwards (and of {', '.join(str(b) for b in CPU_SWEEP_BATCHES[:-1])} "
+                      f"boards for the sweep) on {cores} threads of {os.cpu_count()} host cores"}
 
 
 def gemm_roofline(torch, stream) -> dict:
@@ -248,20 +284,31 @@ def gemm_roofline(torch, stream) -> dict:
 
 
 SWEEP_BATCHES = (1, 16, 64, 256, 1024)
+# batches also run as forwards of chunks, as the reference's chunked_answer_rows splits a batch so a chunk's activations
+# stay in L2 (engine/inference.py:26-35): (batch, chunk)
+SWEEP_CHUNKED = ((1024, 256), (1024, 128))
+# HBM bytes a forward must read whatever the batch: the int8 block weights and the fp16 attention-out (28 blocks, dq
+# cycling 8/16/24), for the small-batch regime's achieved GB/s
+WEIGHT_BYTES = sum(768 * (36 * dq + 576) + 1984 * 768 + 768 * 1024 + 2 * 768 * 768 for dq in [8, 16, 24] * 9 + [8])
 
 
 def batch_sweep(torch, network, device, stream, flush, steps: int) -> dict:
-    """Positions/s and ms per forward at each of SWEEP_BATCHES (a CUDA graph per batch, inputs resident, L2 flushed
-    before each timed replay, CUDA events on the graph's stream)."""
+    """Positions/s and ms per forward at each of SWEEP_BATCHES, and at SWEEP_CHUNKED's batches run as forwards of chunks
+    (a CUDA graph per batch, inputs resident, L2 flushed before each timed replay, CUDA events on the graph's stream).
+    At batch 1 and 16 also the weights' achieved GB/s (WEIGHT_BYTES a forward) against the measured HBM peak."""
     from chess_transformer_b200.boards import random_boards
     results = {}
-    for batch in SWEEP_BATCHES:
+    hbm = peaks()["hbm_gbs"]
+    for batch, chunk in [(batch, batch) for batch in SWEEP_BATCHES] + list(SWEEP_CHUNKED):
         boards = torch.from_numpy(random_boards(batch, 500 + batch)).long().to(device)
+        parts = boards.split(chunk)
         with torch.cuda.stream(stream), torch.no_grad():
-            network(boards)
+            for part in parts:
+                network(part)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
-                network(boards)
+                for part in parts:
+                    network(part)
             for _ in range(3):
                 graph.replay()
             times = []
@@ -274,7 +321,11 @@ def batch_sweep(torch, network, device, stream, flush, steps: int) -> dict:
                 end.synchronize()
                 times.append(start.elapsed_time(end))
         ms = statistics.median(times)
-        results[str(batch)] = {"ms_per_forward": round(ms, 4), "positions_per_s": round(batch / ms * 1000, 1)}
+        entry = {"ms_per_forward": round(ms, 4), "positions_per_s": round(batch / ms * 1000, 1)}
+        if batch <= 16:
+            gbs = WEIGHT_BYTES / (ms / 1000) / 1e9
+            entry.update({"weights_gb_per_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)})
+        results[str(batch) if chunk == batch else f"{batch}_in_chunks_of_{chunk}"] = entry
         del graph
     return results
 
@@ -294,13 +345,13 @@ def main() -> None:
     from chess_transformer_b200.boards import random_boards
     from chess_transformer_b200.network import FRY_SETTINGS, Int8Network, quantize, synthetic_state_dict
     from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
-    from chess_transformer_b200.runtime import GraphedBatches, NativeBatches
+    from chess_transformer_b200.runtime import NativeBatches
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
 
     state = synthetic_state_dict(FRY_SETTINGS, 1000 + rank)
     network = Int8Network(state, FRY_SETTINGS, quantize(state, FRY_SETTINGS), device)
@@ -341,11 +392,11 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    seconds = slowest_over_ranks(sum(start.elapsed_time(end) for start, end in events) / 1000, device)
+    seconds = slowest_over_ranks(sum(start.elapsed_time(end) for start, end in events) / 1000)
 
-    # end to end through the runtime: pinned host boards in, graph replay, answer rows out, every step; two lanes, each
-    # step launched before the previous one is collected, as the reference's search keeps its lanes in flight
-    # (engine/inference.py:144-146)
+    # end to end through the library's C++ lanes (fry_lanes_*): pinned host boards in, graph replay, answer rows out,
+    # every step; two lanes, each step launched before the previous one is collected, as the reference's search keeps its
+    # lanes in flight (engine/inference.py:144-146)
     def pipelined_seconds(launch, collect) -> float:
         def run(count: int) -> None:
             pending = launch()
@@ -360,10 +411,10 @@ def main() -> None:
             dist.barrier()
         start = time.perf_counter()
         run(args.steps)
-        return slowest_over_ranks(time.perf_counter() - start, device)
+        return slowest_over_ranks(time.perf_counter() - start)
 
     host_boards = random_boards(BATCH, 99 + rank)
-    batches = GraphedBatches(network, [LATENCY_BATCH, BATCH], in_flight=E2E_LANES)
+    batches = NativeBatches(network, [LATENCY_BATCH, BATCH], in_flight=E2E_LANES)
     e2e_seconds = pipelined_seconds(lambda: batches.launch(host_boards), batches.collect)
 
     # the same through lean lanes, the Rust round loop's format: rows of tokens and answer columns in (30 moves' columns
@@ -379,14 +430,9 @@ def main() -> None:
         lane.rows_array[:BATCH] = lean_rows
         return runtime.launch_filled(lane, BATCH)
 
-    lean_batches = GraphedBatches(network, [BATCH], in_flight=E2E_LANES, lean=True)
+    lean_batches = NativeBatches(network, [BATCH], in_flight=E2E_LANES, lean=True)
     lean_seconds = pipelined_seconds(lambda: lean_launch(lean_batches), lean_batches.collect)
-    del lean_batches
-
-    # the same lean steps through the library's C++ lanes (fry_lanes_*): one C-ABI call to launch, one to collect
-    native = NativeBatches(network, [BATCH], in_flight=E2E_LANES, lean=True)
-    native_seconds = pipelined_seconds(lambda: lean_launch(native), native.collect)
-    native.close()
+    lean_batches.close()
 
     extra = {}
     if rank == 0 and not args.no_sweep:
@@ -396,7 +442,7 @@ def main() -> None:
             batches.collect(batches.launch(host_boards[:LATENCY_BATCH]))
             latencies.append(time.perf_counter() - t0)
         extra["latency_p50_ms_batch64"] = round(1000 * statistics.median(latencies[10:]), 3)
-    del batches
+    batches.close()
     if rank == 0 and not args.no_sweep:
         extra["batch_sweep"] = batch_sweep(torch, network, device, stream, flush, max(5, args.steps))
 
@@ -420,13 +466,12 @@ def main() -> None:
                 "config": {**workload_config(world), "parallelism": f"replicas x{world}"},
                 "e2e": {"value": BATCH * args.steps * world / e2e_seconds, "unit": "positions/s",
                         "h2d_bytes_per_step": BATCH * 70 * 8, "d2h_bytes_per_step": BATCH * 1969 * 4, "lanes": E2E_LANES,
+                        "runtime": "fry_lanes_* (C++ lanes: one C-ABI call to launch and one to collect)",
                         "note": "lanes on their own streams, a step launched before the previous one is collected; "
                                 "no L2 flush between steps, unlike value"},
                 "e2e_lean": {"value": BATCH * args.steps * world / lean_seconds, "unit": "positions/s",
-                             "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4},
-                "e2e_lean_native": {"value": BATCH * args.steps * world / native_seconds, "unit": "positions/s",
-                                    "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4,
-                                    "runtime": "fry_lanes_* (C++ lanes, one C-ABI call to launch and one to collect)"},
+                             "h2d_bytes_per_step": BATCH * LEAN_ROW, "d2h_bytes_per_step": BATCH * LEAN_COLUMNS * 4,
+                             "runtime": "fry_lanes_* lean lanes (the Rust round loop's rows)"},
                 "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
                 "forward_int8_tops": round(forward_tops, 1),
                 "roofline": roofline, "clocks": clocks.summary(), **extra}

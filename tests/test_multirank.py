@@ -1,6 +1,6 @@
 """The multi-GPU path's host logic on CPU ranks (no GPU): the job's time is the slowest rank's, taken by an all_reduce MAX
-over a world-size-2 gloo group as bench.py takes it over NCCL; and under torchrun the reference arm runs on rank 0 alone,
-which prints the one JSON line, while the other rank exits 0 without work."""
+over a world-size-2 gloo group (bench.py uses the same host-side group on the GPUs: no NCCL); and under torchrun the
+reference arm runs on rank 0 alone, which prints the one JSON line, while the other rank exits 0 without work."""
 import json
 import os
 import socket
@@ -26,7 +26,7 @@ def slowest_worker(rank: int, world: int, port: int, times: list[float], results
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        results.put((rank, bench.slowest_over_ranks(times[rank], "cpu")))
+        results.put((rank, bench.slowest_over_ranks(times[rank])))
     finally:
         dist.destroy_process_group()
 
@@ -47,7 +47,7 @@ def test_the_job_time_is_the_slowest_ranks_over_two_gloo_ranks():
 
 def test_a_rank_alone_keeps_its_own_time():
     assert not dist.is_initialized()
-    assert bench.slowest_over_ranks(0.5, "cpu") == 0.5
+    assert bench.slowest_over_ranks(0.5) == 0.5
 
 
 def test_the_reference_arm_runs_on_rank_zero_alone_under_torchrun():

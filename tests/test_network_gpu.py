@@ -10,7 +10,7 @@ from chess_transformer_b200.build import build
 from chess_transformer_b200.encoding import ANSWER_WIDTH, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD
 from chess_transformer_b200.library import library
 from chess_transformer_b200.network import FRY_SETTINGS, Int8Network
-from chess_transformer_b200.runtime import GraphedBatches, NativeBatches, small_graph_sizes
+from chess_transformer_b200.runtime import NativeBatches, lane_sizes
 from oracle import int8 as oi, model as om
 from tests.conftest import SMALL, TINY
 
@@ -92,28 +92,61 @@ def test_the_28_block_fry_network_is_the_oracle(fry):
 
 
 @pytest.mark.parametrize("batch", [64, 256])
-def test_a_boards_answer_does_not_depend_on_its_batch(fry, batch):
-    network, _ = fry
-    boards = torch.from_numpy(random_boards(batch, batch)).long().cuda()
+def test_the_measured_batches_are_the_oracle_and_a_boards_answer_does_not_depend_on_its_batch(fry, batch):
+    # the bench's own configurations (64 boards: the engine's default batch; 256: the metric's), the whole batch on the
+    # GPU, six of its rows against the oracle's forward of those boards, and the same rows run alone
+    network, prepared = fry
+    boards = torch.from_numpy(random_boards(batch, batch)).long()
     with torch.no_grad():
-        whole = network(boards)
-        picked = [0, batch // 2, batch - 1]
-        alone = network(boards[picked])
+        whole = network(boards.cuda()).cpu()
+        picked = [0, 1, batch // 3, batch // 2, 2 * batch // 3, batch - 1]
+        alone = network(boards[picked].cuda()).cpu()
+    expected = oi.int8_forward(prepared, boards[picked])
+    assert torch.isfinite(whole).all()
+    assert (whole[picked, :-1] - expected[:, :-1]).abs().max() <= LOGIT_TOLERANCE
+    assert (whole[picked, -1] - expected[:, -1]).abs().max() <= SCORE_TOLERANCE
     assert torch.equal(whole[picked], alone)
 
 
-def test_graph_lanes_give_the_eager_bits(fry):
+class Recorded:
+    """The forward as a caller's runtime records it (the reference's contract, engine/inference.py:117-125): on a side
+    stream, after an eager warm-up there, one CUDA graph per batch size sharing one private memory pool, each reading a
+    fixed device input buffer and leaving its answers in a fixed output. replay(n) runs the size-n graph on the stream."""
+
+    def __init__(self, answer, inputs: torch.Tensor, sizes: list[int]):
+        self.stream, self.inputs, self.graphs, self.outputs = torch.cuda.Stream(), inputs, {}, {}
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream), torch.no_grad():
+            for size in sizes:
+                answer(inputs[:size])
+        pool = torch.cuda.graph_pool_handle()
+        for size in sorted(sizes, reverse=True):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=pool, stream=self.stream), torch.no_grad():
+                self.outputs[size] = answer(inputs[:size])
+            self.graphs[size] = graph
+        self.stream.synchronize()
+
+    def replay(self, host_inputs: np.ndarray) -> np.ndarray:
+        count = len(host_inputs)
+        size = min(s for s in self.graphs if s >= count)
+        with torch.cuda.stream(self.stream):
+            self.inputs[:count].copy_(torch.from_numpy(host_inputs))
+            self.graphs[size].replay()
+            answers = self.outputs[size][:count].cpu()
+        return answers.numpy()
+
+
+def test_recorded_graphs_give_the_eager_bits(fry):
     network, _ = fry
     boards = random_boards(24, 5)
     with torch.no_grad():
         eager = network(torch.from_numpy(boards).long().cuda()).cpu().numpy()
-    batches = GraphedBatches(network, small_graph_sizes(24), in_flight=2)
-    first = batches.launch(boards[:10])
-    second = batches.launch(boards)
-    assert np.array_equal(batches.collect(second), eager)
-    assert np.array_equal(batches.collect(first), eager[:10])
+    recorded = Recorded(network, torch.from_numpy(random_boards(24, 6)).long().cuda(), lane_sizes(24))
+    assert np.array_equal(recorded.replay(boards), eager)
+    assert np.array_equal(recorded.replay(boards[:10]), eager[:10])
     for _ in range(20):
-        assert np.array_equal(batches.collect(batches.launch(boards[:17])), eager[:17])
+        assert np.array_equal(recorded.replay(boards[:17]), eager[:17])
 
 
 def test_a_token_outside_the_vocabulary_is_reported_not_faulted(fry):
@@ -156,23 +189,16 @@ def test_lean_answers_are_the_rows_gathered_at_their_columns(fry):
     assert torch.equal(answers, whole.gather(1, torch.from_numpy(columns)))
 
 
-def test_lean_graph_lanes_give_the_eager_bits(fry):
+def test_recorded_lean_graphs_give_the_eager_bits(fry):
     network, _ = fry
     boards = random_boards(24, 9)
     rows_bytes, _ = lean_rows(boards, 9)
     with torch.no_grad():
         eager = network.forward_lean(torch.from_numpy(rows_bytes).cuda()).cpu().numpy()
-    batches = GraphedBatches(network, small_graph_sizes(24), in_flight=2, lean=True)
-    with pytest.raises(RuntimeError, match="launch_filled"):
-        batches.launch(boards)
-    lane = batches.free_lane()
-    lane.rows_array[:24] = rows_bytes
-    first = batches.launch_filled(lane, 24)
-    lane = batches.free_lane()
-    lane.rows_array[:10] = rows_bytes[:10]
-    second = batches.launch_filled(lane, 10)
-    assert np.array_equal(batches.collect(first), eager)
-    assert np.array_equal(batches.collect(second), eager[:10])
+    start_rows, _ = lean_rows(random_boards(24, 10), 10)
+    recorded = Recorded(network.forward_lean, torch.from_numpy(start_rows).cuda(), [8, 16, 24])
+    assert np.array_equal(recorded.replay(rows_bytes), eager)
+    assert np.array_equal(recorded.replay(rows_bytes[:10]), eager[:10])
 
 
 def test_a_lean_column_outside_the_row_is_reported_not_faulted(fry):
@@ -205,30 +231,28 @@ def test_fry_with_fp16_blocks_inside_and_last_runs_the_transitions(fry):
     assert torch.equal(alone, ours[[5]])  # an answer does not depend on its batch here either
 
 
-def test_lean_lanes_replay_by_their_raw_handles_as_the_rust_loop_does(fry):
-    # the Rust round loop's calls (engine/inference.py:175-205 spells them out in Python): copy the rows in, launch the
-    # size's graph executable on the lane's stream, record done, copy the answers out, all by raw handle through cudart
+def test_a_recorded_lean_graph_replays_by_its_raw_handle_as_the_rust_loop_does(fry):
+    # the Rust round loop replays a lane's graph executable by raw handle on the lane's stream, between copies it makes
+    # itself (engine/inference.py:175-205 spells the calls out in Python); here on a graph torch recorded
     import ctypes, os
     network, _ = fry
-    boards = random_boards(16, 13)
-    rows_bytes, _ = lean_rows(boards, 13)
-    batches = GraphedBatches(network, [8, 16], in_flight=1, lean=True)
-    lane = batches.free_lane()
-    lane.rows_array[:16] = rows_bytes
-    expected = batches.collect(batches.launch_filled(lane, 16)).copy()
-    handles = batches.rust_network()["lanes"][0]
+    rows_bytes, _ = lean_rows(random_boards(16, 13), 13)
+    with torch.no_grad():
+        eager = network.forward_lean(torch.from_numpy(rows_bytes).cuda()).cpu().numpy()
+    start_rows, _ = lean_rows(random_boards(16, 14), 14)
+    recorded = Recorded(network.forward_lean, torch.from_numpy(start_rows).cuda(), [8, 16])
+    rows_host = torch.from_numpy(rows_bytes).pin_memory()
+    answers_host = torch.zeros(16, LEAN_COLUMNS, dtype=torch.float32).pin_memory()
+    stream = recorded.stream.cuda_stream
     cudart = ctypes.CDLL(f"libcudart.so.{torch.version.cuda.split('.')[0]}", mode=os.RTLD_NOLOAD | os.RTLD_LAZY)
-    memcpy, launch, record, sync = cudart.cudaMemcpyAsync, cudart.cudaGraphLaunch, cudart.cudaEventRecord, cudart.cudaStreamSynchronize
+    memcpy, launch, sync = cudart.cudaMemcpyAsync, cudart.cudaGraphLaunch, cudart.cudaStreamSynchronize
     memcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
-    launch.argtypes, record.argtypes, sync.argtypes = [ctypes.c_void_p] * 2, [ctypes.c_void_p] * 2, [ctypes.c_void_p]
-    lane.answers_array[:] = 0
-    executable, answers = handles["graphs"][16]
-    assert memcpy(handles["rows"], handles["rows_host"], 16 * LEAN_ROW, 1, handles["stream"]) == 0
-    assert launch(executable, handles["stream"]) == 0
-    assert record(handles["done"], handles["stream"]) == 0
-    assert memcpy(handles["answers_host"], answers, 16 * LEAN_COLUMNS * 4, 2, handles["stream"]) == 0
-    assert sync(handles["stream"]) == 0
-    assert np.array_equal(lane.answers_array[:16], expected)
+    launch.argtypes, sync.argtypes = [ctypes.c_void_p] * 2, [ctypes.c_void_p]
+    assert memcpy(recorded.inputs.data_ptr(), rows_host.data_ptr(), 16 * LEAN_ROW, 1, stream) == 0
+    assert launch(recorded.graphs[16].raw_cuda_graph_exec(), stream) == 0
+    assert memcpy(answers_host.data_ptr(), recorded.outputs[16].data_ptr(), 16 * LEAN_COLUMNS * 4, 2, stream) == 0
+    assert sync(stream) == 0
+    assert np.array_equal(answers_host.numpy(), eager)
 
 
 def test_native_lanes_give_the_eager_bits(fry):
@@ -238,7 +262,7 @@ def test_native_lanes_give_the_eager_bits(fry):
     boards = random_boards(24, 14)
     with torch.no_grad():
         eager = network(torch.from_numpy(boards).long().cuda()).cpu().numpy()
-    batches = NativeBatches(network, small_graph_sizes(24), in_flight=2)
+    batches = NativeBatches(network, lane_sizes(24), in_flight=2)
     try:
         first = batches.launch(boards[:10])
         second = batches.launch(boards)
