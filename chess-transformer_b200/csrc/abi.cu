@@ -38,6 +38,7 @@ int projection_rows(const FryNetwork* n, int dq) {
 }
 
 constexpr int kAnswerWidth = 1969;  // 1968 move logits, then the expected score
+constexpr uint64_t kMaxWaitLimitNs = 60000000000ull;  // the largest wait limit fry_set_wait_limit_ns takes: 60 s
 
 // The forward on boards (int64 [B, 70]) or on lean lanes' rows (uint8 [B, 508]: tokens, then the answer columns that
 // lean_answers [B, 219] gathers from rows), in the caller's workspace of fry_forward_workspace_bytes.
@@ -183,6 +184,19 @@ int fry_device_status(int* code, int* where, int clear) {
     if (where) *where = host[1];
     return check(status, "fry_device_status");
 }
+
+int fry_set_wait_limit_ns(uint64_t limit_ns) {
+    if (limit_ns < 1000 || limit_ns > kMaxWaitLimitNs)
+        return fail(FRY_ERROR_SHAPE, "fry_set_wait_limit_ns takes 1 us to 60 s, got " + std::to_string(limit_ns) + " ns");
+    return check(cudaMemcpyToSymbol(fry::g_wait_limit_ns, &limit_ns, sizeof(limit_ns)), "fry_set_wait_limit_ns");
+}
+
+int fry_wait_limit_ns(uint64_t* limit_ns) {
+    if (!limit_ns) return fail(FRY_ERROR_SHAPE, "fry_wait_limit_ns needs somewhere to write the limit");
+    return check(cudaMemcpyFromSymbol(limit_ns, fry::g_wait_limit_ns, sizeof(*limit_ns)), "fry_wait_limit_ns");
+}
+
+int fry_wait_probe(void* stream) { return check(fry::wait_probe(as_stream(stream)), "fry_wait_probe"); }
 
 int fry_int8_linear(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
                     const uint16_t* residual, const uint16_t* original, const uint16_t* residual_scale, const uint16_t* input_scale,
@@ -348,11 +362,12 @@ int fry_board_embedding(const int64_t* boards, const uint16_t* embed, const uint
     return check(fry::board_embedding(boards, embed, position, table, out, B, D, as_stream(stream)), "fry_board_embedding");
 }
 
-size_t fry_heads_workspace_bytes(int B, int D) { return fry::heads_workspace_bytes(B, D); }
+size_t fry_heads_workspace_bytes(int B, int D) { return B > 0 && D > 0 ? fry::heads_workspace_bytes(B, D) : 0; }
 
 int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
               int D, void* stream) {
     if (!heads || B < 0) return fail(FRY_ERROR_SHAPE, "fry_heads needs its weights and B >= 0");
+    if (D < 16 || D % 16 != 0 || D > 1024) return fail(FRY_ERROR_SHAPE, "fry_heads takes d_model a multiple of 16 from 16 to 1024, got " + std::to_string(D));
     if (!aligned16(stream_x) || !aligned16(workspace) || !aligned16(heads->a_weight) || !aligned16(heads->ln_gain))
         return fail(FRY_ERROR_SHAPE, "fry_heads needs 16-byte aligned tensors");
     fry::HeadWeights w{heads->ln_gain,     heads->a_weight,    heads->a_bias,     heads->narrow_weight, heads->narrow_bias,

@@ -35,8 +35,10 @@ FRY_DEVICE void record_error(int code, int where) {
     if (atomicCAS(&g_status[0], 0, code) == 0) g_status[1] = where;
 }
 
-// Time bound for every wait on an mbarrier: 2 s of the global timer, far beyond any real wait (microseconds).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Time bound for every wait on an mbarrier, in ns of the global timer: by default 2 s, far beyond any real wait
+// (microseconds). fry_set_wait_limit_ns changes it per device; a kernel reads it when a wait first spins.
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+__device__ uint64_t g_wait_limit_ns = kDefaultWaitLimitNs;
 
 FRY_DEVICE uint64_t global_timer_ns() {
     uint64_t t;
@@ -75,10 +77,10 @@ FRY_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of the given parity to complete; false (and the error flag set) if it never does.
 FRY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t start = global_timer_ns();
+    const uint64_t start = global_timer_ns(), limit = g_wait_limit_ns;
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) break;
+        if ((i & 255u) == 0 && global_timer_ns() - start > limit) break;
     }
     record_error(kWaitTimeout, where);
     return false;
@@ -117,10 +119,10 @@ FRY_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
 // mbar_wait for a barrier that other CTAs of the cluster arrive on (acquiring their writes), bounded the same way.
 FRY_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int where) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    const uint64_t start = global_timer_ns();
+    const uint64_t start = global_timer_ns(), limit = g_wait_limit_ns;
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
-        if ((i & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) break;
+        if ((i & 255u) == 0 && global_timer_ns() - start > limit) break;
     }
     record_error(kWaitTimeout, where);
     return false;
@@ -380,6 +382,12 @@ FRY_DEVICE float h2f_exact(uint16_t bits) {
 FRY_DEVICE uint32_t pack_half2_rn(float lo, float hi) {
     const __half2 pair = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&pair);
+}
+// two fp32 values rounded to nearest-even bf16 in one instruction, lo in the low half
+FRY_DEVICE uint32_t pack_bf162_rn(float lo, float hi) {
+    uint32_t pair;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pair) : "f"(hi), "f"(lo));
+    return pair;
 }
 FRY_DEVICE float h2f(__half h) { return __half2float(h); }
 FRY_DEVICE float h2f_bits(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }

@@ -5,6 +5,7 @@
 #include "attention.cu"
 #include "heads.cu"
 #include "gptq.cu"
+#include "health.cu"
 #include "abi.cu"
 #include "noalloc.cu"
 #include "lanes.cu"

@@ -379,12 +379,12 @@ __global__ void __launch_bounds__(256) expected_score_kernel(const float* __rest
 cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, float* rows, void* workspace, size_t workspace_bytes, int B,
                   int D, cudaStream_t stream, std::string* error, const uint8_t* lean_rows, float* lean_answers) {
     if (B <= 0) return cudaSuccess;
-    if (workspace_bytes < heads_workspace_bytes(B, D)) {
-        if (error) *error = "the heads' workspace is smaller than fry_heads_workspace_bytes";
+    if (D < 16 || D % 16 != 0 || D > 1024 || w.bins < 2 || w.bins > 256) {
+        if (error) *error = "the heads take d_model a multiple of 16 from 16 to 1024 and 2 to 256 value bins";
         return cudaErrorInvalidValue;
     }
-    if (D % 16 != 0 || D > 1024 || w.bins < 2 || w.bins > 256) {
-        if (error) *error = "the heads take d_model a multiple of 16 up to 1024 and 2 to 256 value bins";
+    if (workspace_bytes < heads_workspace_bytes(B, D)) {
+        if (error) *error = "the heads' workspace is smaller than fry_heads_workspace_bytes";
         return cudaErrorInvalidValue;
     }
     if (reinterpret_cast<uintptr_t>(w.narrow_weight) % 16 != 0 || reinterpret_cast<uintptr_t>(w.hidden_weight) % 16 != 0 ||

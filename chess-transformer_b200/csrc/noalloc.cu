@@ -13,10 +13,11 @@
 // the narrow outputs, the eval head's units and logits) is written in full by the call before the call reads it.
 //
 // Set-up: the first call on each device looks up the array's device address (cudaGetSymbolAddress, with that device
-// current) and keeps it; make that first call on a device before any stream capture on it.
+// current) and keeps it for the device's context; make that first call on a device before any stream capture on it.
 #include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/fry_b200.h"
 #include "common.cuh"
@@ -34,24 +35,52 @@ static __device__ __align__(256) uint8_t g_heads_scratch[kHeadsScratchBytes];
 
 namespace {
 
-// The array's device address on the current device. In host code g_heads_scratch is only a host-side stand-in for
-// the symbol, never a device address, so the address is looked up once per device with that device current.
+// The id of the calling thread's current context (cuCtxGetId, unique over the process's life), or 0 when none is current
+// yet or the driver lacks the call. The driver's functions come through the runtime, as the library links no libcuda.
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* symbol = nullptr;
+        cudaDriverEntryPointQueryResult found;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &symbol, cudaEnableDefault, &found) == cudaSuccess && found == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(symbol);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &symbol, cudaEnableDefault, &found) == cudaSuccess && found == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(symbol);
+    });
+    CUcontext context = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&context) != CUDA_SUCCESS || !context || get_id(context, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// The array's device address in the current device's context. In host code g_heads_scratch is only a host-side
+// stand-in for the symbol, never a device address, so the address is looked up with the device current, once per
+// context: a device reset (cudaDeviceReset) ends the context and reloads the library's module, and the next call looks
+// the address up anew in the new context.
 cudaError_t heads_scratch(void** address) {
     static std::mutex mutex;
-    static std::map<int, void*> found;
+    static std::map<std::pair<int, unsigned long long>, void*> found;
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return status;
     std::lock_guard<std::mutex> lock(mutex);
-    auto known = found.find(device);
-    if (known != found.end()) {
-        *address = known->second;
-        return cudaSuccess;
+    unsigned long long context = current_context_id();
+    if (context != 0) {
+        auto known = found.find({device, context});
+        if (known != found.end()) {
+            *address = known->second;
+            return cudaSuccess;
+        }
     }
     void* pointer = nullptr;
     status = cudaGetSymbolAddress(&pointer, g_heads_scratch);
     if (status != cudaSuccess) return status;
-    found[device] = pointer;
+    context = current_context_id();  // the lookup made the device's context current if none was
+    if (context != 0) found[{device, context}] = pointer;
     *address = pointer;
     return cudaSuccess;
 }
@@ -64,6 +93,7 @@ cudaError_t heads_scratch(void** address) {
 
 extern "C" int fry_heads_noalloc(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, int B, int D, void* stream) {
     if (!heads || B < 0) return fail(FRY_ERROR_SHAPE, "fry_heads_noalloc needs its weights and B >= 0");
+    if (D < 16 || D % 16 != 0) return fail(FRY_ERROR_SHAPE, "fry_heads_noalloc takes d_model a multiple of 16 from 16, got " + std::to_string(D));
     if (B > fry::kNoAllocMaxBoards || D > fry::kNoAllocMaxWidth)
         return fail(FRY_ERROR_SHAPE, "fry_heads_noalloc takes at most " + std::to_string(fry::kNoAllocMaxBoards) + " boards of d_model up to " +
                                          std::to_string(fry::kNoAllocMaxWidth) + " (its scratch is a fixed device array); got " +

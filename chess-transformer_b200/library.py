@@ -50,6 +50,9 @@ SIGNATURES = {
     "fry_last_error": ([], ctypes.c_char_p),
     "fry_version": ([], ctypes.c_char_p),
     "fry_device_status": ([ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), _c_int], _c_int),
+    "fry_set_wait_limit_ns": ([ctypes.c_uint64], _c_int),
+    "fry_wait_limit_ns": ([ctypes.POINTER(ctypes.c_uint64)], _c_int),
+    "fry_wait_probe": ([_ptr], _c_int),
     "fry_int8_linear": ([_ptr] * 10 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_int8_linear_normed": ([_ptr, _ptr, _c_float] + [_ptr] * 4 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_int8_matmul_i32": ([_ptr] * 3 + [_c_int] * 3 + [_ptr], _c_int),

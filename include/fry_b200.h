@@ -40,6 +40,18 @@ const char* fry_version(void);
  * site. clear != 0 resets it. Synchronous. */
 int fry_device_status(int* code, int* where, int clear);
 
+/* Every wait of a kernel on a barrier (a TMA load, a tensor-core commit, a cluster peer) is bounded: after the current
+ * device's wait limit, 2 s unless set here, it records code 1 in the status word (where = the wait's site) and the
+ * kernel returns without touching what it waited for, so a stalled kernel ends and the context stays usable. The limit
+ * is per device (the current one), 1 us to 60 s; kernels already running keep the limit they read. Synchronous.
+ * The reference's counterpart is its host-side fallback on a failing kernel (model/int8_cuda.py:370-381). */
+int fry_set_wait_limit_ns(uint64_t limit_ns);
+int fry_wait_limit_ns(uint64_t* limit_ns);
+
+/* A health check of that path: enqueues one kernel whose thread waits on a barrier that nothing arrives at, so the wait
+ * runs out after the limit and the status word reads code 1, where 90. No reference counterpart. */
+int fry_wait_probe(void* stream);
+
 /* ---- block ops: each replaces one torch custom op of the reference ----------------------------------------------- */
 
 /* `chess::int8_linear` (model/int8_blocks.py:132-139, kernels :66-128 and model/int8_cuda.py:34-183):
@@ -152,7 +164,8 @@ int fry_heads(const uint16_t* stream_x, const FryHeads* heads, float eps, float*
  * exit), so a call takes at most FRY_HEADS_NOALLOC_MAX_BOARDS boards of d_model up to FRY_HEADS_NOALLOC_MAX_D_MODEL;
  * larger calls return FRY_ERROR_SHAPE before anything is enqueued. All calls on a device share the array, which keeps
  * the last call's contents: calls whose work overlaps on the GPU race and must be ordered by the caller. The first call
- * on a device looks up the array's device address; make it before any stream capture on that device. */
+ * on a device (and the first after a device reset) looks up the array's device address; make it before any stream
+ * capture on that device. d_model must be a multiple of 16 from 16. */
 #define FRY_HEADS_NOALLOC_MAX_BOARDS 16
 #define FRY_HEADS_NOALLOC_MAX_D_MODEL 768
 int fry_heads_noalloc(const uint16_t* stream_x, const FryHeads* heads, float eps, float* rows, int B, int D, void* stream);

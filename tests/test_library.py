@@ -1,5 +1,6 @@
 """Host-side checks that need no GPU: the C-ABI library builds, loads and exports every entry point include/fry_b200.h
 declares; the product's move table, weight layout and synthetic boards agree with the oracle; CPU tensors are refused."""
+import ctypes
 import re
 import subprocess
 from pathlib import Path
@@ -11,7 +12,7 @@ import torch
 import chess_transformer_b200 as fry
 from chess_transformer_b200 import boards as fry_boards, encoding as fry_encoding, network as fry_network
 from chess_transformer_b200.build import build
-from chess_transformer_b200.library import LIBRARY_PATH, SIGNATURES, FryError, library
+from chess_transformer_b200.library import LIBRARY_PATH, SIGNATURES, FryError, FryHeads, library
 from oracle import encoding, int8 as oi, model as om
 from tests.conftest import ROOT, SMALL
 
@@ -54,6 +55,11 @@ def test_shapes_are_refused_on_the_host_before_any_launch(lib):
     with pytest.raises(FryError, match="template attention"):
         lib.fry_template_attention(None, None, None, None, None, 1, 24, 12, 8, 64, 8, 1e-5, None)
     assert "template attention" in lib.fry_last_error().decode()
+    for limit in (0, 999, 60_000_000_001):
+        with pytest.raises(FryError, match="1 us to 60 s"):
+            lib.fry_set_wait_limit_ns(limit)
+    with pytest.raises(FryError, match="d_model"):
+        lib.fry_heads(None, ctypes.byref(FryHeads()), 1e-5, None, None, 0, 2, 0, None)
 
 
 def test_the_ops_refuse_cpu_tensors():

@@ -48,8 +48,12 @@ def rows_without_workspace(lib, stream_x, struct):
     return rows
 
 
-def test_the_allocation_free_heads_give_the_heads_answers_on_two_calls_in_a_row():
+@pytest.fixture(scope="module", autouse=True)
+def built():
     build()
+
+
+def test_the_allocation_free_heads_give_the_heads_answers_on_two_calls_in_a_row():
     lib = library()
     weights = prepared_heads(MAX_D_MODEL)
     struct = heads_struct(*weights)
@@ -72,3 +76,14 @@ def test_the_allocation_free_heads_refuse_more_than_their_array_holds():
     stream_x = torch.zeros(MAX_BOARDS + 1, 70, MAX_D_MODEL, dtype=torch.float16, device="cuda")
     with pytest.raises(FryError, match="at most 16 boards"):
         rows_without_workspace(lib, stream_x, struct)
+
+
+@pytest.mark.parametrize("d_model", [MAX_D_MODEL + 16, 0, -16, 40])
+def test_the_allocation_free_heads_refuse_a_width_they_do_not_take(d_model):
+    lib = library()
+    struct = heads_struct(*prepared_heads(MAX_D_MODEL))
+    stream_x = torch.zeros(2, 70, MAX_D_MODEL, dtype=torch.float16, device="cuda")
+    rows = torch.empty(2, 1969, device="cuda")
+    with pytest.raises(FryError, match="d_model"):
+        lib.fry_heads_noalloc(ctypes.c_void_p(stream_x.data_ptr()), ctypes.byref(struct), 1e-5, ctypes.c_void_p(rows.data_ptr()), 2, d_model,
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
