@@ -283,6 +283,52 @@ def gemm_roofline(torch, stream) -> dict:
     return {"ops_per_forward": total_ops, "seconds_per_forward": total_seconds, "tops_by_shape": per_shape}
 
 
+def timed_launches(torch, stream, flush, run, repeats: int = 10) -> float:
+    """Mean seconds of run() on `stream` by CUDA events, after 3 untimed launches, L2 flushed before each timed one."""
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            run()
+        times = []
+        for _ in range(repeats):
+            flush.fill_(1)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            run()
+            end.record(stream)
+            end.synchronize()
+            times.append(start.elapsed_time(end) / 1000)
+    return statistics.mean(times)
+
+
+def microbench(torch, device, stream, flush) -> dict:
+    """The benchmark's isolated-kernel configuration: the int8 GEMM with the per-row / per-column scale epilogue to bf16
+    at each (K, N) and M it names (TOP/s against the int8 dense peak), and the seq-64 / head_dim-64 attention at 12 heads
+    and batch 64 and 1024 (its HBM bytes, q, k, v read and out written, against the measured HBM peak); L2 flushed
+    before each timed launch, operands seeded as the configuration says."""
+    from chess_transformer_b200 import ops
+    from oracle import microbench as mb
+    peak = peaks()
+    int8_peak = 2 * peak["bf16_tflops"]
+    gemms = {}
+    for K, N in mb.GEMM_SHAPES:
+        for M in mb.GEMM_ROWS:
+            x, weight, x_scale, weight_scale = (torch.from_numpy(a).to(device) for a in mb.gemm_operands(M, K, N, seed=M + K + N))
+            seconds = timed_launches(torch, stream, flush, lambda: ops.int8_matmul_scaled_bf16(x, x_scale, weight, weight_scale))
+            tops = 2.0 * M * K * N / seconds / 1e12
+            gemms[f"M{M}_K{K}_N{N}"] = {"us": round(seconds * 1e6, 2), "tops": round(tops, 1), "frac": round(tops / int8_peak, 4)}
+            del x, weight
+    attention = {}
+    for B in mb.ATTENTION_BATCHES:
+        q, k, v = (t.to(device) for t in mb.attention_operands(B, seed=B))
+        seconds = timed_launches(torch, stream, flush, lambda: ops.attention_bf16(q, k, v, mb.ATTENTION_HEADS))
+        traffic = 4 * q.numel() * 2
+        gbs = traffic / seconds / 1e9
+        attention[str(B)] = {"us": round(seconds * 1e6, 2), "hbm_bytes": traffic, "gb_per_s": round(gbs, 1),
+                             "hbm_frac": round(gbs / peak["hbm_gbs"], 4)}
+    return {"gemm_int8_scaled_bf16": gemms, "attention_bf16_seq64_d64_h12": attention,
+            "peaks": f"int8 dense = 2 x {peak['source']} bf16 burst ({int8_peak:.1f} TOP/s); HBM {peak['hbm_gbs']} GB/s, of {peak['source']}"}
+
+
 SWEEP_BATCHES = (1, 16, 64, 256, 1024)
 # batches also run as forwards of chunks, as the reference's chunked_answer_rows splits a batch so a chunk's activations
 # stay in L2 (engine/inference.py:26-35): (batch, chunk)
@@ -475,6 +521,8 @@ def main() -> None:
                 "gpu_launches": LAUNCHES_PER_FORWARD * args.steps,
                 "forward_int8_tops": round(forward_tops, 1),
                 "roofline": roofline, "clocks": clocks.summary(), **extra}
+        if not args.no_sweep:
+            line["microbench"] = microbench(torch, device, stream, flush)
         if world == 1:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

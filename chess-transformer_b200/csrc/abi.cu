@@ -254,6 +254,34 @@ int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int
     return check(fry::gemm(0, fry::kEpiInt32, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_matmul_i32", detail);
 }
 
+int fry_int8_matmul_scaled_bf16(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, uint16_t* out, int M,
+                                int N, int K, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_scaled_bf16 takes N a multiple of 8 and K a multiple of 16, got N " + std::to_string(N) +
+                                         ", K " + std::to_string(K));
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out))
+        return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_scaled_bf16 needs 16-byte aligned x, weight and out");
+    if (!x_scale || !weight_scale) return fail(FRY_ERROR_SHAPE, "fry_int8_matmul_scaled_bf16 needs both scales");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.x_scale = x_scale;
+    args.w_scale = weight_scale;
+    args.out = out;
+    std::string detail;
+    return check(fry::gemm(0, fry::kEpiScaleBf16, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_matmul_scaled_bf16", detail);
+}
+
+int fry_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int B, int heads, int seq, int head_dim,
+                       void* stream) {
+    if (B < 0 || seq != 64 || head_dim != 64 || heads <= 0 || heads > 1024 || B > 65535)
+        return fail(FRY_ERROR_SHAPE, "fry_attention_bf16 takes sequences of 64 tokens with heads 64 wide (1 to 1024 heads, up to 65535 "
+                                     "sequences), got seq " + std::to_string(seq) + ", head_dim " + std::to_string(head_dim));
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(FRY_ERROR_SHAPE, "fry_attention_bf16 needs 16-byte aligned q, k, v and out");
+    std::string detail;
+    return check(fry::attention64(q, k, v, out, B, heads, as_stream(stream), &detail), "fry_attention_bf16", detail);
+}
+
 int fry_norm_quant(const uint16_t* x, const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int D, void* stream) {
     if (M < 0 || D <= 0 || D % 8 != 0 || D > 1024) return fail(FRY_ERROR_SHAPE, "fry_norm_quant takes D a multiple of 8 up to 1024");
     if (!aligned16(x) || !aligned16(gain) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(FRY_ERROR_SHAPE, "fry_norm_quant needs aligned rows");

@@ -3,6 +3,7 @@
 #include "gemm.cu"
 #include "rows.cu"
 #include "attention.cu"
+#include "attention64.cu"
 #include "heads.cu"
 #include "gptq.cu"
 #include "health.cu"

@@ -57,6 +57,8 @@ constexpr int kNormBarrier = 2;  // named barrier of the 16 epilogue warps alone
 __host__ __device__ constexpr bool linear16(int epi) { return epi == kEpiLinearF16 || epi == kEpiLinearNorm || epi == kEpiMixF16; }
 // epilogues that mix the next block's input (residual and original row operands)
 __host__ __device__ constexpr bool mixes(int epi) { return epi == kEpiMix || epi == kEpiMixF16; }
+// int8 epilogues that scale the sums by the row's activation scale and the column's weight scale
+__host__ __device__ constexpr bool scaled(int epi) { return epi <= kEpiMix || epi == kEpiScaleBf16; }
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
@@ -120,11 +122,11 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
         const int n = n0 + i;
         const bool ok = n < N;
         float scale = 0.0f, second = 0.0f;
-        if constexpr (EPI <= kEpiMix) scale = ok ? p.w_scale[n] : 0.0f;
+        if constexpr (scaled(EPI)) scale = ok ? p.w_scale[n] : 0.0f;
         if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
         if constexpr (EPI == kEpiBias || linear16(EPI) || EPI == kEpiGatedF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
         if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
-        if constexpr (EPI <= kEpiMix) columns[i] = scale;
+        if constexpr (scaled(EPI)) columns[i] = scale;
         if constexpr (EPI == kEpiLinearNorm) columns[i] = (ok && p.norm_gain) ? h2f_bits(p.norm_gain[n]) : 0.0f;
         if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32 || EPI == kEpiGatedF16)
             columns[SECOND + i] = second;
@@ -194,7 +196,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
         float scale_v[16], second_v[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if constexpr (EPI <= kEpiMix) {
+            if constexpr (scaled(EPI)) {
                 const float4 a = reinterpret_cast<const float4*>(scale)[q];
                 scale_v[4 * q] = a.x, scale_v[4 * q + 1] = a.y, scale_v[4 * q + 2] = a.z, scale_v[4 * q + 3] = a.w;
             }
@@ -211,12 +213,14 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
         for (int e = 0; e < 16; e += 2) {
             const uint64_t scale2 = pair2(scale_v[e], scale_v[e + 1]), second2 = pair2(second_v[e], second_v[e + 1]);
             // int8: the int32 sums; fp16: the fp32 sums
-            const uint64_t acc2 = EPI <= kEpiMix
+            const uint64_t acc2 = scaled(EPI)
                                       ? pair2(static_cast<float>(static_cast<int32_t>(acc[e])), static_cast<float>(static_cast<int32_t>(acc[e + 1])))
                                       : pair2(__uint_as_float(acc[e]), __uint_as_float(acc[e + 1]));
             uint64_t value2;
             if constexpr (EPI == kEpiBias) {
                 value2 = fma2(mul2(acc2, xs2), scale2, second2);
+            } else if constexpr (EPI == kEpiScaleBf16) {
+                value2 = mul2(mul2(acc2, xs2), scale2);
             } else if constexpr (EPI == kEpiGated || EPI == kEpiGatedF16) {
                 uint64_t gate2, up2;
                 if constexpr (EPI == kEpiGated) {
@@ -249,9 +253,10 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
             values[e] = value.x;
             values[e + 1] = value.y;
         }
-        // two fp16 roundings an instruction, over the staged residual
+        // two fp16 (bf16) roundings an instruction, over the staged residual
 #pragma unroll
-        for (int i = 0; i < 8; ++i) result[i] = pack_half2_rn(values[2 * i], values[2 * i + 1]);
+        for (int i = 0; i < 8; ++i)
+            result[i] = EPI == kEpiScaleBf16 ? pack_bf162_rn(values[2 * i], values[2 * i + 1]) : pack_half2_rn(values[2 * i], values[2 * i + 1]);
         *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
         *staged.at(1) = make_uint4(result[4], result[5], result[6], result[7]);
     }
@@ -595,7 +600,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
-            if constexpr (EPI <= kEpiMix && NKS == 0) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
+            if constexpr (scaled(EPI) && NKS == 0) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
             if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN, S::kSecond>(args, column_buffers + buffer * S::kColumnArrays * BN, n0, N, threadIdx.x);
         };
         fetch_operands(first_tile, 0);
@@ -734,17 +739,18 @@ bool make_map(CUtensorMap* map, const void* base, int elem_bytes, int k, int row
     return true;
 }
 
-// An fp16 [rows, cols] row-major tensor as a TMA map with a box of 64 columns by 128 rows in the 128-byte swizzle: the
-// boxes the epilogue stages.
-bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::string* error) {
+// An fp16 (bf16) [rows, cols] row-major tensor as a TMA map with a box of 64 columns by 128 rows in the 128-byte
+// swizzle: the boxes the epilogue stages.
+bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::string* error, bool bf16 = false) {
     EncodeTiled encode = encoder(error);
     if (!encode) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(kBlockM)};
     const cuuint32_t element_strides[2] = {1, 1};
-    const CUresult result = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, element_strides,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+    const CUresult result = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                                   dims, strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (result != CUDA_SUCCESS) {
         if (error) *error = "cuTensorMapEncodeTiled (fp16 [" + std::to_string(rows) + ", " + std::to_string(cols) +
@@ -770,7 +776,7 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
     // the staged epilogues' maps; unused ones repeat the output's, which is always valid
     map_out = map_residual = map_original = map_a;
     if constexpr (S::kStaged) {
-        if (!make_box_map(&map_out, args.out, N, M, error)) return cudaErrorInvalidValue;
+        if (!make_box_map(&map_out, args.out, N, M, error, EPI == kEpiScaleBf16)) return cudaErrorInvalidValue;
         map_residual = map_original = map_out;
         if (args.residual && !make_box_map(&map_residual, args.residual, N, M, error)) return cudaErrorInvalidValue;
         if (mixes(EPI) && !make_box_map(&map_original, args.original, N, M, error)) return cudaErrorInvalidValue;
@@ -855,6 +861,10 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 128) return launch<0, 128, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
+            case kEpiScaleBf16:
+                if (width == 256) return launch<0, 256, false, kEpiScaleBf16, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiScaleBf16, 128>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {

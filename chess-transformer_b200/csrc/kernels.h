@@ -23,6 +23,7 @@ enum GemmEpilogue : int {
     // the fp16 blocks' linears (model/fused_blocks.py:209-225), on fp32 sums:
     kEpiGatedF16 = 8,   // fp16: fp16((g * sigmoid(g)) * u), weight rows = gate rows then up rows
     kEpiMixF16 = 9,     // fp16: (acc + bias) + residual rounded to fp16, then fp16(fma(stream, rs, original * is))
+    kEpiScaleBf16 = 10, // int8: bf16((acc * xs) * ws), the scaled GEMM of the isolated-kernel benchmark (no reference op)
 };
 
 struct GemmArgs {
@@ -75,6 +76,10 @@ cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStre
 cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
                                cudaStream_t stream, std::string* error);
+
+// Attention over 64-token sequences with 64-wide heads, bf16 (attention64.cu): q, k, v, out [B, 64, heads * 64].
+cudaError_t attention64(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int B, int heads, cudaStream_t stream,
+                        std::string* error);
 
 // Heads (heads.cu).
 struct HeadWeights {

@@ -56,6 +56,8 @@ SIGNATURES = {
     "fry_int8_linear": ([_ptr] * 10 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_int8_linear_normed": ([_ptr, _ptr, _c_float] + [_ptr] * 4 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_int8_matmul_i32": ([_ptr] * 3 + [_c_int] * 3 + [_ptr], _c_int),
+    "fry_int8_matmul_scaled_bf16": ([_ptr] * 5 + [_c_int] * 3 + [_ptr], _c_int),
+    "fry_attention_bf16": ([_ptr] * 4 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_norm_quant": ([_ptr, _ptr, _c_float, _ptr, _ptr, _c_int, _c_int, _ptr], _c_int),
     "fry_mix_norm_quant": ([_ptr] * 5 + [_c_float] + [_ptr] * 3 + [_c_int, _c_int, _ptr], _c_int),
     "fry_rotate_quant": ([_ptr] * 3 + [_c_int] * 3 + [_ptr], _c_int),

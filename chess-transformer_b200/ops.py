@@ -102,6 +102,47 @@ def _(x, weight):
     return x.new_empty(*x.shape[:-1], weight.shape[0], dtype=torch.int32)
 
 
+@torch.library.custom_op("fry::int8_matmul_scaled_bf16", mutates_args=())
+def int8_matmul_scaled_bf16(x: torch.Tensor, x_scale: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor) -> torch.Tensor:
+    """The benchmark's isolated int8 GEMM: bf16((acc * x_scale[m]) * weight_scale[n]), acc = x . weight^T in int32, on the
+    int8 tensor-core kernel. x int8 [..., K], weight int8 [N, K], scales fp32."""
+    _cuda("int8_matmul_scaled_bf16", x, x_scale, weight, weight_scale)
+    _dtype("int8_matmul_scaled_bf16", x, torch.int8, "x")
+    _dtype("int8_matmul_scaled_bf16", weight, torch.int8, "weight")
+    x, weight = x.contiguous(), weight.contiguous()
+    N, K = weight.shape
+    M = x.numel() // K
+    out = torch.empty(*x.shape[:-1], N, device=x.device, dtype=torch.bfloat16)
+    library().fry_int8_matmul_scaled_bf16(_ptr(x), _ptr(x_scale.contiguous().float()), _ptr(weight), _ptr(weight_scale.contiguous().float()),
+                                          _ptr(out), M, N, K, _stream(x))
+    return out
+
+
+@int8_matmul_scaled_bf16.register_fake
+def _(x, x_scale, weight, weight_scale):
+    return x.new_empty(*x.shape[:-1], weight.shape[0], dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("fry::attention_bf16", mutates_args=())
+def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int) -> torch.Tensor:
+    """The benchmark's isolated attention: softmax(q k^T / 8) v per sequence and head, q, k, v bf16 [B, 64, heads * 64]."""
+    _cuda("attention_bf16", q, k, v)
+    for name, tensor in (("q", q), ("k", k), ("v", v)):
+        _dtype("attention_bf16", tensor, torch.bfloat16, name)
+    if q.dim() != 3 or q.shape != k.shape or q.shape != v.shape or q.shape[-1] % heads != 0:
+        raise FryError(f"attention_bf16 takes q, k and v of one shape [B, seq, heads * head_dim], got {tuple(q.shape)}")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, seq, width = q.shape
+    out = torch.empty_like(q)
+    library().fry_attention_bf16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, heads, seq, width // heads, _stream(q))
+    return out
+
+
+@attention_bf16.register_fake
+def _(q, k, v, heads):
+    return torch.empty_like(q)
+
+
 @torch.library.custom_op("fry::norm_quant", mutates_args=())
 def norm_quant(x: torch.Tensor, gain: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
     """`chess::norm_quant` (model/int8_blocks.py:191-193): int8 rows of RMSNorm(x) * gain and their scales."""

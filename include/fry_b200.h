@@ -78,6 +78,21 @@ int fry_int8_linear_normed(const uint16_t* x, const uint16_t* gain, float eps, c
  * counterpart exposes them; they are the `acc` of model/int8_blocks.py:85-92. */
 int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int M, int N, int K, void* stream);
 
+/* The benchmark's isolated int8 GEMM: out[M, N] bf16 = bf16((acc * x_scale[m]) * weight_scale[n]), acc = x[M, K] .
+ * weight[N, K]^T in int32, on the same tensor-core kernel as fry_int8_linear. No reference op outputs bf16; the
+ * reference's own int8 linear with no bias is fp16(fma(acc * x_scale, weight_scale, 0)) (model/int8_cuda.py:163-165).
+ * N a multiple of 8, K of 16; x, weight and out 16-byte aligned. */
+int fry_int8_matmul_scaled_bf16(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, uint16_t* out, int M,
+                                int N, int K, void* stream);
+
+/* The benchmark's isolated attention: out = softmax(q k^T / sqrt(64)) v per sequence and head, bf16 in and out, fp32
+ * sums and softmax. q, k, v and out are [B, seq, heads * head_dim] (a projection's rows, heads side by side). Takes
+ * seq 64 and head_dim 64 only, 1 to 1024 heads, B up to 65535. The reference's attention of this shape family is its
+ * template attention (model/fused_blocks.py:54-97), which fry_template_attention replaces; this one has no bias, no
+ * norms and no grouped heads. */
+int fry_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int B, int heads, int seq, int head_dim,
+                       void* stream);
+
 /* `chess::norm_quant` (model/int8_blocks.py:191-193, kernel :156-175): q[M, D] int8, scale[M] fp32 of
  * RMSNorm(x) * gain, a row's scale its absmax / 127. D a multiple of 8 up to 1024. */
 int fry_norm_quant(const uint16_t* x, const uint16_t* gain, float eps, int8_t* q, float* scale, int M, int D, void* stream);
