@@ -254,6 +254,12 @@ int fry_int8_matmul_i32(const int8_t* x, const int8_t* weight, int32_t* out, int
     return check(fry::gemm(0, fry::kEpiInt32, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_matmul_i32", detail);
 }
 
+int fry_square_feature_rows(const int64_t* boards, int B, int32_t* rows, void* stream) {
+    if (B < 0) return fail(FRY_ERROR_SHAPE, "fry_square_feature_rows needs B >= 0");
+    if (!aligned16(boards) || (reinterpret_cast<uintptr_t>(rows) & 3u)) return fail(FRY_ERROR_SHAPE, "fry_square_feature_rows needs aligned tensors");
+    return check(fry::square_feature_rows(boards, rows, B, as_stream(stream)), "fry_square_feature_rows");
+}
+
 int fry_int8_matmul_scaled_bf16(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, uint16_t* out, int M,
                                 int N, int K, void* stream) {
     if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0)

@@ -69,6 +69,9 @@ cudaError_t board_embedding_lean(const uint8_t* lean_rows, const uint16_t* embed
                                  uint16_t* out, int B, int D, cudaStream_t stream);
 cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
                             uint16_t* out, int B, int D, cudaStream_t stream);
+// Each square's 23 feature rows of the table (SquareFeatures.indices with the features' first rows added,
+// model/model.py:134-169): boards int64 [B, 70] -> rows int32 [B, 64, 23].
+cudaError_t square_feature_rows(const int64_t* boards, int32_t* rows, int B, cudaStream_t stream);
 
 // Template attention (attention.cu).
 // paired [64][64][8] fp16: templates[t][i][j] at paired[i][j][t]

@@ -128,17 +128,14 @@ FRY_DEVICE int code_at(const int* codes, int file, int rank) {
     return (file >= 0 && file < 8 && rank >= 0 && rank < 8) ? codes[rank * 8 + file] : kEdge;
 }
 
-// One CTA per (board, 256 columns): the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
-// A board's tokens: int64 [70] (boards, pitch 70) or the first 70 bytes of a lean lane's row (pitch kLeanRow).
+// A board's tokens into codes[70] (a token outside the vocabulary read as 0 and recorded), the squares of our king,
+// their king, our queen and their queen into firsts[4] (64: none), and each square's 23 feature rows of the table, each
+// feature's first row added (SquareFeatures.indices, model/model.py:134-169), into rows[64][23]. A board's tokens:
+// int64 [70] (boards, pitch 70) or the first 70 bytes of a lean lane's row (pitch kLeanRow). All 256 threads of the
+// CTA call it; it ends with the rows written but not yet synchronised.
 template <typename Token>
-__global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict__ boards, int pitch, const uint16_t* __restrict__ embed,
-                                                        const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
-                                                        uint16_t* __restrict__ out, int D) {
-    grid_dependency_start();
-    __shared__ int codes[kTokens];
-    __shared__ int firsts[4];
-    __shared__ int rows[kSquares][kFeatures];
-    const int b = blockIdx.x, tid = threadIdx.x;
+FRY_DEVICE void board_feature_rows(const Token* __restrict__ boards, int pitch, int b, int* codes, int* firsts, int (*rows)[kFeatures],
+                                   int tid) {
     for (int t = tid; t < kTokens; t += blockDim.x) {
         const int64_t token = static_cast<int64_t>(boards[static_cast<size_t>(b) * pitch + t]);
         const bool ok = t < kSquares ? (token >= 0 && token < kPieceCodes) : (token >= 0 && token < kVocab);
@@ -202,6 +199,19 @@ __global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict_
             }
         }
     }
+}
+
+// One CTA per (board, 256 columns): the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
+template <typename Token>
+__global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict__ boards, int pitch, const uint16_t* __restrict__ embed,
+                                                        const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
+                                                        uint16_t* __restrict__ out, int D) {
+    grid_dependency_start();
+    __shared__ int codes[kTokens];
+    __shared__ int firsts[4];
+    __shared__ int rows[kSquares][kFeatures];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    board_feature_rows(boards, pitch, b, codes, firsts, rows, tid);
     __syncthreads();
     // this CTA's slice of the columns: [blockIdx.y * 256, + 256)
     const int first = blockIdx.y * 256, width = D - first < 256 ? D - first : 256;
@@ -231,6 +241,18 @@ __global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict_
             packed[i] = f2h_bits(__fadd_rn(__fadd_rn(e[i], p[i]), h2f_bits(f2h_bits(features[i]))));
         *reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * kTokens + t) * D + col) = *reinterpret_cast<const uint4*>(packed);
     }
+}
+
+// One CTA per board: its squares' 23 feature rows, int32 [64, 23] a board (the rows embedding_kernel sums).
+__global__ void __launch_bounds__(256) feature_rows_kernel(const int64_t* __restrict__ boards, int32_t* __restrict__ out) {
+    grid_dependency_start();
+    __shared__ int codes[kTokens];
+    __shared__ int firsts[4];
+    __shared__ int rows[kSquares][kFeatures];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    board_feature_rows(boards, kTokens, b, codes, firsts, rows, tid);
+    __syncthreads();
+    for (int i = tid; i < kSquares * kFeatures; i += blockDim.x) out[static_cast<size_t>(b) * kSquares * kFeatures + i] = rows[i / kFeatures][i % kFeatures];
 }
 
 // ---- launchers ------------------------------------------------------------------------------------------------
@@ -329,6 +351,11 @@ cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const 
     if (D % 8 != 0) return cudaErrorInvalidValue;
     return launch_dependent(embedding_kernel<int64_t>, dim3(B, (D + 255) / 256), dim3(256), 0, stream, boards, kTokens, embed, position,
                             table, out, D);
+}
+
+cudaError_t square_feature_rows(const int64_t* boards, int32_t* rows, int B, cudaStream_t stream) {
+    if (B <= 0) return cudaSuccess;
+    return launch_dependent(feature_rows_kernel, dim3(B), dim3(256), 0, stream, boards, rows);
 }
 
 cudaError_t board_embedding_lean(const uint8_t* lean_rows, const uint16_t* embed, const uint16_t* position, const uint16_t* table,

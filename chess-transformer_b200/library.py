@@ -67,6 +67,7 @@ SIGNATURES = {
     "fry_linear_full": ([_ptr] * 8 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_linear_norm_quant": ([_ptr] * 6 + [_c_float] + [_ptr] * 2 + [_c_int] * 3 + [_ptr], _c_int),
     "fry_board_embedding": ([_ptr] * 5 + [_c_int, _c_int, _ptr], _c_int),
+    "fry_square_feature_rows": ([_ptr, _c_int, _ptr, _ptr], _c_int),
     "fry_heads_workspace_bytes": ([_c_int, _c_int], _size),
     "fry_heads": ([_ptr, ctypes.POINTER(FryHeads), _c_float, _ptr, _ptr, _size, _c_int, _c_int, _ptr], _c_int),
     "fry_heads_noalloc": ([_ptr, ctypes.POINTER(FryHeads), _c_float, _ptr, _c_int, _c_int, _ptr], _c_int),

@@ -12,14 +12,16 @@ weights are folded in fp64 (model/fused_blocks.py:815-824). The whole forward is
 enqueues every kernel on the current stream, so the module records into CUDA graphs like the reference's.
 """
 import ctypes
+import itertools
 import math
+import weakref
 from pathlib import Path
 
 import numpy as np
 import torch
 from torch import nn
 
-from .encoding import BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
+from .encoding import ANSWER_WIDTH, BOARD_VOCAB_SIZE, FEATURE_TABLE_ROWS, LEAN_COLUMNS, LEAN_ROW, TOKENS_PER_BOARD, VALUE_TOKEN_DIM
 from .library import BLOCK_FP16, BLOCK_INT8, FryBlock, FryError, FryNetwork, library
 from .ops import heads_struct, pair_templates
 
@@ -184,6 +186,9 @@ class Int8Network(nn.Module):
             self.tensors["templates"] = pair_templates(self.tensors["templates"])
             torch.cuda.current_stream(device).synchronize()
         self._network = self._struct()
+        self._handle = next(_HANDLES)
+        _NETWORKS[self._handle] = weakref.ref(self)
+        weakref.finalize(self, _NETWORKS.pop, self._handle, None)
 
     def _struct(self) -> FryNetwork:
         g, t = self.geometry, self.tensors
@@ -203,12 +208,39 @@ class Int8Network(nn.Module):
 
     def forward_lean(self, lean_rows: torch.Tensor) -> torch.Tensor:
         """Lean lanes' rows uint8 [B, LEAN_ROW] cuda (tokens, then int16 answer columns) -> answers fp32 [B, LEAN_COLUMNS]:
-        forward(tokens) gathered at the columns (engine/inference.py:130-135), the gather in the heads' last kernel."""
+        forward(tokens) gathered at the columns (engine/inference.py:130-135), the gather in the heads' last kernel. Runs
+        as the torch op fry::forward_lean."""
         if not lean_rows.is_cuda or lean_rows.device != self.device:
             raise FryError(f"Int8Network on {self.device} got lean rows on {lean_rows.device}")
+        return torch.ops.fry.forward_lean(lean_rows, self._handle)
+
+    def workspace_bytes(self, boards: int) -> int:
+        return library().fry_forward_workspace_bytes(ctypes.byref(self._network), boards)
+
+    def forward(self, board_state: torch.Tensor) -> torch.Tensor:
+        """boards [B, 70] tokens on this network's device -> answer rows fp32 [B, 1969], as the torch op fry::forward, so
+        torch.compile sees the forward through the op's fake implementation, as it sees the reference's custom ops."""
+        if not board_state.is_cuda or board_state.device != self.device:
+            raise FryError(f"Int8Network on {self.device} got boards on {board_state.device}")
+        return torch.ops.fry.forward(board_state.to(torch.int64), self._handle)
+
+    def _rows(self, boards: torch.Tensor) -> torch.Tensor:
+        boards = boards.contiguous()
+        if boards.dtype != torch.int64 or boards.dim() != 2 or boards.shape[1] != TOKENS_PER_BOARD:
+            raise FryError(f"boards are int64 [B, {TOKENS_PER_BOARD}] tokens, got {boards.dtype} {tuple(boards.shape)}")
+        B = boards.shape[0]
+        rows = torch.empty(B, ANSWER_WIDTH, device=self.device, dtype=torch.float32)
+        lib = library()
+        size = lib.fry_forward_workspace_bytes(ctypes.byref(self._network), B)
+        workspace = torch.empty(max(size, 1), device=self.device, dtype=torch.uint8)
+        lib.fry_forward(ctypes.byref(self._network), ctypes.c_void_p(boards.data_ptr()), B, ctypes.c_void_p(rows.data_ptr()),
+                        ctypes.c_void_p(workspace.data_ptr()), size, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        return rows
+
+    def _lean_answers(self, lean_rows: torch.Tensor) -> torch.Tensor:
+        lean_rows = lean_rows.contiguous()
         if lean_rows.dtype != torch.uint8 or lean_rows.dim() != 2 or lean_rows.shape[1] != LEAN_ROW:
             raise FryError(f"lean rows are uint8 [B, {LEAN_ROW}], got {lean_rows.dtype} {tuple(lean_rows.shape)}")
-        lean_rows = lean_rows.contiguous()
         B = lean_rows.shape[0]
         answers = torch.empty(B, LEAN_COLUMNS, device=self.device, dtype=torch.float32)
         lib = library()
@@ -218,23 +250,44 @@ class Int8Network(nn.Module):
                              ctypes.c_void_p(workspace.data_ptr()), size, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
         return answers
 
-    def workspace_bytes(self, boards: int) -> int:
-        return library().fry_forward_workspace_bytes(ctypes.byref(self._network), boards)
 
-    def forward(self, board_state: torch.Tensor) -> torch.Tensor:
-        if not board_state.is_cuda or board_state.device != self.device:
-            raise FryError(f"Int8Network on {self.device} got boards on {board_state.device}")
-        boards = board_state.to(torch.int64).contiguous()
-        B = boards.shape[0]
-        if boards.dim() != 2 or boards.shape[1] != TOKENS_PER_BOARD:
-            raise FryError(f"boards are [B, {TOKENS_PER_BOARD}] tokens, got {tuple(boards.shape)}")
-        rows = torch.empty(B, 1969, device=self.device, dtype=torch.float32)
-        lib = library()
-        size = lib.fry_forward_workspace_bytes(ctypes.byref(self._network), B)
-        workspace = torch.empty(max(size, 1), device=self.device, dtype=torch.uint8)
-        lib.fry_forward(ctypes.byref(self._network), ctypes.c_void_p(boards.data_ptr()), B, ctypes.c_void_p(rows.data_ptr()),
-                        ctypes.c_void_p(workspace.data_ptr()), size, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
-        return rows
+# The networks the ops below run, by handle: an op takes tensors and plain values, so a network is named by an integer
+# that Int8Network sets up (torch.compile keeps it as a constant of the traced graph). The registry holds weak
+# references: a network that is gone is refused, not kept alive.
+_NETWORKS: dict[int, "weakref.ReferenceType[Int8Network]"] = {}
+_HANDLES = itertools.count(1)
+
+
+def _registered(handle: int) -> Int8Network:
+    found = _NETWORKS.get(handle)
+    network = found() if found is not None else None
+    if network is None:
+        raise FryError(f"no live Int8Network has handle {handle}")
+    return network
+
+
+@torch.library.custom_op("fry::forward", mutates_args=())
+def forward_op(boards: torch.Tensor, network: int) -> torch.Tensor:
+    """`FusedTransformer.forward` + `answer_rows` (model/fused_blocks.py:856-862, engine/inference.py:19-23) of the
+    network with this handle: boards int64 [B, 70] -> rows fp32 [B, 1969], one fry_forward on the current stream."""
+    return _registered(network)._rows(boards)
+
+
+@forward_op.register_fake
+def _(boards, network):
+    return boards.new_empty(boards.shape[0], ANSWER_WIDTH, dtype=torch.float32)
+
+
+@torch.library.custom_op("fry::forward_lean", mutates_args=())
+def forward_lean_op(lean_rows: torch.Tensor, network: int) -> torch.Tensor:
+    """The lean lanes' forward (engine/inference.py:130-135) of the network with this handle: rows uint8 [B, 508] ->
+    answers fp32 [B, 219], one fry_forward_lean on the current stream."""
+    return _registered(network)._lean_answers(lean_rows)
+
+
+@forward_lean_op.register_fake
+def _(lean_rows, network):
+    return lean_rows.new_empty(lean_rows.shape[0], LEAN_COLUMNS, dtype=torch.float32)
 
 
 def load_checkpoint(checkpoint_path: Path) -> tuple[dict, dict]:
@@ -246,15 +299,21 @@ def load_checkpoint(checkpoint_path: Path) -> tuple[dict, dict]:
     return {name: tensor.float() if tensor.is_floating_point() else tensor for name, tensor in checkpoint["state_dict"].items()}, settings
 
 
-def int8_model(checkpoint_path: Path, fp16_blocks: int = 0, weights: dict | None = None, device: torch.device | str | None = None) -> Int8Network:
+def int8_model(checkpoint_path: Path, fp16_blocks: int = 0, weights: dict | None = None, device: torch.device | str | None = None,
+               calibration: tuple[torch.Tensor, torch.Tensor | None] | None = None) -> Int8Network:
     """`engine.inference.int8_model` (engine/inference.py:267-272) on this engine: the blocks `weights` has run in int8,
     the others in fp16. `weights` are Int8Weights (the reference's cached GPTQ weights load unchanged, their blocks
-    fixing the layout); None rounds every block but the last (FP16_LAST_LAYERS, engine/quantization.py:46,128) to
-    nearest. Choosing fp16_blocks > 0 more blocks needs the reference's calibration (block_errors,
-    engine/quantization.py:148-172): with weights None it is refused."""
-    if fp16_blocks and weights is None:
-        raise FryError("choosing fp16_blocks needs the reference's calibration: pass its cached weights, which leave those blocks out")
+    fixing the layout). Without them, as the reference does, the checkpoint's weights come from
+    `quantization.int8_weights(checkpoint_path, fp16_blocks, calibration)`: the weights the reference cached for this
+    checkpoint, or with `calibration` (boards int64 [n, 70], and for fp16_blocks > 0 their legal moves bool [n, 1968])
+    GPTQ over those positions on this GPU with the fp16_blocks blocks of the largest block_errors kept fp16, cached."""
+    device = torch.device(device if device is not None else "cuda")
+    if device.type != "cuda":
+        raise FryError("int8_model runs on a CUDA device only")
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     state, settings = load_checkpoint(Path(checkpoint_path))
     if weights is None:
-        weights = quantize(state, settings, list(range(geometry(settings)["layers"] - FP16_LAST_LAYERS)))
+        from .quantization import int8_weights
+        weights = int8_weights(Path(checkpoint_path), fp16_blocks, calibration, device)
     return Int8Network(state, settings, weights, device)

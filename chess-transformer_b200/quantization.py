@@ -1,15 +1,33 @@
 """GPTQ on the device: drop-ins for the reference's `gptq` (engine/quantization.py:76-99), `input_hessians` (:103-119),
-`compute_int8_weights` (:122-140) and `block_errors` (:144-169), the ranking that picks the blocks kept in fp16.
+`compute_int8_weights` (:122-140), `block_errors` (:144-169), the ranking that picks the blocks kept in fp16, and
+`int8_weights` (:188-207), a checkpoint's int8 weights read from the cache or computed and cached.
 fry_gptq rounds a matmul's weights in fp64 on its GPU, and fry_hessian_accumulate sums the inputs x^T x that its Hessian
 is made of; the answers are the reference's Int8Weights.
 """
 import ctypes
+import hashlib
+import os
+import sys
+from contextlib import suppress
+from pathlib import Path
 
 import torch
 from torch import nn
 
+from .calibration import CalibrationNetwork
+from .encoding import NUM_MOVE_IDS, TOKENS_PER_BOARD
 from .library import FryError, library
-from .network import FP16_LAST_LAYERS, HADAMARD_BLOCK, Int8Network, down_inputs, hadamard
+from .network import DOWN_INPUT_MULTIPLE, FP16_LAST_LAYERS, HADAMARD_BLOCK, Int8Network, down_inputs, geometry, hadamard, load_checkpoint
+
+# The cache of computed int8 weights, shared with the reference's engine: the same folder (its environment variable, else
+# ~/.cache/chess_transformer/int8) and, for the reference's own calibration, the same file names, so the weights the
+# reference cached for a checkpoint load here unchanged (engine/quantization.py:26-48,174-185).
+CACHE_VARIABLE = "CHESS_TRANSFORMER_INT8_CACHE"
+# what the reference's cached files are named by: its rounding code's version, its calibration (1024 positions of its
+# PGN from game 1000, every 9th ply), GPTQ's dampening and column block, the blocks kept fp16 at the end, the down's
+# rotation and padding, and for a choice of fp16 blocks the choice's version and count
+REFERENCE_ROUNDING = (1, 1024, 1000, 9, 0.01, 128, FP16_LAST_LAYERS, HADAMARD_BLOCK, DOWN_INPUT_MULTIPLE)
+CHOICE_VERSION = 1
 
 NOT_POSITIVE_DEFINITE = 6  # the device status code fry_gptq records
 
@@ -130,3 +148,100 @@ def block_errors(state: dict, settings: dict, weights: dict, boards: torch.Tenso
 def fp16_choice(errors: dict[int, float], fp16_blocks: int) -> list[int]:
     """engine/quantization.py:196-198: the fp16_blocks blocks of the largest block_errors, which stay fp16."""
     return sorted(errors, key=errors.get, reverse=True)[:fp16_blocks]
+
+
+def cache_folder() -> Path | None:
+    """The weights cache's folder: $CHESS_TRANSFORMER_INT8_CACHE, else ~/.cache/chess_transformer/int8; None without
+    either (engine/quantization.py:29-35)."""
+    if os.environ.get(CACHE_VARIABLE):
+        return Path(os.environ[CACHE_VARIABLE])
+    try:
+        return Path.home() / ".cache" / "chess_transformer" / "int8"
+    except RuntimeError:
+        return None
+
+
+def calibration_digest(boards: torch.Tensor, legal: torch.Tensor | None = None) -> str:
+    """sha256 of the calibration positions' tokens (and legal-move masks, when given), naming weights calibrated on them."""
+    digest = hashlib.sha256(boards.detach().to(device="cpu", dtype=torch.int64).contiguous().numpy().tobytes())
+    if legal is not None:
+        digest.update(legal.detach().to(device="cpu", dtype=torch.bool).contiguous().numpy().tobytes())
+    return digest.hexdigest()
+
+
+def cached_weights_path(checkpoint_path: Path, fp16_blocks: int, calibration: str | None = None) -> Path | None:
+    """The cache file of a checkpoint's int8 weights: named by the checkpoint's sha256 and a digest of how they were
+    rounded. With calibration None, the reference's own name for its own calibration (engine/quantization.py:174-185);
+    with a calibration digest, the same name with that digest among the rounding's settings, so weights calibrated on
+    other positions never pass for the reference's."""
+    folder = cache_folder()
+    if folder is None:
+        return None
+    with open(checkpoint_path, "rb") as checkpoint:
+        digest = hashlib.file_digest(checkpoint, "sha256").hexdigest()
+    rounding = REFERENCE_ROUNDING + ((CHOICE_VERSION, fp16_blocks) if fp16_blocks else ())
+    if calibration is not None:
+        rounding += ("calibration", calibration)
+    return folder / f"{digest}_{hashlib.sha256(repr(rounding).encode()).hexdigest()[:16]}.pt"
+
+
+def save_cached_weights(weights: dict, path: Path | None) -> None:
+    """Written under another name and renamed, so engines starting together never read half a file; a cache that cannot
+    be written only costs the next start its time (engine/quantization.py:211-224)."""
+    if path is None:
+        print("the int8 weights are not cached: there is no cache folder", file=sys.stderr)
+        return
+    partial = path.with_name(f"{path.name}.{os.getpid()}.partial")
+    try:
+        path.parent.mkdir(parents=True, exist_ok=True)
+        torch.save(weights, partial)
+        os.replace(partial, path)
+    except (OSError, RuntimeError) as error:
+        with suppress(OSError):
+            partial.unlink()
+        print(f"the int8 weights are not cached: {error}", file=sys.stderr)
+
+
+def int8_weights(checkpoint_path: Path, fp16_blocks: int, calibration: tuple[torch.Tensor, torch.Tensor | None] | None = None,
+                 device: torch.device | str | None = None) -> dict:
+    """engine/quantization.py:188-207: the checkpoint's Int8Weights on the CPU, every block in int8 but the last and the
+    fp16_blocks blocks of the largest block_errors.
+
+    calibration None: the weights the reference cached for this checkpoint (its own calibration on its PGN's positions,
+    under its own file name), or FryError if it has none. calibration (boards int64 [n, 70], legal bool [n, 1968] or
+    None): weights calibrated on those positions, read from the cache or computed on `device` (GPTQ over the fp64
+    network's input Hessians, then, for fp16_blocks > 0, block_errors over the positions' legal moves) and cached."""
+    if fp16_blocks < 0:
+        raise ValueError(f"a count of blocks to keep in fp16, not {fp16_blocks}")
+    checkpoint_path = Path(checkpoint_path)
+    if calibration is None:
+        path = cached_weights_path(checkpoint_path, fp16_blocks)
+        if path is not None and path.exists():
+            return torch.load(path, weights_only=True)
+        raise FryError(f"no cached int8 weights for {checkpoint_path} with {fp16_blocks} more fp16 blocks, and no calibration positions to "
+                       "compute them: pass calibration=(boards [n, 70], legal [n, 1968]) (the reference reads 1024 positions of its PGN "
+                       "through python-chess), or the weights themselves")
+    boards, legal = calibration if isinstance(calibration, (tuple, list)) else (calibration, None)
+    boards = torch.as_tensor(boards)
+    if boards.dim() != 2 or boards.shape[1] != TOKENS_PER_BOARD:
+        raise FryError(f"calibration boards are [n, {TOKENS_PER_BOARD}] tokens, got {tuple(boards.shape)}")
+    if fp16_blocks and (legal is None or tuple(legal.shape) != (boards.shape[0], NUM_MOVE_IDS)):
+        raise FryError(f"choosing {fp16_blocks} fp16 blocks needs the calibration positions' legal moves, bool [n, {NUM_MOVE_IDS}]")
+    path = cached_weights_path(checkpoint_path, fp16_blocks, calibration_digest(boards, legal if fp16_blocks else None))
+    if path is not None and path.exists():
+        return torch.load(path, weights_only=True)
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    state, settings = load_checkpoint(checkpoint_path)
+    if fp16_blocks:
+        weights = int8_weights(checkpoint_path, 0, (boards, None), device)
+        errors = block_errors(state, settings, weights, boards, legal)
+        kept = fp16_choice(errors, fp16_blocks)
+        weights = {layer: matmuls for layer, matmuls in weights.items() if layer not in kept}
+    else:
+        with torch.cuda.device(device):
+            model = CalibrationNetwork(state, geometry(settings), device)
+            weights = {layer: {name: tuple(tensor.cpu() for tensor in pair) for name, pair in matmuls.items()}
+                       for layer, matmuls in int8_weights_from_sums(state, input_hessians(model, boards)).items()}
+            del model
+    save_cached_weights(weights, path)
+    return weights

@@ -151,6 +151,11 @@ int fry_linear_norm_quant(const uint16_t* x, const uint16_t* weight, const uint1
 int fry_board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table, uint16_t* out,
                         int B, int D, void* stream);
 
+/* `SquareFeatures.indices` (model/model.py:134-169) with each feature's first row added: boards int64 [B, 70] -> rows
+ * int32 [B, 64, 23], the row of the square-feature table each square reads for each of the 23 features (the rows
+ * fry_board_embedding sums). For offline work on the checkpoint's own precision, such as calibration. */
+int fry_square_feature_rows(const int64_t* boards, int B, int32_t* rows, void* stream);
+
 /* The heads after the last block, as the reference runs them on B200 (model/fused_blocks.py:863-874, weights folded by
  * head_weights :815-824) with answer_rows (engine/inference.py:19-23). stream [B, 70, D] fp16 -> rows [B, 1969] fp32.
  * workspace: device scratch of fry_heads_workspace_bytes(B, D) bytes. */

@@ -77,27 +77,12 @@ sys.modules["engine.inference"] = _inference
 import engine.quantization as ref_quantization
 
 from oracle.model import seeded_state_dict
+from seeded_boards import golden_boards  # noqa: E402  (tests/golden, on the path above)
 
 SMALL = {"d_model": 128, "num_layers": 3, "n_heads": 4, "kv_heads": 2, "qk_ratio": [0.25, 0.5, 0.75], "mlp_hidden": 320, "value_bins": 16}
 # config 0's network in Fry's geometry: d 256, 8 query heads of 32, 4 key/value heads, dq 8/16/24, SwiGLU 1024, 128 bins
 TINY = {"d_model": 256, "num_layers": 6, "n_heads": 8, "kv_heads": 4, "qk_ratio": [0.25, 0.5, 0.75] * 2, "mlp_hidden": 1024,
         "value_bins": 128}
-
-
-def golden_boards(count: int, seed: int) -> np.ndarray:
-    """Seeded legal-looking boards (each king once, 2-30 other pieces, no pawns on the back ranks, flag tokens)."""
-    rng = np.random.default_rng(seed)
-    boards = np.zeros((count, 70), dtype=np.uint8)
-    for b in range(count):
-        squares = rng.permutation(64)
-        boards[b, squares[0]], boards[b, squares[1]] = 6, 12
-        for square in squares[2:2 + int(rng.integers(2, 31))]:
-            codes = [2, 3, 4, 5, 8, 9, 10, 11] if square < 8 or square >= 56 else [1, 2, 3, 4, 5, 7, 8, 9, 10, 11]
-            boards[b, square] = rng.choice(codes)
-        boards[b, 64] = 13 + rng.integers(0, 2)
-        boards[b, 65:69] = 15 + rng.integers(0, 2, size=4)
-        boards[b, 69] = 17 + (int(rng.integers(40, 48)) if rng.random() < 0.2 else 0)
-    return boards
 
 
 def reference_model(settings: dict, seed: int) -> ref_model.ChessTransformer:

@@ -119,12 +119,48 @@ def test_the_synthetic_checkpoint_loads_into_the_oracles_shapes():
     assert all(tuple(state[name].shape) == shape for name, shape in shapes.items())
 
 
-def test_int8_model_needs_the_references_weights_to_choose_fp16_blocks(tmp_path):
+def test_int8_model_without_weights_needs_a_cache_or_calibration_positions(tmp_path, monkeypatch):
+    from chess_transformer_b200 import quantization
+    monkeypatch.setenv(quantization.CACHE_VARIABLE, str(tmp_path / "cache"))
     torch.save({"model_settings": SMALL, "state_dict": om.seeded_state_dict(SMALL, 0)}, tmp_path / "model.pt")
-    with pytest.raises(FryError, match="calibration"):
-        fry_network.int8_model(tmp_path / "model.pt", fp16_blocks=1)
+    for blocks in (0, 1):
+        with pytest.raises(FryError, match="calibration"):
+            quantization.int8_weights(tmp_path / "model.pt", blocks)
+    with pytest.raises(FryError, match="legal moves"):
+        quantization.int8_weights(tmp_path / "model.pt", 1, (torch.zeros(4, 70, dtype=torch.long), None))
+    with pytest.raises(ValueError, match="count of blocks"):
+        quantization.int8_weights(tmp_path / "model.pt", -1)
     with pytest.raises(FryError, match="CUDA"):
         fry_network.int8_model(tmp_path / "model.pt", device="cpu")
+
+
+def test_the_weights_cache_is_named_as_the_references(tmp_path, monkeypatch):
+    # engine/quantization.py:174-185: <sha256 of the checkpoint>_<16 hex of the rounding settings>.pt under the cache
+    # folder, so the weights the reference cached load unchanged; weights calibrated on other positions get other names
+    import hashlib
+    from chess_transformer_b200 import quantization
+    monkeypatch.setenv(quantization.CACHE_VARIABLE, str(tmp_path))
+    checkpoint = tmp_path / "model.pt"
+    checkpoint.write_bytes(b"checkpoint bytes")
+    digest = hashlib.sha256(b"checkpoint bytes").hexdigest()
+    rounding = (1, 1024, 1000, 9, 0.01, 128, 1, 32, 128)
+    assert quantization.cached_weights_path(checkpoint, 0) == tmp_path / f"{digest}_{hashlib.sha256(repr(rounding).encode()).hexdigest()[:16]}.pt"
+    with_choice = rounding + (1, 2)
+    assert quantization.cached_weights_path(checkpoint, 2).name == f"{digest}_{hashlib.sha256(repr(with_choice).encode()).hexdigest()[:16]}.pt"
+    ours = quantization.cached_weights_path(checkpoint, 0, quantization.calibration_digest(torch.zeros(2, 70, dtype=torch.long)))
+    assert ours.name.startswith(digest) and ours != quantization.cached_weights_path(checkpoint, 0)
+
+
+def test_the_forward_ops_have_fake_implementations_for_torch_compile():
+    # dynamo traces the forward through these (the reference's custom ops register fakes the same way,
+    # model/int8_blocks.py:141-144); no GPU is touched
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import chess_transformer_b200.network  # noqa: F401  (registers fry::forward and fry::forward_lean)
+    with FakeTensorMode():
+        rows = torch.ops.fry.forward(torch.empty(5, 70, dtype=torch.int64), 1)
+        answers = torch.ops.fry.forward_lean(torch.empty(3, fry_encoding.LEAN_ROW, dtype=torch.uint8), 1)
+    assert rows.shape == (5, fry_encoding.ANSWER_WIDTH) and rows.dtype == torch.float32
+    assert answers.shape == (3, fry_encoding.LEAN_COLUMNS) and answers.dtype == torch.float32
 
 
 def test_the_lean_row_format_is_the_rust_loops():

@@ -149,6 +149,31 @@ def test_recorded_graphs_give_the_eager_bits(fry):
         assert np.array_equal(recorded.replay(boards[:17]), eager[:17])
 
 
+def test_the_engines_compiled_wrapping_records_and_replays_the_eager_bits(fry):
+    # engine_search.network_graphs on capability (10, 0) (engine/engine_search.py:196-205) wraps the network in
+    # ExactSizeCompiled (engine/inference.py:252-263): torch.compile(dynamic=False) for the chunk size and dynamic=True
+    # for the rest, floats specialised; its runtime then records every size on a side stream, one private pool per lane.
+    # The forward is the custom op fry::forward, which dynamo takes whole through its fake implementation.
+    network, _ = fry
+    chunk = 16
+    exact, dynamic = torch.compile(network, dynamic=False), torch.compile(network, dynamic=True)
+
+    def compiled(boards: torch.Tensor) -> torch.Tensor:
+        with torch._dynamo.config.patch(specialize_float=True):
+            return (exact if len(boards) == chunk else dynamic)(boards)
+
+    boards = random_boards(chunk, 21)
+    with torch.no_grad():
+        eager = network(torch.from_numpy(boards).long().cuda()).cpu().numpy()
+        assert np.array_equal(compiled(torch.from_numpy(boards).long().cuda()).cpu().numpy(), eager)
+        assert np.array_equal(compiled(torch.from_numpy(boards[:5]).long().cuda()).cpu().numpy(), eager[:5])
+    for _ in range(2):  # two lanes, each with its own graphs and pool
+        recorded = Recorded(compiled, torch.from_numpy(random_boards(chunk, 22)).long().cuda(), [1, 2, 5, 8, chunk])
+        assert np.array_equal(recorded.replay(boards), eager)
+        assert np.array_equal(recorded.replay(boards[:5]), eager[:5])
+        assert np.array_equal(recorded.replay(boards[:7]), eager[:7])
+
+
 def test_a_token_outside_the_vocabulary_is_reported_not_faulted(fry):
     network, _ = fry
     lib = library()
