@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             for (int r = 0; r < kRowHalves; ++r) {
                 if (!SQUARES && r == 1) continue;
                 const uint64_t x = fma2(s2[j][r], log2e2, shift2[r]);  // (s - top) log2 e
-                const uint64_t p = pair2(ex2_approx(lane0(x)), ex2_approx(lane1(x)));
+                const uint64_t p = pair2(ex2_approx_ftz(lane0(x)), ex2_approx_ftz(lane1(x)));
                 s2[j][r] = p;
                 total2[r] = add2(total2[r], p);
             }

@@ -121,10 +121,10 @@ __global__ void __launch_bounds__(kAttention64Threads) attention64_kernel(const 
     float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        s[j][0] = ex2_approx(__fmaf_rn(s[j][0], scale_log2, -top0));
-        s[j][1] = ex2_approx(__fmaf_rn(s[j][1], scale_log2, -top0));
-        s[j][2] = ex2_approx(__fmaf_rn(s[j][2], scale_log2, -top1));
-        s[j][3] = ex2_approx(__fmaf_rn(s[j][3], scale_log2, -top1));
+        s[j][0] = ex2_approx_ftz(__fmaf_rn(s[j][0], scale_log2, -top0));
+        s[j][1] = ex2_approx_ftz(__fmaf_rn(s[j][1], scale_log2, -top0));
+        s[j][2] = ex2_approx_ftz(__fmaf_rn(s[j][2], scale_log2, -top1));
+        s[j][3] = ex2_approx_ftz(__fmaf_rn(s[j][3], scale_log2, -top1));
         sum0 += s[j][0] + s[j][1];
         sum1 += s[j][2] + s[j][3];
     }

@@ -350,6 +350,20 @@ FRY_DEVICE float ex2_approx(float x) {
     asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// 2^x with denormal results flushed to zero (the bare 2^x instruction): where 2^x only enters 1 + 2^x or a softmax's
+// probabilities, which fp16 rounds to 0 far above fp32's denormals, the results are those of ex2_approx
+FRY_DEVICE float ex2_approx_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// 1/x by the reciprocal instruction alone (at most 1 ulp off; no full-range scaling: for x from 1 up, where it is exact
+// in range and gives 0 at infinity)
+FRY_DEVICE float rcp_approx_ftz(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 FRY_DEVICE float div_full(float a, float b) {
     float y;
     asm("div.full.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));

@@ -231,10 +231,11 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                     gate2 = add2(acc2, second2);
                     up2 = pair2(__uint_as_float(up[e]), __uint_as_float(up[e + 1]));
                 }
-                // silu(g) = g * sigmoid(g), sigmoid from the 2^x instruction: 1 / (1 + 2^(-g log2 e))
+                // silu(g) = g * sigmoid(g), sigmoid from the 2^x and reciprocal instructions: 1 / (1 + 2^(-g log2 e)), the
+                // denominator from 1 to infinity
                 const float2 power = lanes(mul2(gate2, pair2(-1.4426950408889634f, -1.4426950408889634f)));
-                const float2 denominator = lanes(add2(pair2(ex2_approx(power.x), ex2_approx(power.y)), pair2(1.0f, 1.0f)));
-                const uint64_t sigmoid2 = pair2(div_full(1.0f, denominator.x), div_full(1.0f, denominator.y));
+                const float2 denominator = lanes(add2(pair2(ex2_approx_ftz(power.x), ex2_approx_ftz(power.y)), pair2(1.0f, 1.0f)));
+                const uint64_t sigmoid2 = pair2(rcp_approx_ftz(denominator.x), rcp_approx_ftz(denominator.y));
                 value2 = mul2(mul2(gate2, sigmoid2), up2);
             } else if constexpr (EPI == kEpiResidual || EPI == kEpiMix) {
                 value2 = fma2(mul2(acc2, xs2), scale2, pair2(h2f_exact(res[e]), h2f_exact(res[e + 1])));
