@@ -249,10 +249,24 @@ def cpu_baseline() -> dict:
                       f"boards for the sweep) on {cores} threads of {os.cpu_count()} host cores"}
 
 
+def graphed(torch, stream, run):
+    """run() recorded once into a CUDA graph on `stream` (after two eager warm-up calls); returns the graph's replay. A
+    replay launches the kernel as the forward's graph does, so CUDA events around it time the kernel, not the host's
+    argument checks and tensor-map encoding that precede an eager launch."""
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            run()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run()
+    return graph.replay
+
+
 def gemm_roofline(torch, stream) -> dict:
     """The dominant kernel, the int8 tensor-core GEMM, timed alone at the forward's shapes (M = 256 x 70 tokens, the
-    launches of profile_target.GEMMS with their counts per forward) with CUDA events on its stream, L2 flushed before
-    each launch: algorithmic int8 ops per launch / mean launch time, against the int8 dense peak."""
+    launches of profile_target.GEMMS with their counts per forward): each recorded in a CUDA graph and replayed between
+    CUDA events on its stream, L2 flushed before each replay: algorithmic int8 ops per launch / mean launch time,
+    against the int8 dense peak."""
     from chess_transformer_b200 import ops
     from chess_transformer_b200.profile_target import GEMMS, gemm_runner
     M = BATCH * 70
@@ -263,7 +277,7 @@ def gemm_roofline(torch, stream) -> dict:
         for name, (N, K, kind, count) in GEMMS.items():
             if kind == "fp16" or count == 0:
                 continue
-            run = gemm_runner(torch, ops, name, M)
+            run = graphed(torch, stream, gemm_runner(torch, ops, name, M))
             for _ in range(3):
                 run()
             times = []
@@ -284,7 +298,9 @@ def gemm_roofline(torch, stream) -> dict:
 
 
 def timed_launches(torch, stream, flush, run, repeats: int = 10) -> float:
-    """Mean seconds of run() on `stream` by CUDA events, after 3 untimed launches, L2 flushed before each timed one."""
+    """Mean seconds of run() on `stream` by CUDA events (replays of a CUDA graph of it), after 3 untimed launches, L2
+    flushed before each timed one."""
+    run = graphed(torch, stream, run)
     with torch.cuda.stream(stream):
         for _ in range(3):
             run()

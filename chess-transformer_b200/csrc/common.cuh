@@ -150,6 +150,11 @@ FRY_DEVICE void tma_store_2d(const CUtensorMap* map, const void* src, int x, int
 FRY_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // every bulk async-group of this thread has finished reading its shared memory
 FRY_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// waits until at most N of this thread's committed bulk groups have not yet read their shared-memory sources
+template <int N>
+FRY_DEVICE void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 // every bulk async-group of this thread has completed
 FRY_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // orders this thread's shared-memory accesses before later async-proxy (TMA) accesses

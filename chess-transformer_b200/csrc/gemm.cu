@@ -16,8 +16,8 @@
 // fp16 outputs leave through shared memory, a sub-tile of SUB columns at a time: staged as 64-column boxes of 128 rows x
 // 128 bytes in the 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8), so the 32 rows of a warp's store spread
 // over all banks), which warp 18 writes to global memory with TMA stores; no thread stores a row of its own. The row
-// operands (residual, original) arrive the same way, as TMA loads of the same boxes that warp 18 issues a sub-tile ahead
-// into the other of two slots, and each output overwrites its residual in the slot. A tile's column operands (weight
+// operands (residual, original) arrive the same way, as TMA loads of the same boxes that warp 18 issues two sub-tiles
+// ahead into one of three slots, and each output overwrites its residual in the slot. A tile's column operands (weight
 // scales, bias) are staged one tile ahead in shared memory too, so one barrier a sub-tile suffices.
 //
 // Normed A (NKS > 0): the int8 A operand is not loaded but made in the prologue of each 128-row block: the epilogue warps
@@ -85,10 +85,11 @@ struct GemmShape {
     static_assert(!kStaged || (SUB % kBoxCols == 0 && BN % SUB == 0), "a staged sub-tile is whole 64-column boxes");
     static_assert(kStaged || SUB == BN, "unstaged epilogues take the tile whole");
     // one slot holds a sub-tile's row operands (the output overwrites the first) or, without row operands, its output;
-    // there are two, so the next sub-tile's operands load, and the last one's stores drain, while one is worked on
+    // there are three, so while one is worked on, the next sub-tiles' row operands load two ahead, or (without row
+    // operands) the last sub-tile's stores keep reading their slot through the next sub-tile. The normed A and the norm
+    // epilogue keep two, which leaves their larger shared-memory residents their pipeline stages.
     static constexpr int kSlotBytes = kStaged ? (kRowTensors > 1 ? kRowTensors : 1) * kBoxes * kBoxBytes : 0;
-    // the mix's two row operands a sub-tile take three slots, so their loads run two sub-tiles ahead of the one staged
-    static constexpr int kSlots = mixes(EPI) ? 3 : 2;
+    static constexpr int kSlots = (NKS > 0 || EPI == kEpiLinearNorm) ? 2 : 3;
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
     // (the mix and residual epilogues use the scales alone, the fp16 linears the bias alone: one array)
@@ -540,7 +541,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == kStoreWarp) {
         // the staged sub-tiles' TMA traffic: after sub-tile j's barrier, its stores from slot j % kSlots; once they have
         // read the slot, the row operands of sub-tile j + kSlots into it (those of the first kSlots sub-tiles first).
-        // Waiting for the reads before the next barrier also frees the slot for sub-tile j + kSlots's outputs.
+        // Sub-tile j + kSlots is staged into the slot after barrier j + kSlots - 1, which this warp reaches only once the
+        // reads are done: with row operands it waits for them here, before loading the rows; without, it waits for all
+        // but the last kSlots - 2 groups, so sub-tile j's stores keep reading while the next kSlots - 2 sub-tiles stage.
         if constexpr (S::kStaged) {
             const bool has_rows = S::kRowTensors > 0 && (!linear16(EPI) || args.residual != nullptr);
             const bool issuer = lane == 0;
@@ -567,7 +570,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
                             tma_store_2d(&map_out, staged + b * kBoxBytes, n0 + b * kBoxCols, m0);
                         bulk_commit();
-                        bulk_wait_read_all();
+                        if (has_rows) bulk_wait_read_all();
+                        else bulk_wait_read<S::kSlots - 2>();
                     }
                     load_rows(ahead_tile, ahead_sub, slot);
                     advance(ahead_tile, ahead_sub);
@@ -816,8 +820,10 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 }  // namespace
 
 // Tile widths: one N = 256 MMA a K step where N allows (gate_up's 128 columns hold 256 accumulators, its gate and its
-// up), staged in 128-column sub-tiles. Mixing stages 64-column sub-tiles (two row operands a slot) and, in place of 256,
-// takes 192-column tiles, whose 40 KB stages fit four deep beside its 64 KB of slots (three at 256). When that leaves fewer tiles
+// up), staged in 64-column sub-tiles in three slots (16 KB each, so three 48 KB pipeline stages still fit: against two
+// 32 KB slots of 128-column sub-tiles, 1.5-3% faster launches, the stores reading one slot while the next is staged).
+// Mixing (two row operands a slot) takes, in place of 256, 192-column tiles, whose 40 KB stages fit four deep beside
+// its 96 KB of slots (three at 256). When that leaves fewer tiles
 // than SMs (small batches), narrower tiles (128, then 64 columns: more CTAs streaming the weights, deeper pipelines)
 // take their place. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
@@ -847,15 +853,15 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
     if (kind == 0) {
         switch (epilogue) {
             case kEpiBias:
-                if (width == 256) return launch<0, 256, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
-                if (width == 128) return launch<0, 128, false, kEpiBias, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
             case kEpiGated:
-                if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated>(a, b, args, M, N, K, stream, error);
+                if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual:
-                if (width == 256) return launch<0, 256, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
-                if (width == 128) return launch<0, 128, false, kEpiResidual, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
             case kEpiMix:
                 if (width == 256) return launch<0, 192, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
@@ -863,20 +869,20 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 return launch<0, 64, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             case kEpiScaleBf16:
-                if (width == 256) return launch<0, 256, false, kEpiScaleBf16, 128>(a, b, args, M, N, K, stream, error);
-                if (width == 128) return launch<0, 128, false, kEpiScaleBf16, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
             default: break;
         }
     } else {
         switch (epilogue) {
             case kEpiLinearF16:
-                if (width == 256) return launch<1, 256, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
-                if (width == 128) return launch<1, 128, false, kEpiLinearF16, 128>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<1, 256, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<1, 128, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             case kEpiGatedF16:
-                if (width >= 128 || tiles(128) >= multiprocessors) return launch<1, 128, true, kEpiGatedF16>(a, b, args, M, N, K, stream, error);
+                if (width >= 128 || tiles(128) >= multiprocessors) return launch<1, 128, true, kEpiGatedF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, true, kEpiGatedF16>(a, b, args, M, N, K, stream, error);
             case kEpiMixF16:
                 if (width == 256) return launch<1, 192, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
