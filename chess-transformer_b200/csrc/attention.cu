@@ -131,33 +131,44 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     const float dq_reciprocal = 1.0f / static_cast<float>(dq);
     auto mean_of = [&](float sum) { return dq_pow2 ? __fmul_rn(sum, dq_reciprocal) : __fdiv_rn(sum, static_cast<float>(dq)); };
 
-    // normalised keys (zero past dq and past the 70th key), 16-byte loads and stores
-    for (int item = tid; item < kv_here * kAttnKeys; item += blockDim.x) {
+    // values as they are, [kv][key][dv], zero past the 70th key: 16-byte cp.async copies, a thread's all in flight at
+    // once while the keys below are normalised; waited for before the first phase
+    for (int item = tid; item < kv_here * kAttnKeys * (kAttnDv / 8); item += blockDim.x) {
+        const int kv = item / (kAttnKeys * 4), rest = item % (kAttnKeys * 4), key = rest / 4, part = rest % 4;
+        uint16_t* to = values + (kv * kAttnKeys + key) * kValueRow + part * 8;
+        if (key < kAttnTokens) cp_async16(to, board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8);
+        else *reinterpret_cast<uint4*>(to) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
+    // normalised keys (zero past dq and past the 70th key), 16-byte loads and stores; a thread's keys' loads are issued
+    // together, ahead of their arithmetic
+    constexpr int kKeyParts = DQP / 8;
+    auto load_key = [&](int item, uint4 (&raw)[kKeyParts]) {
+        const int kv = item / kAttnKeys, key = item % kAttnKeys;
+        const uint16_t* from = board + key * width + k_offset + (first_kv + kv) * dq;
+#pragma unroll
+        for (int part = 0; part < kKeyParts; ++part)
+            raw[part] = (key < kAttnTokens && part * 8 < dq) ? __ldcs(reinterpret_cast<const uint4*>(from + part * 8)) : make_uint4(0, 0, 0, 0);
+    };
+    auto store_key = [&](int item, const uint4 (&raw)[kKeyParts]) {
         const int kv = item / kAttnKeys, key = item % kAttnKeys;
         float k[DQP];
 #pragma unroll
-        for (int i = 0; i < DQP; ++i) k[i] = 0.0f;
-        float squares = 0.0f;
-        if (key < kAttnTokens) {
-            const uint16_t* from = board + key * width + k_offset + (first_kv + kv) * dq;
+        for (int part = 0; part < kKeyParts; ++part) {
+            const uint32_t words[4] = {raw[part].x, raw[part].y, raw[part].z, raw[part].w};
 #pragma unroll
-            for (int part = 0; part < DQP / 8; ++part)
-                if (part * 8 < dq) {
-                    const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(from + part * 8));
-                    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        k[part * 8 + 2 * w] = low_half(words[w]);
-                        k[part * 8 + 2 * w + 1] = high_half(words[w]);
-                    }
-                }
-#pragma unroll
-            for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
+            for (int w = 0; w < 4; ++w) {
+                k[part * 8 + 2 * w] = low_half(words[w]);
+                k[part * 8 + 2 * w + 1] = high_half(words[w]);
+            }
         }
+        float squares = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
         const float inverse = rsqrtf(__fadd_rn(mean_of(squares), eps));
         uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
 #pragma unroll
-        for (int part = 0; part < DQP / 8; ++part) {
+        for (int part = 0; part < kKeyParts; ++part) {
             uint32_t words[4];
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
@@ -168,18 +179,23 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             }
             *reinterpret_cast<uint4*>(row + part * 8) = make_uint4(words[0], words[1], words[2], words[3]);
         }
-    }
-    // values as they are, [kv][key][dv], zero past the 70th key
-    for (int item = tid; item < kv_here * kAttnKeys * (kAttnDv / 8); item += blockDim.x) {
-        const int kv = item / (kAttnKeys * 4), rest = item % (kAttnKeys * 4), key = rest / 4, part = rest % 4;
-        uint4 raw = make_uint4(0, 0, 0, 0);
-        if (key < kAttnTokens) raw = __ldcs(reinterpret_cast<const uint4*>(board + key * width + v_offset + (first_kv + kv) * kAttnDv + part * 8));
-        *reinterpret_cast<uint4*>(values + (kv * kAttnKeys + key) * kValueRow + part * 8) = raw;
+    };
+    const int key_items = kv_here * kAttnKeys;
+    for (int item = tid; item < key_items; item += 2 * blockDim.x) {
+        const int second = item + blockDim.x;
+        uint4 first_raw[kKeyParts], second_raw[kKeyParts];
+        load_key(item, first_raw);
+        if (second < key_items) load_key(second, second_raw);
+        store_key(item, first_raw);
+        if (second < key_items) store_key(second, second_raw);
     }
     // this CTA's phases: all five, or with a phase split (blockIdx.z, small batches), a share of them
     const int phases = (5 + gridDim.z - 1) / gridDim.z;
     const int phase_begin = blockIdx.z * phases, phase_end = min(5, phase_begin + phases);
-    if (phase_begin >= 5) return;  // uniform across the CTA; the launcher gives every group a phase
+    if (phase_begin >= 5) {  // uniform across the CTA; the launcher gives every group a phase
+        cp_async_wait<0>();    // no copy may still be writing this CTA's shared memory when it leaves
+        return;
+    }
     if (phase_begin < 4) make_bias_slab(bias, board, paired, phase_begin, width, c_offset, first_head, heads_here, warp, warps, g, t);
 
     const int head = first_head + warp;
@@ -197,6 +213,7 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             }
     uint32_t raw_q[KS][2][2];
     load_queries<KS>(raw_q, board, phase_begin * kSlab, width, head, dq, g, t);
+    cp_async_wait<0>();  // this thread's value copies have landed; the barrier makes everyone's visible
     __syncthreads();
 
     const uint64_t scale2 = pair2(scale, scale), log2e2 = pair2(1.4426950408889634f, 1.4426950408889634f);

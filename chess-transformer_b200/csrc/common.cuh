@@ -157,6 +157,15 @@ FRY_DEVICE void bulk_wait_read() {
 }
 // every bulk async-group of this thread has completed
 FRY_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// 16 bytes global -> shared without a register round trip (L2 only), in this thread's current cp.async group
+FRY_DEVICE void cp_async16(void* shared, const void* global) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(shared))), "l"(global)
+                 : "memory");
+}
+FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most PENDING of this thread's cp.async groups are still in flight
+template <int PENDING>
+FRY_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory"); }
 // orders this thread's shared-memory accesses before later async-proxy (TMA) accesses
 FRY_DEVICE void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

@@ -165,13 +165,6 @@ __global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kerne
         }
 }
 
-FRY_DEVICE void cp_async16(void* shared, const void* global) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(shared))), "l"(global)
-                 : "memory");
-}
-FRY_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int PENDING>
-FRY_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory"); }
 
 // One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits. The board's 64 square rows of a
 // (fp32) and y (fp16) stream through shared memory in chunks of kPolicyChunk columns, kPolicyStages deep, by 16-byte cp.async
