@@ -90,6 +90,9 @@ int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_
         const bool mixes_own = i == 0 || n->blocks[i - 1].precision != b.precision;
         const bool mixes_next = i + 1 < n->layers && n->blocks[i + 1].precision == b.precision;
         const int rows_p = projection_rows(n, b.dq);
+        // an int8 block whose query/key heads are 8 or 16 wide has its projection's epilogue apply the attention's q and
+        // k RMSNorm (the same bits as the attention's own), so the attention copies them
+        const bool qk_normed = !fp16 && (b.dq == 8 || b.dq == 16) && (n->heads * b.dq) % 16 == 0 && ((n->heads + n->kv_heads) * b.dq) % 16 == 0;
         fry::GemmArgs projection;
         projection.bias = b.projection_bias;
         projection.out = projected;
@@ -111,11 +114,19 @@ int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_
             if (status != cudaSuccess) return check(status, where + " ln1");
             projection.x_scale = scale;
             projection.w_scale = b.projection_scale;
-            status = fry::gemm(0, fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
+            if (qk_normed) {
+                projection.q_gain = b.q_gain;
+                projection.k_gain = b.k_gain;
+                projection.qk_dq = b.dq;
+                projection.qk_queries = n->heads * b.dq;
+                projection.qk_keys = (n->heads + n->kv_heads) * b.dq;
+                projection.norm_eps = n->eps;
+            }
+            status = fry::gemm(0, qk_normed ? fry::kEpiBiasQkNorm : fry::kEpiBias, q, b.projection, projection, M, rows_p, D, s, &detail);
         }
         if (status != cudaSuccess) return check(status, where + " projection", detail);
         status = fry::template_attention(projected, n->templates, b.q_gain, b.k_gain, attended, B, n->heads, n->kv_heads, b.dq, n->dv,
-                                         n->templates_count, n->eps, s, &detail);
+                                         n->templates_count, n->eps, s, &detail, qk_normed);
         if (status != cudaSuccess) return check(status, where + " attention", detail);
         fry::GemmArgs combine;
         combine.bias = b.combine_heads_bias;
@@ -325,6 +336,43 @@ int fry_template_attention(const uint16_t* projected, const uint16_t* paired_tem
     return check(fry::template_attention(projected, paired_templates, q_gain, k_gain, out, B, heads, kv_heads, dq, dv, templates_count, eps,
                                          as_stream(stream), &detail),
                  "fry_template_attention", detail);
+}
+
+int fry_int8_linear_qk_norm(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
+                            const uint16_t* q_gain, const uint16_t* k_gain, float eps, uint16_t* out, int M, int N, int K, int heads,
+                            int kv_heads, int dq, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0 || (dq != 8 && dq != 16) || heads <= 0 || kv_heads <= 0 ||
+        (heads * dq) % 16 != 0 || ((heads + kv_heads) * dq) % 16 != 0 || (heads + kv_heads) * dq > N)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm takes query/key heads 8 or 16 wide whose blocks start on 16-column boundaries "
+                                     "within N (a multiple of 8), K a multiple of 16");
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out)) return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm needs 16-byte aligned x, weight and out");
+    if (!x_scale || !weight_scale || !q_gain || !k_gain) return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm needs both scales and both gains");
+    if (M == 0) return check(cudaSuccess, "");
+    fry::GemmArgs args;
+    args.x_scale = x_scale;
+    args.w_scale = weight_scale;
+    args.bias = bias;
+    args.out = out;
+    args.q_gain = q_gain;
+    args.k_gain = k_gain;
+    args.qk_dq = dq;
+    args.qk_queries = heads * dq;
+    args.qk_keys = (heads + kv_heads) * dq;
+    args.norm_eps = eps;
+    std::string detail;
+    return check(fry::gemm(0, fry::kEpiBiasQkNorm, x, weight, args, M, N, K, as_stream(stream), &detail), "fry_int8_linear_qk_norm", detail);
+}
+
+int fry_template_attention_normed(const uint16_t* projected, const uint16_t* paired_templates, uint16_t* out, int B, int heads, int kv_heads,
+                                  int dq, int dv, int templates_count, void* stream) {
+    if (B < 0) return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed takes B >= 0");
+    if (dq != 8 && dq != 16) return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed takes dq 8 or 16");
+    if (!aligned16(projected) || !aligned16(out) || !aligned16(paired_templates))
+        return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed needs 16-byte aligned projections, templates and outputs");
+    std::string detail;
+    return check(fry::template_attention(projected, paired_templates, nullptr, nullptr, out, B, heads, kv_heads, dq, dv, templates_count, 0.0f,
+                                         as_stream(stream), &detail, true),
+                 "fry_template_attention_normed", detail);
 }
 
 int fry_linear(const uint16_t* x, const uint16_t* weight, const void* bias, const uint16_t* residual, void* out, int M, int N, int K,

@@ -107,7 +107,9 @@ FRY_DEVICE void load_queries(uint32_t (&raw)[KS][2][2], const uint16_t* board, i
 // DQP: dq padded to the MMA depth (16 or 32). Shared: keys [kv][80][DQP + 8], values [kv][80][40], one bias slab (at most
 // 70 KB). Two CTAs an SM, with up to 128 registers a thread: three (80 registers, some spilled) measured the same at 256
 // boards and 3-6% slower at 8, 16 and 192.
-template <int DQP>
+// NORMED: the projected rows' query and key columns are already RMS-normalised with their gains (the projection GEMM's
+// kEpiBiasQkNorm epilogue did it, to the same bits), so keys are copied and queries used as they are.
+template <int DQP, bool NORMED>
 __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     attention_kernel(const uint16_t* __restrict__ projected, const uint16_t* __restrict__ paired, const uint16_t* __restrict__ q_gain,
                      const uint16_t* __restrict__ k_gain, uint16_t* __restrict__ out, int heads, int kv_heads, int dq, float eps, float scale) {
@@ -152,6 +154,11 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     };
     auto store_key = [&](int item, const uint4 (&raw)[kKeyParts]) {
         const int kv = item / kAttnKeys, key = item % kAttnKeys;
+        if constexpr (NORMED) {  // zero past dq and past the 70th key, as loaded
+#pragma unroll
+            for (int part = 0; part < kKeyParts; ++part) *reinterpret_cast<uint4*>(keys + (kv * kAttnKeys + key) * KROW + part * 8) = raw[part];
+            return;
+        }
         float k[DQP];
 #pragma unroll
         for (int part = 0; part < kKeyParts; ++part) {
@@ -234,6 +241,13 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
             if (!SQUARES && r == 1) {
 #pragma unroll
                 for (int ks = 0; ks < KS; ++ks) a[ks][1] = a[ks][3] = 0u;
+                continue;
+            }
+            if constexpr (NORMED) {
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) a[ks][r + 2 * half] = raw_q[ks][r][half];
                 continue;
             }
             float squares = 0.0f;
@@ -363,7 +377,7 @@ cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStre
 
 cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
-                               cudaStream_t stream, std::string* error) {
+                               cudaStream_t stream, std::string* error, bool qk_normed) {
     if (B <= 0) return cudaSuccess;
     const int group = kv_heads > 0 ? heads / kv_heads : 0;
     const int per_cta = heads < kMaxHeadsPerCta ? heads : kMaxHeadsPerCta;
@@ -391,18 +405,18 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
-    if (dqp == 16) {
-        const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<16>), static_cast<int>(bytes));
-        if (attribute != cudaSuccess) return attribute;
-        return launch_dependent(attention_kernel<16>, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads,
-                                kv_heads, dq, eps, scale);
-    } else {
-        const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(attention_kernel<32>), static_cast<int>(bytes));
-        if (attribute != cudaSuccess) return attribute;
-        return launch_dependent(attention_kernel<32>, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads,
-                                kv_heads, dq, eps, scale);
+    if (qk_normed && dqp != 16) {
+        if (error) *error = "template attention takes normalised queries and keys for dq up to 16 only";
+        return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
+    auto run = [&](auto kernel) {
+        const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(bytes));
+        if (attribute != cudaSuccess) return attribute;
+        return launch_dependent(kernel, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps,
+                                scale);
+    };
+    if (qk_normed) return run(attention_kernel<16, true>);
+    return dqp == 16 ? run(attention_kernel<16, false>) : run(attention_kernel<32, false>);
 }
 
 }  // namespace fry

@@ -58,7 +58,9 @@ __host__ __device__ constexpr bool linear16(int epi) { return epi == kEpiLinearF
 // epilogues that mix the next block's input (residual and original row operands)
 __host__ __device__ constexpr bool mixes(int epi) { return epi == kEpiMix || epi == kEpiMixF16; }
 // int8 epilogues that scale the sums by the row's activation scale and the column's weight scale
-__host__ __device__ constexpr bool scaled(int epi) { return epi <= kEpiMix || epi == kEpiScaleBf16; }
+__host__ __device__ constexpr bool scaled(int epi) { return epi <= kEpiMix || epi == kEpiScaleBf16 || epi == kEpiBiasQkNorm; }
+// the bias epilogue, with or without the q/k norm after it
+__host__ __device__ constexpr bool biased(int epi) { return epi == kEpiBias || epi == kEpiBiasQkNorm; }
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
@@ -93,12 +95,13 @@ struct GemmShape {
     static constexpr int kIoBytes = kSlots * kSlotBytes;
     // the tile's column operands, double-buffered by tile: [2][2][BN] floats (weight scales; up's scales or the bias)
     // (the mix and residual epilogues use the scales alone, the fp16 linears the bias alone: one array)
-    static constexpr int kColumnArrays = (EPI == kEpiBias || EPI == kEpiGated || EPI == kEpiLinearNorm) ? 2 : 1;
+    // (the q/k norm epilogue a third: each column's gain, 0 past the key columns)
+    static constexpr int kColumnArrays = EPI == kEpiBiasQkNorm ? 3 : (biased(EPI) || EPI == kEpiGated || EPI == kEpiLinearNorm) ? 2 : 1;
     // kEpiLinearNorm: the cluster's exchange of row partials [2 tiles][kMaxCluster ranks][128 rows][2] and the epilogue
     // warps' own [2][4 parts][128 rows], floats
     static constexpr int kNormBytes = EPI == kEpiLinearNorm ? (2 * kMaxCluster * kBlockM * 2 + 2 * 4 * kBlockM) * 4 : 0;
     static_assert(EPI != kEpiLinearNorm || (KIND == 1 && SUB == 128), "the norm epilogue keeps 4 chunks a thread (fp16 linear, 128-column sub-tiles)");
-    static constexpr int kSecond = kColumnArrays == 2 ? BN : 0;  // where the second operand (up's scales, the bias) starts
+    static constexpr int kSecond = kColumnArrays >= 2 ? BN : 0;  // where the second operand (up's scales, the bias) starts
     static constexpr int kColumnBytes = 2 * kColumnArrays * BN * 4;
     static constexpr int kStagesFit = (kSmemBudget - kResidentBytes - kRowScaleBytes - kIoBytes - kColumnBytes - kNormBytes) / kStageBytes;
     static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
@@ -125,12 +128,18 @@ FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, 
         float scale = 0.0f, second = 0.0f;
         if constexpr (scaled(EPI)) scale = ok ? p.w_scale[n] : 0.0f;
         if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
-        if constexpr (EPI == kEpiBias || linear16(EPI) || EPI == kEpiGatedF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
+        if constexpr (biased(EPI) || linear16(EPI) || EPI == kEpiGatedF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
         if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
         if constexpr (scaled(EPI)) columns[i] = scale;
         if constexpr (EPI == kEpiLinearNorm) columns[i] = (ok && p.norm_gain) ? h2f_bits(p.norm_gain[n]) : 0.0f;
-        if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32 || EPI == kEpiGatedF16)
+        if constexpr (biased(EPI) || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32 || EPI == kEpiGatedF16)
             columns[SECOND + i] = second;
+        if constexpr (EPI == kEpiBiasQkNorm) {
+            float gain = 0.0f;
+            if (n < p.qk_queries) gain = h2f_bits(p.q_gain[n % p.qk_dq]);
+            else if (n < p.qk_keys) gain = h2f_bits(p.k_gain[(n - p.qk_queries) % p.qk_dq]);
+            columns[2 * BN + i] = gain;
+        }
     }
 }
 
@@ -158,6 +167,58 @@ struct StagedChunk {
     FRY_DEVICE uint4* at(int h) const { return reinterpret_cast<uint4*>(row + (((unit + h) ^ swizzle) << 4)); }
 };
 
+// kEpiBiasQkNorm: the attention's q/k RMSNorm on one row's 16 fp16 outputs (as pairs) from output column `column`,
+// where they are query or key columns: each head's dq values x (the rounded projection) become fp16((x * inverse) *
+// gain), inverse = rsqrt(mean(x^2) + eps). The sums of squares follow the attention kernel's own orders, so the result
+// equals what it computes from the unnormalised rows bit for bit: a key's squares in column order; a query's as four
+// partial sums (a quad lane's columns 2t, 2t + 1, then 8 + 2t, 9 + 2t) added as (s0 + s1) + (s2 + s3). A head's
+// columns lie within the chunk (dq 8 or 16, and the query and key blocks start on 16-column boundaries).
+template <int DQ>
+FRY_DEVICE void normalize_qk_heads(const GemmArgs& p, bool key, const float* gains, uint32_t (&result)[8]) {
+    float gain[16], x[16], y[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 four = reinterpret_cast<const float4*>(gains)[q];
+        gain[4 * q] = four.x, gain[4 * q + 1] = four.y, gain[4 * q + 2] = four.z, gain[4 * q + 3] = four.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        x[2 * i] = h2f_exact(static_cast<uint16_t>(result[i] & 0xffff));
+        x[2 * i + 1] = h2f_exact(static_cast<uint16_t>(result[i] >> 16));
+    }
+    constexpr float kReciprocal = 1.0f / DQ;  // exact: the mean as the attention takes it
+#pragma unroll
+    for (int first = 0; first < 16; first += DQ) {
+        float squares = 0.0f;
+        if (key) {
+#pragma unroll
+            for (int i = 0; i < DQ; ++i) squares = __fmaf_rn(x[first + i], x[first + i], squares);
+        } else {
+            float s[4];
+#pragma unroll
+            for (int lane = 0; lane < 4; ++lane) {
+                s[lane] = __fmaf_rn(x[first + 2 * lane + 1], x[first + 2 * lane + 1], __fmaf_rn(x[first + 2 * lane], x[first + 2 * lane], 0.0f));
+                if constexpr (DQ == 16)
+                    s[lane] = __fmaf_rn(x[first + 9 + 2 * lane], x[first + 9 + 2 * lane], __fmaf_rn(x[first + 8 + 2 * lane], x[first + 8 + 2 * lane], s[lane]));
+            }
+            squares = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
+        }
+        const float inverse = rsqrtf(__fadd_rn(__fmul_rn(squares, kReciprocal), p.norm_eps));
+#pragma unroll
+        for (int i = 0; i < DQ; ++i) y[first + i] = __fmul_rn(__fmul_rn(x[first + i], inverse), gain[first + i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) result[i] = pack_half2_rn(y[2 * i], y[2 * i + 1]);
+}
+
+// gains: the chunk's 16 column gains in shared memory (staged with the tile's column operands)
+FRY_DEVICE void normalize_qk(const GemmArgs& p, int column, const float* gains, uint32_t (&result)[8]) {
+    if (column >= p.qk_keys) return;
+    const bool key = column >= p.qk_queries;
+    if (p.qk_dq == 8) normalize_qk_heads<8>(p, key, gains, result);
+    else normalize_qk_heads<16>(p, key, gains, result);
+}
+
 // Applies the epilogue to one row's 16 consecutive columns. acc (and up, gated) hold the raw TMEM words, xs the row's
 // activation scale, rs and is the next block's input-mix scales, scale and second the chunk's column operands in shared
 // memory. Staged epilogues read the row's residual (and original) from its staged chunk and write the fp16 results over
@@ -165,7 +226,7 @@ struct StagedChunk {
 template <int EPI>
 FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, const uint32_t (&acc)[16], const uint32_t (&up)[16],
                            const float* scale, const float* second, const StagedChunk& staged, const StagedChunk& original, size_t row,
-                           int valid, uint32_t (&result)[8]) {
+                           int valid, int column, const float* gains, uint32_t (&result)[8]) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -201,7 +262,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                 const float4 a = reinterpret_cast<const float4*>(scale)[q];
                 scale_v[4 * q] = a.x, scale_v[4 * q + 1] = a.y, scale_v[4 * q + 2] = a.z, scale_v[4 * q + 3] = a.w;
             }
-            if constexpr (EPI == kEpiBias || EPI == kEpiGated || linear16(EPI) || EPI == kEpiGatedF16) {
+            if constexpr (biased(EPI) || EPI == kEpiGated || linear16(EPI) || EPI == kEpiGatedF16) {
                 const float4 b = reinterpret_cast<const float4*>(second)[q];
                 second_v[4 * q] = b.x, second_v[4 * q + 1] = b.y, second_v[4 * q + 2] = b.z, second_v[4 * q + 3] = b.w;
             }
@@ -218,7 +279,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
                                       ? pair2(static_cast<float>(static_cast<int32_t>(acc[e])), static_cast<float>(static_cast<int32_t>(acc[e + 1])))
                                       : pair2(__uint_as_float(acc[e]), __uint_as_float(acc[e + 1]));
             uint64_t value2;
-            if constexpr (EPI == kEpiBias) {
+            if constexpr (biased(EPI)) {
                 value2 = fma2(mul2(acc2, xs2), scale2, second2);
             } else if constexpr (EPI == kEpiScaleBf16) {
                 value2 = mul2(mul2(acc2, xs2), scale2);
@@ -259,6 +320,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             result[i] = EPI == kEpiScaleBf16 ? pack_bf162_rn(values[2 * i], values[2 * i + 1]) : pack_half2_rn(values[2 * i], values[2 * i + 1]);
+        if constexpr (EPI == kEpiBiasQkNorm) normalize_qk(p, column, gains, result);
         *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
         *staged.at(1) = make_uint4(result[4], result[5], result[6], result[7]);
     }
@@ -665,7 +727,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         uint32_t result[8];
                         if (S::kStaged || m < M)
                             epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + S::kSecond + c, staged, original,
-                                            static_cast<size_t>(m) * N + n0 + c, valid, result);
+                                            static_cast<size_t>(m) * N + n0 + c, valid, n0 + c, columns + 2 * BN + c, result);
                         if constexpr (EPI == kEpiLinearNorm) {
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
@@ -860,6 +922,17 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 256) return launch<0, 256, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
+            case kEpiBiasQkNorm:
+                if ((args.qk_dq != 8 && args.qk_dq != 16) || args.qk_queries % 16 || args.qk_keys % 16 || args.qk_keys > N || !args.q_gain ||
+                    !args.k_gain) {
+                    if (error) *error = "the q/k norm epilogue takes heads 8 or 16 wide in blocks starting on 16-column boundaries, and both gains";
+                    return cudaErrorInvalidValue;
+                }
+                if (width == 256 && (N + 191) / 192 * 192 < (N + 255) / 256 * 256)
+                    return launch<0, 192, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 128) return launch<0, 128, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
+                return launch<0, 64, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
             case kEpiGated:
                 if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);

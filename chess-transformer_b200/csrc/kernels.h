@@ -24,6 +24,7 @@ enum GemmEpilogue : int {
     kEpiGatedF16 = 8,   // fp16: fp16((g * sigmoid(g)) * u), weight rows = gate rows then up rows
     kEpiMixF16 = 9,     // fp16: (acc + bias) + residual rounded to fp16, then fp16(fma(stream, rs, original * is))
     kEpiScaleBf16 = 10, // int8: bf16((acc * xs) * ws), the scaled GEMM of the isolated-kernel benchmark (no reference op)
+    kEpiBiasQkNorm = 11,// int8: kEpiBias, then the attention's q and k RMSNorm with gains on the query and key columns (qk_*)
 };
 
 struct GemmArgs {
@@ -47,6 +48,11 @@ struct GemmArgs {
     // kEpiLinearNorm: the int8 rows [M, N] and their scales [M] of norm_quant(out) with norm_gain and norm_eps
     int8_t* norm_q = nullptr;
     float* norm_scale = nullptr;
+    // kEpiBiasQkNorm: columns [0, qk_queries) are query heads and [qk_queries, qk_keys) key heads, qk_dq (8 or 16) wide,
+    // each RMS-normalised (eps norm_eps) and scaled by q_gain / k_gain [qk_dq] after the fp16 rounding
+    const uint16_t* q_gain = nullptr;
+    const uint16_t* k_gain = nullptr;
+    int qk_dq = 0, qk_queries = 0, qk_keys = 0;
 };
 
 // kind 0: int8 A [M, K], B [N, K] (gated: [2N, K]); kind 1: fp16 A [M, K], B [N, K].
@@ -76,9 +82,10 @@ cudaError_t square_feature_rows(const int64_t* boards, int32_t* rows, int B, cud
 // Template attention (attention.cu).
 // paired [64][64][8] fp16: templates[t][i][j] at paired[i][j][t]
 cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream);
+// qk_normed: the projected rows' query and key columns are already normalised with their gains (kEpiBiasQkNorm; dq <= 16)
 cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
-                               cudaStream_t stream, std::string* error);
+                               cudaStream_t stream, std::string* error, bool qk_normed = false);
 
 // Attention over 64-token sequences with 64-wide heads, bf16 (attention64.cu): q, k, v, out [B, 64, heads * 64].
 cudaError_t attention64(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int B, int heads, cudaStream_t stream,

@@ -63,6 +63,8 @@ SIGNATURES = {
     "fry_rotate_quant": ([_ptr] * 3 + [_c_int] * 3 + [_ptr], _c_int),
     "fry_pair_templates": ([_ptr, _ptr, _c_int, _ptr], _c_int),
     "fry_template_attention": ([_ptr] * 5 + [_c_int] * 6 + [_c_float, _ptr], _c_int),
+    "fry_int8_linear_qk_norm": ([_ptr] * 7 + [_c_float, _ptr] + [_c_int] * 6 + [_ptr], _c_int),
+    "fry_template_attention_normed": ([_ptr] * 3 + [_c_int] * 6 + [_ptr], _c_int),
     "fry_linear": ([_ptr] * 5 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_linear_full": ([_ptr] * 8 + [_c_int] * 4 + [_ptr], _c_int),
     "fry_linear_norm_quant": ([_ptr] * 6 + [_c_float] + [_ptr] * 2 + [_c_int] * 3 + [_ptr], _c_int),

@@ -119,6 +119,21 @@ int fry_pair_templates(const uint16_t* templates, uint16_t* paired, int template
 int fry_template_attention(const uint16_t* projected, const uint16_t* paired_templates, const uint16_t* q_gain, const uint16_t* k_gain,
                            uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps, void* stream);
 
+/* `chess::int8_linear` for the projection (model/int8_blocks.py:132-139, bias epilogue) with the next op's q and k
+ * RMSNorm (`template_attention`'s q_norm and k_norm with their gains, model/fused_blocks.py:54-97) in its epilogue:
+ * out[M, N] fp16 is fry_int8_linear's output with columns [0, heads*dq) (queries) and [heads*dq, (heads+kv_heads)*dq)
+ * (keys) replaced, head by head, by fp16((x * inverse) * gain), inverse = rsqrt(mean(x^2) + eps), summed in the order
+ * fry_template_attention sums them, so fry_template_attention_normed on it equals fry_template_attention on the plain
+ * projection bit for bit. dq 8 or 16, the query and key blocks on 16-column boundaries. */
+int fry_int8_linear_qk_norm(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
+                            const uint16_t* q_gain, const uint16_t* k_gain, float eps, uint16_t* out, int M, int N, int K, int heads,
+                            int kv_heads, int dq, void* stream);
+
+/* fry_template_attention on a projection whose query and key columns fry_int8_linear_qk_norm has normalised: the
+ * queries and keys are used as they are. dq 8 or 16; otherwise as fry_template_attention. */
+int fry_template_attention_normed(const uint16_t* projected, const uint16_t* paired_templates, uint16_t* out, int B, int heads, int kv_heads,
+                                  int dq, int dv, int templates_count, void* stream);
+
 /* `chess::linear` (model/fused_blocks.py:308-313, kernel :229-304) for fp16 inputs: out[M, N] = (x[M, K] . weight^T + bias)
  * + residual, fp32 accumulation, fp16 out (out_fp32 == 0) or fp32 out without residual (out_fp32 != 0, the reference's
  * accumulate_fp32). weight is [N, K] fp16 (the reference stores it transposed, [K, N]). bias fp16 [N] (fp32 [N] when

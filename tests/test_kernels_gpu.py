@@ -348,3 +348,41 @@ def test_heads_are_the_oracles(boards):
     difference = (found[:, :-1] - expected[:, :-1]).abs()
     assert difference.max() <= 2e-3 and difference.median() <= 1e-5
     assert torch.allclose(found[:, -1], expected[:, -1], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("dq", [8, 16])
+@pytest.mark.parametrize("boards", [1, 5, 64, 256])
+def test_the_q_k_norm_in_the_projection_epilogue_gives_the_attentions_own_bits(dq, boards):
+    # the forward's fused pair for dq 8 and 16 (fry_int8_linear_qk_norm, then fry_template_attention_normed) against the
+    # plain pair (fry_int8_linear, then fry_template_attention, which normalises queries and keys itself), at Fry's
+    # geometry: the value and template-mix columns and the attention's output are the same bits
+    import ctypes
+    from chess_transformer_b200.library import library
+    lib = library()
+    heads, kv_heads, dv, templates_count, D = 24, 12, 32, 8, 768
+    N, M = (heads + kv_heads) * dq + kv_heads * dv + heads * templates_count, boards * 70
+    generator = torch.Generator().manual_seed(dq * 1000 + boards)
+    x = torch.randint(-127, 128, (M, D), generator=generator, dtype=torch.int8).cuda()
+    weight = torch.randint(-127, 128, (N, D), generator=generator, dtype=torch.int8).cuda()
+    x_scale = (torch.rand(M, generator=generator) / 100 + 1e-3).cuda()
+    weight_scale = (torch.rand(N, generator=generator) / 100 + 1e-3).cuda()
+    bias = torch.randn(N, generator=generator).half().cuda()
+    q_gain, k_gain = (1 + torch.randn(2, dq, generator=generator) / 10).half().cuda()
+    paired = ops.pair_templates((torch.randn(8, 64, 64, generator=generator) / 2).half().cuda())
+    plain = ops.int8_linear(x, x_scale, weight, weight_scale, bias, None, False, "projection")
+    fused = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    pointer = lambda t: ctypes.c_void_p(t.data_ptr())
+    lib.fry_int8_linear_qk_norm(pointer(x), pointer(x_scale), pointer(weight), pointer(weight_scale), pointer(bias), pointer(q_gain),
+                                pointer(k_gain), 1e-5, pointer(fused), M, N, D, heads, kv_heads, dq, stream)
+    qk = (heads + kv_heads) * dq
+    assert torch.equal(fused[:, qk:], plain[:, qk:])
+    assert not torch.equal(fused[:, :qk], plain[:, :qk])
+    expected = torch.empty(boards, 70, heads * dv, dtype=torch.float16, device="cuda")
+    found = torch.empty_like(expected)
+    lib.fry_template_attention(pointer(plain), pointer(paired), pointer(q_gain), pointer(k_gain), pointer(expected), boards, heads, kv_heads,
+                               dq, dv, templates_count, 1e-5, stream)
+    lib.fry_template_attention_normed(pointer(fused), pointer(paired), pointer(found), boards, heads, kv_heads, dq, dv, templates_count, stream)
+    torch.cuda.synchronize()
+    assert torch.isfinite(expected).all()
+    assert torch.equal(found, expected)
