@@ -399,9 +399,10 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    // 1, 2, 3 or 5 groups: each has a phase (4 groups of 2 phases would leave the last without one)
+    // 1, 2, 3 or 5 groups: each has a phase (4 groups of 2 phases would leave the last without one). Three groups only
+    // from 4 fit: at 64 boards (3.5 fit) two groups measured 17.8 / 22.0 us a launch (dq 16 / 24) against 18.2 / 23.4
     const int ctas = heads / per_cta * B, fit = 9 * multiprocessors / (2 * ctas);
-    const dim3 grid(heads / per_cta, B, fit >= 5 ? 5 : fit >= 3 ? 3 : fit >= 2 ? 2 : 1);
+    const dim3 grid(heads / per_cta, B, fit >= 5 ? 5 : fit >= 4 ? 3 : fit >= 2 ? 2 : 1);
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
