@@ -15,10 +15,11 @@ from pathlib import Path
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 # the GEMMs of a block at M = batch x 70: name -> (output columns N, depth K, kind), and how many of the 28 blocks run
-# each: the projection at dq 8/16/24, gate_up, down mixing the next block's input (the last block's adds its residual
-# only), and the attention-out fp16 linear; then the GEMMs with the norm in their prologue (kinds "_normed"), which the
-# forward does not run (count 0), for profiling them beside the others
-GEMMS = {"projection864": (864, 768, "bias", 10), "projection1152": (1152, 768, "bias", 9), "projection1440": (1440, 768, "bias", 9),
+# each: the projection at dq 8/16/24 (at dq 8 and 16 with the attention's q/k norm in its epilogue, "bias_qk"), gate_up,
+# down mixing the next block's input (the last block's adds its residual only), and the attention-out fp16 linear; then
+# the GEMMs with the norm in their prologue (kinds "_normed"), which the forward does not run (count 0), for profiling
+# them beside the others
+GEMMS = {"projection864": (864, 768, "bias_qk", 10), "projection1152": (1152, 768, "bias_qk", 9), "projection1440": (1440, 768, "bias", 9),
          "gate_up": (992, 768, "gated", 28), "down": (768, 1024, "mixing", 27), "down_last": (768, 1024, "residual", 1),
          "combine": (768, 768, "fp16", 28), "projection1152_normed": (1152, 768, "bias_normed", 0),
          "gate_up_normed": (992, 768, "gated_normed", 0)}
@@ -47,7 +48,17 @@ def gemm_runner(torch, ops, name: str, M: int):
     x = torch.randint(-127, 128, (M, K), generator=generator, dtype=torch.int8).cuda()
     w = torch.randint(-127, 128, ((2 if gated else 1) * N, K), generator=generator, dtype=torch.int8).cuda()
     xs, ws = (torch.rand(M, generator=generator) / 100).cuda(), (torch.rand(len(w), generator=generator) / 100).cuda()
-    bias = torch.randn(N, generator=generator).half().cuda() if kind == "bias" else None
+    bias = torch.randn(N, generator=generator).half().cuda() if kind.startswith("bias") else None
+    if kind == "bias_qk":  # Fry's projection rows: 24 query heads, 12 key heads of dq = (N - 576) / 36
+        import ctypes
+        from chess_transformer_b200 import library
+        dq = (N - 576) // 36
+        gains = (1 + torch.randn(2, dq, generator=generator) / 10).half().cuda()
+        out = torch.empty(M, N, dtype=torch.half, device="cuda")
+        pointer = lambda tensor: ctypes.c_void_p(tensor.data_ptr())
+        return lambda: library().fry_int8_linear_qk_norm(pointer(x), pointer(xs), pointer(w), pointer(ws), pointer(bias), pointer(gains[0]),
+                                                         pointer(gains[1]), 1e-5, pointer(out), M, N, K, 24, 12, dq,
+                                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     residual = torch.randn(M, N, generator=generator).half().cuda() if kind in ("residual", "mixing") else None
     mix = ()
     if kind == "mixing":
