@@ -219,6 +219,49 @@ FRY_DEVICE void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// ---- CTA pairs (cta_group::2): one MMA of M = 256 rows whose A halves and B halves lie in the shared memory of the two
+// CTAs of a cluster, at the same offsets, and whose accumulator halves lie in each CTA's TMEM (rows 0-127 in the even
+// CTA's, 128-255 in the odd one's). The even CTA issues the MMAs; every tcgen05 instruction of such a kernel is of the
+// pair group. The TMEM allocation is one for the pair: a warp of each CTA allocates (and frees) it together.
+FRY_DEVICE void tmem_alloc_pair(uint32_t* dst_smem, uint32_t columns) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)), "r"(columns)
+                 : "memory");
+}
+FRY_DEVICE void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+FRY_DEVICE void tmem_dealloc_pair(uint32_t addr, uint32_t columns) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(addr), "r"(columns) : "memory");
+}
+template <int KIND>
+FRY_DEVICE void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    if constexpr (KIND == 0) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    }
+}
+// Arrives on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's) once every pair MMA this thread
+// issued before it has completed.
+FRY_DEVICE void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory that completes on an mbarrier of either CTA of the pair (`bar` a
+// shared::cluster address): both CTAs' operand loads complete on the even CTA's stage barrier. Not a multicast.
+FRY_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
 // 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape: lane i of the warp reads TMEM lane base+i).
 FRY_DEVICE void tmem_load32(uint32_t addr, uint32_t (&r)[32]) {
     asm volatile(
@@ -255,13 +298,13 @@ FRY_DEVICE uint64_t smem_desc_sw128(uint32_t smem_byte_addr) {
     return desc;
 }
 
-// Instruction descriptor for a dense MMA with both operands K-major, M = 128 rows:
+// Instruction descriptor for a dense MMA with both operands K-major, M = 128 rows (256 for a CTA pair's):
 // D format [4,6) (1 f32, 2 s32), A format [7,10) and B format [10,13) (kind::i8: 1 signed; kind::f16: 0 f16),
 // N >> 3 at [17,23), M >> 4 at [24,29).
 template <int KIND>
-__host__ __device__ constexpr uint32_t instr_desc(int n) {
+__host__ __device__ constexpr uint32_t instr_desc(int n, int m = 128) {
     return (KIND == 0 ? (2u << 4) | (1u << 7) | (1u << 10) : (1u << 4)) | (static_cast<uint32_t>(n >> 3) << 17) |
-           (static_cast<uint32_t>(128 >> 4) << 24);
+           (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---- programmatic dependent launch ---------------------------------------------------------------------

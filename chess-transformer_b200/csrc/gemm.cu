@@ -24,6 +24,11 @@
 // run norm_quant (rowops.cuh) on the block's fp16 rows straight into NKS resident 128-byte K slices of shared memory,
 // in the layout the MMA reads, and the row scales beside them; the CTA then takes every column tile of the block in turn
 // while only B streams. The norm's output never reaches global memory.
+// CTA pairs (PAIR, the fp16 linear at large M): two CTAs of a cluster share each M = 256 MMA (tcgen05 of the pair
+// group). Each loads its 128 rows of A and half of B's rows into its own shared memory; both CTAs' loads complete on
+// the even CTA's stage barrier; the even CTA's MMA warp issues the pair's MMAs and commits to the stage and accumulator
+// barriers of both CTAs; each CTA's epilogue reads its own TMEM (its 128 rows) and returns the accumulator to the even
+// CTA's barrier. A tile is then 256 rows, and each CTA moves half the B bytes.
 // No TMA load multicasts.
 #include <mutex>
 #include <string>
@@ -64,16 +69,21 @@ __host__ __device__ constexpr bool biased(int epi) { return epi == kEpiBias || e
 
 // SUB: the columns an epilogue sub-tile stages (whole 64-column boxes, dividing BN); a BN-wide accumulator (one MMA of
 // up to N = 256) leaves in BN / SUB sub-tiles, so the staging slots stay small beside the pipeline stages.
-template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS>
+template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS, bool PAIR = false>
 struct GemmShape {
     static constexpr int kElem = KIND == 0 ? 1 : 2;
     static constexpr int kBoxK = kTileKBytes / kElem;
     static constexpr int kABytes = kBlockM * kTileKBytes;
-    static constexpr int kBBytes = BN * kTileKBytes;
+    // PAIR (the two CTAs of a cluster share one M = 256 MMA): each holds half of the MMA's B rows, the gate's or the
+    // up's when gated
+    static constexpr int kBRows = PAIR && !GATED ? BN / 2 : BN;
+    static constexpr int kBBytes = kBRows * kTileKBytes;
     // a normed A is resident (NKS slices), so a stage holds B alone
     static constexpr int kResidentBytes = NKS * kABytes;
     static constexpr int kRowScaleBytes = NKS > 0 ? kBlockM * 4 : 0;
-    static constexpr int kStageBytes = (NKS > 0 ? 0 : kABytes) + kBBytes * (GATED ? 2 : 1);
+    static constexpr int kStageBytes = (NKS > 0 ? 0 : kABytes) + kBBytes * (GATED && !PAIR ? 2 : 1);
+    static_assert(!PAIR || (NKS == 0 && EPI != kEpiLinearNorm && kBRows % 8 == 0),
+                  "a CTA pair loads its A, has no cluster epilogue and holds B halves of whole 8-row swizzle atoms");
     static_assert(NKS == 0 || (KIND == 0 && NKS * kTileKBytes <= 1024 && NKS % 2 == 0), "a normed A is int8, 256 to 1024 columns");
     // fp16 outputs are staged for TMA stores; int32 and fp32 outputs are stored by their threads
     static constexpr bool kStaged = EPI != kEpiInt32 && EPI != kEpiLinearF32;
@@ -435,16 +445,16 @@ FRY_DEVICE void norm_rows_of_tile(const GemmArgs& p, float* norm_smem, uint64_t*
     }
 }
 
-template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS>
+template <int KIND, int BN, bool GATED, int EPI, int SUB, int NKS, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_residual,
                 const __grid_constant__ CUtensorMap map_original, const GemmArgs args, int M, int N, int K) {
-    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem[];
     if (smem_addr(smem) & 1023u) {  // uniform across the CTA: every thread leaves before any barrier
         if (threadIdx.x == 0) record_error(kMisaligned, 20);
-        if constexpr (EPI == kEpiLinearNorm) cluster_sync();  // its peers leave the same way
+        if constexpr (EPI == kEpiLinearNorm || PAIR) cluster_sync();  // its peers leave the same way
         return;
     }
     uint8_t* resident = smem;                                            // a normed A: [NKS][128 rows][128 bytes, swizzled]
@@ -464,17 +474,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = (N + BN - 1) / BN;
-    const int row_blocks = (M + kBlockM - 1) / kBlockM;
+    // PAIR: a tile is the pair's 256 rows, of which this CTA (cluster rank 0 or 1) takes 128 from 128 * rank; the
+    // pairs walk the tiles as single CTAs do
+    constexpr int kTileRows = PAIR ? 2 * kBlockM : kBlockM;
+    const int rank = PAIR ? static_cast<int>(cluster_rank()) : 0;
+    const int workers = PAIR ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+    const int worker = PAIR ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+    const int row_blocks = (M + kTileRows - 1) / kTileRows;
     const int tiles = row_blocks * n_blocks;
+    auto row0 = [&](int tile) { return (tile / n_blocks) * kTileRows + rank * kBlockM; };  // this CTA's first row
     const int k_tiles = (K * S::kElem + kTileKBytes - 1) / kTileKBytes;
     // Tile order (tile = row block * n_blocks + column tile). Plain: round robin over the tiles. Normed A: round robin over
     // units, a unit being a row block's column tiles g, g + groups, ... (groups = gridDim.x / row_blocks, at least 1, the
     // launch's choice), so a CTA makes a unit's A once and reuses it for each of the unit's tiles.
     const int groups = NKS > 0 ? max(1, static_cast<int>(gridDim.x) / row_blocks) : 1;
     auto unit_tile = [&](int unit) { return (unit / groups) * n_blocks + unit % groups; };
-    const int first_tile = NKS > 0 ? unit_tile(blockIdx.x) : static_cast<int>(blockIdx.x);
+    const int first_tile = NKS > 0 ? unit_tile(blockIdx.x) : worker;
     auto next_tile = [&](int tile) {
-        if (NKS == 0) return tile + static_cast<int>(gridDim.x);
+        if (NKS == 0) return tile + workers;
         const int column = tile % n_blocks;
         if (column + groups < n_blocks) return tile + groups;
         const int unit = (tile / n_blocks) * groups + column % groups + static_cast<int>(gridDim.x);
@@ -502,7 +519,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], kEpilogueWarps);
+            mbar_init(&tmem_empty[b], PAIR ? 2 * kEpilogueWarps : kEpilogueWarps);  // PAIR: both CTAs' warps, on the even CTA's
         }
         for (int b = 0; b < S::kSlots; ++b) mbar_init(&rows_full[b], 1);
         mbar_init(a_ready, kEpilogueWarps);
@@ -510,8 +527,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(tmem_slot, S::kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, S::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, S::kTmemCols);
+            tmem_relinquish();
+        }
     }
     if (warp == kProducerWarp && lane == 0) {
         prefetch_tensor_map(&map_a);
@@ -519,20 +541,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if constexpr (EPI == kEpiLinearNorm) cluster_sync();  // every rank's barriers are initialised before any remote arrival
+    if constexpr (EPI == kEpiLinearNorm || PAIR) cluster_sync();  // every rank's barriers are initialised before any remote arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // weights that no earlier kernel writes (args.b_constant): the producer loads B of the first stages (the ring is
     // empty) before waiting for the earlier kernels, so those loads overlap their tail; A follows after the wait, into
     // the same stages, whose barriers expect both
+    // A stage's loads. PAIR: both CTAs' loads (each its A rows and its half of B) complete on the even CTA's stage
+    // barrier, which its producer arms for the pair's bytes; the odd CTA's producer does not arrive
+    auto arm_stage = [&](int s) {
+        if (!PAIR || rank == 0) mbar_arrive_expect_tx(&full[s], (PAIR ? 2 : 1) * S::kStageBytes);
+    };
+    auto load_b = [&](uint8_t* b, int s, int kt, int n0) {
+        if constexpr (PAIR) {
+            const int rows = GATED ? (rank == 0 ? n0 : N + n0) : n0 + rank * S::kBRows;
+            tma_load_2d_pair(b, &map_b, peer_smem(&full[s], 0), kt * S::kBoxK, rows);
+        } else {
+            tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
+            if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
+        }
+    };
+    auto load_a = [&](uint8_t* a, int s, int kt, int m0) {
+        if constexpr (PAIR) tma_load_2d_pair(a, &map_a, peer_smem(&full[s], 0), kt * S::kBoxK, m0);
+        else tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
+    };
     int preloaded = 0;
     if (args.b_constant && warp == kProducerWarp && elect_one()) {
         for (int tile = first_tile, kt = 0; preloaded < S::kStages && tile < tiles; ++preloaded) {
             uint8_t* b = stages + preloaded * S::kStageBytes + (NKS > 0 ? 0 : S::kABytes);
-            const int n0 = column0(tile);
-            mbar_arrive_expect_tx(&full[preloaded], S::kStageBytes);
-            tma_load_2d(b, &map_b, &full[preloaded], kt * S::kBoxK, n0);
-            if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[preloaded], kt * S::kBoxK, N + n0);
+            arm_stage(preloaded);
+            load_b(b, preloaded, kt, column0(tile));
             if (++kt == k_tiles) {
                 kt = 0;
                 tile = next_tile(tile);
@@ -546,36 +584,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int it = 0;
             bool ok = true;
             for (int tile = first_tile; tile < tiles && ok; tile = next_tile(tile)) {
-                const int m0 = (tile / n_blocks) * kBlockM, n0 = column0(tile);
+                const int m0 = row0(tile), n0 = column0(tile);
                 for (int kt = 0; kt < k_tiles; ++kt, ++it) {
                     const int s = it % S::kStages;
                     const uint32_t phase = (it / S::kStages) & 1;
                     uint8_t* a = stages + s * S::kStageBytes;
                     uint8_t* b = NKS > 0 ? a : a + S::kABytes;
                     if (it >= preloaded) {  // a preloaded stage has its barrier armed and its B in flight
-                        if (!mbar_wait(&empty[s], phase ^ 1, 10)) {
+                        // PAIR: the even CTA's MMA warp frees the stage in both CTAs
+                        if (!(PAIR ? mbar_wait_cluster(&empty[s], phase ^ 1, 10) : mbar_wait(&empty[s], phase ^ 1, 10))) {
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-                        tma_load_2d(b, &map_b, &full[s], kt * S::kBoxK, n0);
-                        if constexpr (GATED) tma_load_2d(b + S::kBBytes, &map_b, &full[s], kt * S::kBoxK, N + n0);
+                        arm_stage(s);
+                        load_b(b, s, kt, n0);
                     }
-                    if constexpr (NKS == 0) tma_load_2d(a, &map_a, &full[s], kt * S::kBoxK, m0);
+                    if constexpr (NKS == 0) load_a(a, s, kt, m0);
                 }
             }
         }
     } else if (warp == kMmaWarp) {
-        if (elect_one()) {
+        // PAIR: the even CTA issues the pair's MMAs and frees stages and hands over accumulators in both CTAs
+        auto commit = [&](uint64_t* bar) {
+            if constexpr (PAIR) {
+                mma_commit_pair(smem_addr(bar));
+                mma_commit_pair(peer_smem(bar, 1));
+            } else {
+                mma_commit(bar);
+            }
+        };
+        if ((!PAIR || rank == 0) && elect_one()) {
             // gated: the gate's and the up's B boxes lie back to back, 2 BN rows at the swizzle's 1024 bytes per 8, so one MMA of
             // N = 2 BN fills both accumulator halves
-            constexpr uint32_t idesc = instr_desc<KIND>(S::kAccCols);
+            constexpr uint32_t idesc = instr_desc<KIND>(S::kAccCols, kTileRows);
             int it = 0, local = 0, units = 0;
             bool ok = true;
             for (int tile = first_tile; tile < tiles && ok; tile = next_tile(tile), ++local) {
                 const int buffer = local & 1;
                 if (unit_start(tile) && !mbar_wait(a_ready, (units++) & 1, 16)) break;  // the unit's A is made
-                if (!mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)) break;
+                if (!(PAIR ? mbar_wait_cluster(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)
+                           : mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)))
+                    break;
                 tc_fence_after();
                 const uint32_t accumulator = tmem + buffer * S::kAccCols;
                 for (int kt = 0; kt < k_tiles; ++kt, ++it) {
@@ -593,11 +642,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int k = 0; k < kTileKBytes / kMmaKBytes; ++k) {
                         const uint64_t da = smem_desc_sw128(a + k * kMmaKBytes);
                         const uint32_t accumulate = (kt > 0 || k > 0) ? 1u : 0u;
-                        mma_ss<KIND>(accumulator, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
+                        if constexpr (PAIR) mma_ss_pair<KIND>(accumulator, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
+                        else mma_ss<KIND>(accumulator, da, smem_desc_sw128(b + k * kMmaKBytes), idesc, accumulate);
                     }
-                    mma_commit(&empty[s]);
+                    commit(&empty[s]);
                 }
-                mma_commit(&tmem_full[buffer]);
+                commit(&tmem_full[buffer]);
             }
         }
     } else if (warp == kStoreWarp) {
@@ -612,7 +662,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             auto load_rows = [&](int tile, int sub, int slot) {
                 if (!issuer || !has_rows || tile >= tiles) return;
                 load_sub_rows<EPI, SUB>(&map_residual, &map_original, io + slot * S::kSlotBytes, &rows_full[slot],
-                                        (tile / n_blocks) * kBlockM, column0(tile) + sub * SUB, N);
+                                        row0(tile), column0(tile) + sub * SUB, N);
             };
             int ahead_tile = first_tile, ahead_sub = 0;  // the sub-tile kSlots ahead of the one being stored
             for (int slot = 0; slot < S::kSlots; ++slot) {
@@ -627,7 +677,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     __syncwarp();
                     epilogue_sync();  // sub-tile j is staged
                     if (issuer) {
-                        const int m0 = (tile / n_blocks) * kBlockM, n0 = column0(tile) + sub * SUB;
+                        const int m0 = row0(tile), n0 = column0(tile) + sub * SUB;
                         uint8_t* staged = io + slot * S::kSlotBytes;
                         for (int b = 0; b < S::kBoxes && n0 + b * kBoxCols < N; ++b)
                             tma_store_2d(&map_out, staged + b * kBoxBytes, n0 + b * kBoxCols, m0);
@@ -656,7 +706,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const bool has_rows = S::kRowTensors > 0 && (!linear16(EPI) || args.residual != nullptr);
         auto tile_origin = [&](int tile, int& m0, int& n0) {
-            m0 = (tile / n_blocks) * kBlockM;
+            m0 = row0(tile);
             n0 = column0(tile);
         };
         // a tile's column operands and this thread's row scale are fetched during the tile before (the first tile's here),
@@ -694,7 +744,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             const float xs = NKS > 0 ? xs_unit : xs_next;
-            if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
+            if (alive && !(PAIR ? mbar_wait_cluster(&tmem_full[buffer], (local >> 1) & 1, 13) : mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)))
+                alive = false;
             const float* columns = column_buffers + buffer * S::kColumnArrays * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
             // kEpiLinearNorm: this thread's fp16 outputs (its row, its chunks) and their partial sums for the row's norm:
@@ -744,7 +795,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     // this warp's reads of the accumulator are complete: the MMA warp may fill it again
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&tmem_empty[buffer]);
+                    if (lane == 0) {
+                        if constexpr (PAIR) mbar_arrive_peer(peer_smem(&tmem_empty[buffer], 0));  // the even CTA's MMA warp waits on it
+                        else mbar_arrive(&tmem_empty[buffer]);
+                    }
                     if (next < tiles) fetch_operands(next, buffer ^ 1);
                 }
                 // this thread's staged writes, visible to the async proxy before the stores read them
@@ -758,9 +812,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    // PAIR: neither CTA frees the pair's TMEM, or leaves, before the other is done with it and with the even CTA's barriers
+    if constexpr (PAIR) cluster_sync();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, S::kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, S::kTmemCols);
+        else tmem_dealloc(tmem, S::kTmemCols);
     }
     // no rank leaves while a peer may still write its shared memory or arrive on its barriers
     if constexpr (EPI == kEpiLinearNorm) cluster_sync();
@@ -827,14 +884,14 @@ bool make_box_map(CUtensorMap* map, const void* base, int cols, int rows, std::s
     return true;
 }
 
-template <int KIND, int BN, bool GATED, int EPI, int SUB = BN, int NKS = 0>
+template <int KIND, int BN, bool GATED, int EPI, int SUB = BN, int NKS = 0, bool PAIR = false>
 cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream, std::string* error) {
-    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS>;
-    auto kernel = gemm_kernel<KIND, BN, GATED, EPI, SUB, NKS>;
+    using S = GemmShape<KIND, BN, GATED, EPI, SUB, NKS, PAIR>;
+    auto kernel = gemm_kernel<KIND, BN, GATED, EPI, SUB, NKS, PAIR>;
     const cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), S::kSmemBytes);
     if (attribute != cudaSuccess) return attribute;
     CUtensorMap map_a, map_b, map_out, map_residual, map_original;
-    if (!make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, BN, error)) return cudaErrorInvalidValue;
+    if (!make_map(&map_b, b, S::kElem, K, GATED ? 2 * N : N, S::kBRows, error)) return cudaErrorInvalidValue;
     if (NKS > 0) {
         map_a = map_b;  // a normed A is made in shared memory, not loaded
     } else if (!make_map(&map_a, a, S::kElem, K, M, kBlockM, error)) {
@@ -854,6 +911,20 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
     int grid = tiles < multiprocessors ? tiles : multiprocessors;
+    if constexpr (PAIR) {
+        // CTA pairs, as many as the device holds at once, none without a tile of 256 rows
+        const int pair_tiles = ((M + 2 * kBlockM - 1) / (2 * kBlockM)) * n_blocks;
+        int clusters = 0;
+        status = max_active_clusters(kernel, dim3(kGemmThreads), S::kSmemBytes, 2, &clusters);
+        if (status != cudaSuccess) return status;
+        if (clusters < 1) {
+            if (error) *error = "no CTA pair of this GEMM fits the device";
+            return cudaErrorInvalidValue;
+        }
+        const int pairs = pair_tiles < clusters ? pair_tiles : clusters;
+        return launch_dependent_cluster(kernel, dim3(2 * pairs), dim3(kGemmThreads), S::kSmemBytes, 2, stream, map_a, map_b, map_out,
+                                        map_residual, map_original, args, M, N, K);
+    }
     if constexpr (EPI == kEpiLinearNorm) {
         // clusters of a row block's n_blocks CTAs, as many as the device holds at once (a persistent cluster takes row
         // blocks b, b + clusters, ...)
@@ -957,7 +1028,10 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
     } else {
         switch (epilogue) {
             case kEpiLinearF16:
-                if (width == 256) return launch<1, 256, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
+                // CTA pairs where the tiles fill the SMs: each CTA loads half of B, which is the larger share of this
+                // GEMM's operand traffic (its fp16 K is twice the int8 GEMMs' bytes): 23.6 -> 21.7 us a launch at 256
+                // boards. The int8 GEMMs measured slower as pairs (their projections 14.4 -> 18.3 us; down the same)
+                if (width == 256) return launch<1, 256, false, kEpiLinearF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<1, 128, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);

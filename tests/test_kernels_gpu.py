@@ -82,8 +82,7 @@ def test_int8_linear_is_the_references(golden, key):
     assert np.allclose(found.cpu().double().numpy(), exact, atol=1e-3, rtol=2e-3)
 
 
-# 17920 and 19001 rows take the A-resident kernels (a CTA per 128-row block; past 148 blocks a CTA takes two, the last
-# one partial)
+# 17920 and 19001 rows: 140 and 149 row blocks over the SMs, so some CTAs take two (the last block partial)
 @pytest.mark.parametrize("M", [5, 70, 4480, 17920, 19001])
 @pytest.mark.parametrize("epilogue", ["bias", "gated", "residual", "mixing"])
 def test_int8_linear_is_the_oracle_on_fry_shapes(M, epilogue):
@@ -161,7 +160,8 @@ def test_linear_norm_quant_is_linear_then_norm_quant(M, N):
     assert ((q.cpu().float() * scale.cpu()[:, None] - normed).abs() <= 0.501 * step[:, None] + 1e-6).all()
 
 
-@pytest.mark.parametrize("M, N, K", [(70, 200, 128), (4480, 768, 768)])
+# 17920 and 19001 rows take CTA pairs (at 19001 the last 256-row tile holds 57 real rows, all in its first CTA)
+@pytest.mark.parametrize("M, N, K", [(70, 200, 128), (4480, 768, 768), (17920, 768, 768), (19001, 768, 768)])
 def test_fp16_linear_is_the_oracle(M, N, K):
     g = torch.Generator().manual_seed(N)
     x = torch.randn(M, K, generator=g).half()
