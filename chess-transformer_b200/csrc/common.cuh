@@ -105,6 +105,11 @@ FRY_DEVICE void st_peer_f32x2(uint32_t address, float a, float b) {
 FRY_DEVICE void mbar_arrive_peer(uint32_t address) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(address) : "memory");
 }
+// An arrival on a cluster CTA's mbarrier that publishes no memory of its own (release at CTA scope, the instruction's
+// default): a hand-over whose ordering other fences provide, such as TMEM reads before tcgen05's thread-sync fence.
+FRY_DEVICE void mbar_arrive_remote(uint32_t address) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(address) : "memory");
+}
 FRY_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
     uint32_t done;
     asm volatile(

@@ -591,8 +591,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     uint8_t* a = stages + s * S::kStageBytes;
                     uint8_t* b = NKS > 0 ? a : a + S::kABytes;
                     if (it >= preloaded) {  // a preloaded stage has its barrier armed and its B in flight
-                        // PAIR: the even CTA's MMA warp frees the stage in both CTAs
-                        if (!(PAIR ? mbar_wait_cluster(&empty[s], phase ^ 1, 10) : mbar_wait(&empty[s], phase ^ 1, 10))) {
+                        // PAIR: the even CTA's MMA warp frees the stage in both CTAs (its commit arrives on both)
+                        if (!mbar_wait(&empty[s], phase ^ 1, 10)) {
                             ok = false;
                             break;
                         }
@@ -622,9 +622,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int tile = first_tile; tile < tiles && ok; tile = next_tile(tile), ++local) {
                 const int buffer = local & 1;
                 if (unit_start(tile) && !mbar_wait(a_ready, (units++) & 1, 16)) break;  // the unit's A is made
-                if (!(PAIR ? mbar_wait_cluster(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)
-                           : mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)))
-                    break;
+                if (!mbar_wait(&tmem_empty[buffer], ((local >> 1) & 1) ^ 1, 11)) break;
                 tc_fence_after();
                 const uint32_t accumulator = tmem + buffer * S::kAccCols;
                 for (int kt = 0; kt < k_tiles; ++kt, ++it) {
@@ -744,8 +742,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             const float xs = NKS > 0 ? xs_unit : xs_next;
-            if (alive && !(PAIR ? mbar_wait_cluster(&tmem_full[buffer], (local >> 1) & 1, 13) : mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)))
-                alive = false;
+            if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             const float* columns = column_buffers + buffer * S::kColumnArrays * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
             // kEpiLinearNorm: this thread's fp16 outputs (its row, its chunks) and their partial sums for the row's norm:
@@ -796,7 +793,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
-                        if constexpr (PAIR) mbar_arrive_peer(peer_smem(&tmem_empty[buffer], 0));  // the even CTA's MMA warp waits on it
+                        if constexpr (PAIR) mbar_arrive_remote(peer_smem(&tmem_empty[buffer], 0));  // the even CTA's MMA warp waits on it
                         else mbar_arrive(&tmem_empty[buffer]);
                     }
                     if (next < tiles) fetch_operands(next, buffer ^ 1);
@@ -959,6 +956,10 @@ cudaError_t launch(const void* a, const void* b, const GemmArgs& args, int M, in
 // its 96 KB of slots (three at 256). When that leaves fewer tiles
 // than SMs (small batches), narrower tiles (128, then 64 columns: more CTAs streaming the weights, deeper pipelines)
 // take their place. An fp16 output needs N a multiple of 8 (its rows 16-byte aligned for the TMA maps).
+// Where the 256-column tiles fill the SMs (large batches), every GEMM with an fp16 or bf16 output runs as CTA pairs
+// (PAIR), the normed-A and norm-epilogue forms excepted: a CTA loads half the B bytes, and a launch at 256 boards takes projection 16.8 -> 16.4 (1152) and 20.3 ->
+// 18.9 us (1440), gate_up 24.4 -> 23.8, down 24.1 -> 21.6, attention-out 23.5 -> 19.8 (ten launches a graph). At 64
+// boards pairs of 128-column tiles measured slower (gate_up 9.6 -> 10.5 us), so smaller batches keep single CTAs.
 cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const GemmArgs& args, int M, int N, int K, cudaStream_t stream,
                  std::string* error) {
     int device = 0, multiprocessors = 0;
@@ -989,8 +990,8 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 // 192-column tiles where they pad N less than 256-column ones (the projection at dq 8: 960 against 1024
                 // columns; 40 KB stages, four deep): 20.4 -> 19-19.9 us a launch at 256 boards; 128 columns did not gain
                 if (width == 256 && (N + 191) / 192 * 192 < (N + 255) / 256 * 256)
-                    return launch<0, 192, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
-                if (width == 256) return launch<0, 256, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
+                    return launch<0, 192, false, kEpiBias, 64, 0, true>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiBias, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
             case kEpiBiasQkNorm:
@@ -1000,27 +1001,28 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                     return cudaErrorInvalidValue;
                 }
                 if (width == 256 && (N + 191) / 192 * 192 < (N + 255) / 256 * 256)
-                    return launch<0, 192, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
-                if (width == 256) return launch<0, 256, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
+                    return launch<0, 192, false, kEpiBiasQkNorm, 64, 0, true>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiBiasQkNorm, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
             case kEpiGated:
+                if (width == 256) return launch<0, 128, true, kEpiGated, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual:
-                if (width == 256) return launch<0, 256, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiResidual, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
             case kEpiMix:
                 // 192 columns also where they take the tiles in one round that 128 would take in two (64 boards: 12.3
                 // against 13.8 us a launch)
-                if (width == 256 || (width == 128 && tiles(192) <= multiprocessors))
-                    return launch<0, 192, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 192, false, kEpiMix, 64, 0, true>(a, b, args, M, N, K, stream, error);
+                if (width == 128 && tiles(192) <= multiprocessors) return launch<0, 192, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiMix, 64>(a, b, args, M, N, K, stream, error);
             case kEpiInt32: return launch<0, 128, false, kEpiInt32>(a, b, args, M, N, K, stream, error);
             case kEpiScaleBf16:
-                if (width == 256) return launch<0, 256, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<0, 256, false, kEpiScaleBf16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiScaleBf16, 64>(a, b, args, M, N, K, stream, error);
             default: break;
@@ -1028,18 +1030,16 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
     } else {
         switch (epilogue) {
             case kEpiLinearF16:
-                // CTA pairs where the tiles fill the SMs: each CTA loads half of B, which is the larger share of this
-                // GEMM's operand traffic (its fp16 K is twice the int8 GEMMs' bytes): 23.6 -> 21.7 us a launch at 256
-                // boards. The int8 GEMMs measured slower as pairs (their projections 14.4 -> 18.3 us; down the same)
                 if (width == 256) return launch<1, 256, false, kEpiLinearF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<1, 128, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             case kEpiGatedF16:
+                if (width == 256) return launch<1, 128, true, kEpiGatedF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width >= 128 || tiles(128) >= multiprocessors) return launch<1, 128, true, kEpiGatedF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, true, kEpiGatedF16>(a, b, args, M, N, K, stream, error);
             case kEpiMixF16:
-                if (width == 256) return launch<1, 192, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
+                if (width == 256) return launch<1, 192, false, kEpiMixF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<1, 128, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiMixF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearNorm:
