@@ -1006,7 +1006,8 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 128) return launch<0, 128, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
             case kEpiGated:
-                if (width == 256) return launch<0, 128, true, kEpiGated, 64, 0, true>(a, b, args, M, N, K, stream, error);
+                // as pairs, 128-column sub-tiles (two chunks a warp between barriers): 23.8 -> 22.5 us a launch at 256 boards
+                if (width == 256) return launch<0, 128, true, kEpiGated, 128, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width >= 128 || tiles(128) >= multiprocessors) return launch<0, 128, true, kEpiGated, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual:
