@@ -258,7 +258,8 @@ FRY_DEVICE void mma_commit_pair(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 // 2-D tiled TMA load into this CTA's shared memory that completes on an mbarrier of either CTA of the pair (`bar` a
-// shared::cluster address): both CTAs' operand loads complete on the even CTA's stage barrier. Not a multicast.
+// shared::cluster address): both CTAs' operand loads complete on the even CTA's stage barrier. Each CTA loads only
+// into its own shared memory.
 FRY_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
