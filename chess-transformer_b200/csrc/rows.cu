@@ -143,20 +143,32 @@ FRY_DEVICE void board_feature_rows(const Token* __restrict__ boards, int pitch, 
         codes[t] = ok ? static_cast<int>(token) : 0;
     }
     __syncthreads();
-    if (tid < 4) {
-        const int wanted[4] = {6, 12, 5, 11};  // our king, their king, our queen, their queen
-        int first = kSquares;
-        for (int s = 0; s < kSquares; ++s)
-            if (codes[s] == wanted[tid]) {
-                first = s;
-                break;
-            }
-        firsts[tid] = first;
+    if (tid < 32) {  // the first square of our king, their king, our queen, their queen: a warp's ballots over the squares
+        const int wanted[4] = {6, 12, 5, 11};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const unsigned low = __ballot_sync(0xffffffffu, codes[tid] == wanted[i]), high = __ballot_sync(0xffffffffu, codes[32 + tid] == wanted[i]);
+            if (tid == 0) firsts[i] = low ? __ffs(low) - 1 : high ? 32 + __ffs(high) - 1 : kSquares;
+        }
     }
     __syncthreads();
     {
+        // four threads a square, the walks along lines shared out so no thread takes more than about 28 lookups
         const int s = tid & 63, part = tid >> 6, file = s & 7, rank = s >> 3;
         int* r = rows[s];
+        // the nearest piece along direction d: 1 + (code - 1) * 7 + (distance - 1), 0 if none before the edge
+        auto line_row = [&](int d) {
+            int line = 0;
+            for (int k = 1; k <= 7; ++k) {
+                const int c = code_at(codes, file + kDirections[d][0] * k, rank + kDirections[d][1] * k);
+                if (c == kEdge) break;
+                if (c != 0) {
+                    line = 1 + (c - 1) * 7 + (k - 1);
+                    break;
+                }
+            }
+            r[12 + d] = kFeatureRowOffset[12 + d] + line;
+        };
         if (part == 0) {
             for (int i = 0; i < 4; ++i) {
                 const int p = firsts[i];
@@ -171,20 +183,13 @@ FRY_DEVICE void board_feature_rows(const Token* __restrict__ boards, int pitch, 
             r[20] = kFeatureRowOffset[20] + min(ours, 2) * 3 + min(theirs, 2);
         } else if (part == 1) {
             for (int d = 0; d < 8; ++d) r[4 + d] = kFeatureRowOffset[4 + d] + code_at(codes, file + kDirections[d][0], rank + kDirections[d][1]);
+            line_row(0);
+            line_row(1);
         } else if (part == 2) {
-            for (int d = 0; d < 8; ++d) {
-                int line = 0;
-                for (int k = 1; k <= 7; ++k) {
-                    const int c = code_at(codes, file + kDirections[d][0] * k, rank + kDirections[d][1] * k);
-                    if (c == kEdge) break;
-                    if (c != 0) {
-                        line = 1 + (c - 1) * 7 + (k - 1);
-                        break;
-                    }
-                }
-                r[12 + d] = kFeatureRowOffset[12 + d] + line;
-            }
+            for (int d = 2; d < 6; ++d) line_row(d);
         } else {
+            line_row(6);
+            line_row(7);
             for (int d = 0; d < 2; ++d) {  // up and down the file: the nearest pawn of either side, others do not block
                 int pawn = 0;
                 for (int k = 1; k <= 7; ++k) {
@@ -201,11 +206,13 @@ FRY_DEVICE void board_feature_rows(const Token* __restrict__ boards, int pitch, 
     }
 }
 
-// One CTA per (board, 256 columns): the 64 x 23 feature rows into shared memory, then every (token, 8 columns) summed.
+// One CTA per (board, slice of `slice` columns, group of tokens): the 64 x 23 feature rows into shared memory, then
+// every (token, 8 columns) of its share summed. Small batches split a board's tokens over more CTAs (gridDim.z), so
+// each thread's chain of gathers is short.
 template <typename Token>
 __global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict__ boards, int pitch, const uint16_t* __restrict__ embed,
                                                         const uint16_t* __restrict__ position, const uint16_t* __restrict__ table,
-                                                        uint16_t* __restrict__ out, int D) {
+                                                        uint16_t* __restrict__ out, int D, int slice) {
     grid_dependency_start();
     __shared__ int codes[kTokens];
     __shared__ int firsts[4];
@@ -213,11 +220,12 @@ __global__ void __launch_bounds__(256) embedding_kernel(const Token* __restrict_
     const int b = blockIdx.x, tid = threadIdx.x;
     board_feature_rows(boards, pitch, b, codes, firsts, rows, tid);
     __syncthreads();
-    // this CTA's slice of the columns: [blockIdx.y * 256, + 256)
-    const int first = blockIdx.y * 256, width = D - first < 256 ? D - first : 256;
+    // this CTA's slice of the columns, [blockIdx.y * slice, + slice), and its tokens, [token_begin, token_end)
+    const int first = blockIdx.y * slice, width = D - first < slice ? D - first : slice;
     const int vectors = width / 8;
-    for (int idx = tid; idx < kTokens * vectors; idx += blockDim.x) {
-        const int t = idx / vectors, col = first + (idx % vectors) * 8;
+    const int token_begin = blockIdx.z * kTokens / gridDim.z, token_end = (blockIdx.z + 1) * kTokens / gridDim.z;
+    for (int idx = tid; idx < (token_end - token_begin) * vectors; idx += blockDim.x) {
+        const int t = token_begin + idx / vectors, col = first + (idx % vectors) * 8;
         float e[8], p[8];
         unpack8(*reinterpret_cast<const uint4*>(embed + static_cast<size_t>(codes[t]) * D + col), e);
         unpack8(*reinterpret_cast<const uint4*>(position + static_cast<size_t>(t) * D + col), p);
@@ -345,12 +353,35 @@ cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int 
                             width);
 }
 
+// The embedding's grid: 256-column slices while the boards give at least two CTAs an SM; below that 128-column slices
+// and each board's tokens split over up to 10 CTAs, as many as take the CTAs to two an SM (1 board: 60 CTAs of 7 tokens).
+cudaError_t embedding_grid(int B, int D, dim3* grid, int* slice) {
+    int device = 0, multiprocessors = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const int wanted = 2 * multiprocessors;
+    *slice = 256;
+    int slices = (D + 255) / 256, groups = 1;
+    if (B * slices < wanted) {
+        *slice = 128;
+        slices = (D + 127) / 128;
+        groups = (wanted + B * slices - 1) / (B * slices);
+        groups = groups < 1 ? 1 : groups > 10 ? 10 : groups;
+    }
+    *grid = dim3(B, slices, groups);
+    return cudaSuccess;
+}
+
 cudaError_t board_embedding(const int64_t* boards, const uint16_t* embed, const uint16_t* position, const uint16_t* table,
                             uint16_t* out, int B, int D, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
     if (D % 8 != 0) return cudaErrorInvalidValue;
-    return launch_dependent(embedding_kernel<int64_t>, dim3(B, (D + 255) / 256), dim3(256), 0, stream, boards, kTokens, embed, position,
-                            table, out, D);
+    dim3 grid;
+    int slice = 0;
+    const cudaError_t status = embedding_grid(B, D, &grid, &slice);
+    if (status != cudaSuccess) return status;
+    return launch_dependent(embedding_kernel<int64_t>, grid, dim3(256), 0, stream, boards, kTokens, embed, position, table, out, D, slice);
 }
 
 cudaError_t square_feature_rows(const int64_t* boards, int32_t* rows, int B, cudaStream_t stream) {
@@ -362,8 +393,12 @@ cudaError_t board_embedding_lean(const uint8_t* lean_rows, const uint16_t* embed
                                  uint16_t* out, int B, int D, cudaStream_t stream) {
     if (B <= 0) return cudaSuccess;
     if (D % 8 != 0) return cudaErrorInvalidValue;
-    return launch_dependent(embedding_kernel<uint8_t>, dim3(B, (D + 255) / 256), dim3(256), 0, stream, lean_rows, kLeanRow, embed, position,
-                            table, out, D);
+    dim3 grid;
+    int slice = 0;
+    const cudaError_t status = embedding_grid(B, D, &grid, &slice);
+    if (status != cudaSuccess) return status;
+    return launch_dependent(embedding_kernel<uint8_t>, grid, dim3(256), 0, stream, lean_rows, kLeanRow, embed, position, table, out, D,
+                            slice);
 }
 
 }  // namespace fry
