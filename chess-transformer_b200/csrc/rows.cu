@@ -16,19 +16,24 @@ namespace fry {
 
 constexpr int kRowWarps = 8;
 constexpr int kRowCtasPerSm = 3;  // persistent row kernels: CTAs of kRowWarps warps an SM
+// from kMidRows up to kLargeRows rows the persistent row kernels take more, smaller CTAs, more warps an SM: at 64 boards
+// (4480 rows) rotate_quant 4.90 -> 4.2 us and norm_quant 3.80 -> 3.63 us a launch, the forward 1.844 -> 1.823 ms; at
+// 16 boards the forward was 2.6% slower that way, and at 256 boards 8 x 3 stays best or level
+constexpr int kSmallRowWarps = 4, kSmallRowCtasPerSm = 7, kMidRows = 4096, kLargeRows = 8192;
+inline bool mid_rows(int M) { return M >= kMidRows && M < kLargeRows; }
 
 // x [M, D] fp16 -> q [M, D] int8, scale [M]; with MIX, x is first mixed with original and the mix stored to mixed.
 // Persistent warps: warp w of W takes rows w, w + W, ..., loading the next row while it works on this one. A row's
 // arithmetic is the single-row order: per lane over its chunks, then the warp's tree.
-template <int CHUNKS, bool MIX>
-__global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
+template <int CHUNKS, bool MIX, int WARPS = kRowWarps, int CTAS = kRowCtasPerSm>
+__global__ void __launch_bounds__(WARPS * 32, CTAS) norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ original,
                                                                     const uint16_t* residual_scale, const uint16_t* input_scale,
                                                                     const uint16_t* __restrict__ gain, float eps, uint16_t* mixed,
                                                                     int8_t* __restrict__ q, float* __restrict__ scale, int M, int D) {
     grid_dependency_start();
     const int lane = threadIdx.x & 31;
-    const int stride = gridDim.x * kRowWarps;
-    int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int stride = gridDim.x * WARPS;
+    int row = blockIdx.x * WARPS + (threadIdx.x >> 5);
     if (row >= M) return;
     float rs = 0.0f, is = 0.0f;
     if constexpr (MIX) {
@@ -97,12 +102,13 @@ __global__ void __launch_bounds__(kRowWarps * 32) rms_norm_kernel(const uint16_t
 
 // h [M, hidden] fp16 -> q [M, width] int8 (width <= 1024, a multiple of 32), scale [M], by rotate_quant_row.
 // Persistent warps, as norm_quant: warp w of W takes rows w, w + W, ..., loading the next row while it works on one.
-__global__ void __launch_bounds__(kRowWarps * 32, kRowCtasPerSm) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
-                                                                                     float* __restrict__ scale, int M, int hidden, int width) {
+template <int WARPS = kRowWarps, int CTAS = kRowCtasPerSm>
+__global__ void __launch_bounds__(WARPS * 32, CTAS) rotate_quant_kernel(const uint16_t* __restrict__ h, int8_t* __restrict__ q,
+                                                                        float* __restrict__ scale, int M, int hidden, int width) {
     grid_dependency_start();
     const int lane = threadIdx.x & 31;
-    const int stride = gridDim.x * kRowWarps;
-    int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int stride = gridDim.x * WARPS;
+    int row = blockIdx.x * WARPS + (threadIdx.x >> 5);
     if (row >= M) return;
     uint4 raw[4];
     load_row_chunks<4, true>(h + static_cast<size_t>(row) * hidden, hidden, lane, raw);
@@ -270,25 +276,34 @@ cudaError_t norm_quant(const uint16_t* x, const uint16_t* original, const uint16
     if (M <= 0) return cudaSuccess;
     if (D % 8 != 0 || D > 1024) return cudaErrorInvalidValue;
     const bool mix = original != nullptr;
-    // persistent warps: up to kRowCtasPerSm CTAs an SM, each warp looping over rows
+    // persistent warps: up to kRowCtasPerSm CTAs an SM, each warp looping over rows (kSmallRow* from kMidRows to kLargeRows)
     int device = 0, multiprocessors = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    const int wanted = (M + kRowWarps - 1) / kRowWarps, most = multiprocessors * kRowCtasPerSm;
+    const bool small = mid_rows(M);
+    const int warps = small ? kSmallRowWarps : kRowWarps, ctas = small ? kSmallRowCtasPerSm : kRowCtasPerSm;
+    const int wanted = (M + warps - 1) / warps, most = multiprocessors * ctas;
     const dim3 grid(wanted < most ? wanted : most);
     const int chunks = (D + 255) / 256;
-#define FRY_NQ(C)                                                                                                                  \
-    status = mix ? launch_dependent(norm_quant_kernel<C, true>, grid, dim3(kRowWarps * 32), 0, stream, x, original, residual_scale,   \
-                                    input_scale, gain, eps, mixed, q, scale, M, D)                                                  \
-                 : launch_dependent(norm_quant_kernel<C, false>, grid, dim3(kRowWarps * 32), 0, stream, x, original, residual_scale,  \
+#define FRY_NQ_SHAPE(C, W, N)                                                                                                         \
+    status = mix ? launch_dependent(norm_quant_kernel<C, true, W, N>, grid, dim3(W * 32), 0, stream, x, original, residual_scale,     \
+                                    input_scale, gain, eps, mixed, q, scale, M, D)                                                    \
+                 : launch_dependent(norm_quant_kernel<C, false, W, N>, grid, dim3(W * 32), 0, stream, x, original, residual_scale,    \
                                     input_scale, gain, eps, mixed, q, scale, M, D)
+#define FRY_NQ(C)                                                                                                                    \
+    if (small) {                                                                                                                     \
+        FRY_NQ_SHAPE(C, kSmallRowWarps, kSmallRowCtasPerSm);                                                                        \
+    } else {                                                                                                                         \
+        FRY_NQ_SHAPE(C, kRowWarps, kRowCtasPerSm);                                                                                  \
+    }
     switch (chunks) {
         case 1: FRY_NQ(1); break;
         case 2: FRY_NQ(2); break;
         case 3: FRY_NQ(3); break;
         default: FRY_NQ(4); break;
     }
+#undef FRY_NQ_SHAPE
 #undef FRY_NQ
     return status;
 }
@@ -348,8 +363,13 @@ cudaError_t rotate_quant(const uint16_t* h, int8_t* q, float* scale, int M, int 
     cudaError_t status = cudaGetDevice(&device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
+    if (mid_rows(M)) {
+        const int wanted = (M + kSmallRowWarps - 1) / kSmallRowWarps, most = multiprocessors * kSmallRowCtasPerSm;
+        return launch_dependent(rotate_quant_kernel<kSmallRowWarps, kSmallRowCtasPerSm>, dim3(wanted < most ? wanted : most),
+                                dim3(kSmallRowWarps * 32), 0, stream, h, q, scale, M, hidden, width);
+    }
     const int wanted = (M + kRowWarps - 1) / kRowWarps, most = multiprocessors * kRowCtasPerSm;
-    return launch_dependent(rotate_quant_kernel, dim3(wanted < most ? wanted : most), dim3(kRowWarps * 32), 0, stream, h, q, scale, M, hidden,
+    return launch_dependent(rotate_quant_kernel<>, dim3(wanted < most ? wanted : most), dim3(kRowWarps * 32), 0, stream, h, q, scale, M, hidden,
                             width);
 }
 
