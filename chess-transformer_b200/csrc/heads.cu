@@ -166,28 +166,34 @@ __global__ void __launch_bounds__(kNarrowTiles * kNarrowParts * 32) narrow_kerne
 }
 
 
-// One CTA (8 warps) per board: L = a_sq . y_sq^T (64 x 64), then the 1968 move logits. The board's 64 square rows of a
-// (fp32) and y (fp16) stream through shared memory in chunks of kPolicyChunk columns, kPolicyStages deep, by 16-byte cp.async
-// (whole 128-byte lines per 8 lanes); each warp takes its 16 x 32 tile of L from fragments read out of shared memory,
-// the padded pitches putting each fragment load on distinct banks.
+// One CTA (8 warps) per (board, Q-th of the from-squares): its 64 / Q rows of L = a_sq . y_sq^T (64 x 64), then the
+// move logits of the moves from those squares. The CTA's square rows of a (fp32) and the board's 64 of y (fp16) stream
+// through shared memory in chunks of kPolicyChunk columns, kPolicyStages deep, by 16-byte cp.async (whole 128-byte lines
+// per 8 lanes); each warp takes its 16 x 32 / Q tile of L from fragments read out of shared memory, the padded pitches
+// putting each fragment load on distinct banks. Q = 1 but at a few boards, which split a board over 4 CTAs. Each
+// logit's sums run in the same order whatever Q, so the rows do not depend on it.
+template <int Q>
 __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a, const uint16_t* __restrict__ y,
                                                      const float* __restrict__ narrow, float* __restrict__ rows, int D) {
+    static_assert(Q == 1 || Q == 2 || Q == 4, "a board's from-squares in 1, 2 or 4 parts");
+    constexpr int kRowsHere = kHeadSquares / Q, kNt = 4 / Q;  // a's rows this CTA; n tiles of 8 a warp
     extern __shared__ __align__(16) float policy_smem[];  // a chunks, then y chunks; the logits reuse the a chunks at the end
     auto a_chunks = reinterpret_cast<float(*)[kHeadSquares * kPolicyAPitch]>(policy_smem);
     auto y_chunks = reinterpret_cast<uint16_t(*)[kHeadSquares * kPolicyYPitch]>(policy_smem + kPolicyStages * kHeadSquares * kPolicyAPitch);
     auto logits = reinterpret_cast<float(*)[kHeadSquares + 1]>(policy_smem);
     grid_dependency_start();
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int m_tile = warp >> 1, n_first = (warp & 1) * 4;
+    // this CTA's from-squares [row0, row0 + kRowsHere); 2 Q warps a 16-row m tile, each with kNt n tiles
+    const int row0 = blockIdx.y * kRowsHere, m_tile = warp / (2 * Q), n_first = (warp % (2 * Q)) * kNt;
     const size_t board = static_cast<size_t>(b) * kHeadTokens;
     const int chunks = (D + kPolicyChunk - 1) / kPolicyChunk;
     auto load_chunk = [&](int chunk) {
         const int stage = chunk % kPolicyStages, k0 = chunk * kPolicyChunk;
         constexpr int a_pieces = kPolicyChunk / 4, y_pieces = kPolicyChunk / 8;  // 16-byte pieces of a row
 #pragma unroll
-        for (int i = threadIdx.x; i < kHeadSquares * a_pieces; i += 256) {
+        for (int i = threadIdx.x; i < kRowsHere * a_pieces; i += 256) {
             const int r = i / a_pieces, piece = i % a_pieces, k = k0 + piece * 4;
-            if (k < D) cp_async16(&a_chunks[stage][r * kPolicyAPitch + piece * 4], a + (board + r) * D + k);
+            if (k < D) cp_async16(&a_chunks[stage][r * kPolicyAPitch + piece * 4], a + (board + row0 + r) * D + k);
         }
 #pragma unroll
         for (int i = threadIdx.x; i < kHeadSquares * y_pieces; i += 256) {
@@ -200,9 +206,9 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
         if (chunk < chunks) load_chunk(chunk);
         cp_async_commit();
     }
-    float hi[4][4], lo[4][4];
+    float hi[kNt][4], lo[kNt][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < kNt; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) hi[n][e] = lo[n][e] = 0.0f;
     for (int chunk = 0; chunk < chunks; ++chunk) {
@@ -222,7 +228,7 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
 #pragma unroll
                 for (int i = 0; i < 4; ++i) split_pair(a_pairs[i], ah[i], al[i]);
 #pragma unroll
-                for (int n = 0; n < 4; ++n) {
+                for (int n = 0; n < kNt; ++n) {
                     const uint16_t* yn = ys + n * 8 * kPolicyYPitch + kk;
                     const uint32_t b0 = *reinterpret_cast<const uint32_t*>(yn), b1 = *reinterpret_cast<const uint32_t*>(yn + 8);
                     mma_f16_heads(hi[n], ah, b0, b1);
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
     cp_async_wait<0>();
     __syncthreads();  // every warp is done reading the chunks the logits overwrite
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < kNt; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int row = m_tile * 16 + g + (e >> 1) * 8, col = (n_first + n) * 8 + 2 * t + (e & 1);
@@ -244,7 +250,8 @@ __global__ void __launch_bounds__(256) policy_kernel(const float* __restrict__ a
     const float* board_narrow = narrow + board * kNarrowStride;
     for (int m = threadIdx.x; m < kMoves; m += blockDim.x) {
         const int pair = kMovePairs[m], from = pair >> 6, to = pair & 63;
-        float logit = __fadd_rn(logits[from][to], board_narrow[from * kNarrowStride]);
+        if (from < row0 || from >= row0 + kRowsHere) continue;  // another CTA's square
+        float logit = __fadd_rn(logits[from - row0][to], board_narrow[from * kNarrowStride]);
         const int promotion = kMovePromotion[m];
         if (promotion >= 0) logit = __fadd_rn(logit, board_narrow[to * kNarrowStride + 1 + promotion]);
         rows[static_cast<size_t>(b) * (kMoves + 1) + m] = logit;
@@ -410,9 +417,18 @@ cudaError_t heads(const uint16_t* stream_x, const HeadWeights& w, float eps, flo
                               narrow_smem, stream, y, w.narrow_weight, w.narrow_bias, narrow, eval_in, M, D);
     if (status != cudaSuccess) return status;
     const size_t policy_smem = kPolicyStages * kHeadSquares * (kPolicyAPitch * sizeof(float) + kPolicyYPitch * sizeof(uint16_t));
-    status = ensure_smem(reinterpret_cast<const void*>(policy_kernel), static_cast<int>(policy_smem));
+    // a board's from-squares over 4 CTAs while that leaves at least half the SMs idle: at 1 board the forward 918 -> 912
+    // us; at 64 and 256 boards, the 4 CTAs a board measured slower (1.822 -> 1.830, 4.75 -> 4.78 ms)
+    int device = 0, multiprocessors = 0;
+    status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&multiprocessors, cudaDevAttrMultiProcessorCount, device);
     if (status != cudaSuccess) return status;
-    status = launch_dependent(policy_kernel, dim3(B), dim3(256), policy_smem, stream, a, y, narrow, rows, D);
+    auto run_policy = [&](auto kernel, int parts) {
+        cudaError_t attribute = ensure_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(policy_smem));
+        if (attribute != cudaSuccess) return attribute;
+        return launch_dependent(kernel, dim3(B, parts), dim3(256), policy_smem, stream, a, y, narrow, rows, D);
+    };
+    status = 8 * B <= multiprocessors ? run_policy(policy_kernel<4>, 4) : run_policy(policy_kernel<1>, 1);
     if (status != cudaSuccess) return status;
     // the eval head: hidden = GELU(W1 . eval_in + b1), logits = W2 . hidden + b2, each as split-K partial products
     const int split1 = split_size(kEvalInputs), splits1 = (kEvalInputs + split1 - 1) / split1;
