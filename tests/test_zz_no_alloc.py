@@ -69,6 +69,32 @@ def test_the_allocation_free_heads_give_the_heads_answers_on_two_calls_in_a_row(
         assert torch.isfinite(found).all()
 
 
+def test_the_allocation_free_heads_replay_from_a_captured_graph():
+    # the header's contract: one call outside a capture (it sets the kernels' attributes), then the entry point records
+    # into a CUDA graph on a side stream with no allocation, and every replay writes the heads' answers
+    lib = library()
+    weights = prepared_heads(MAX_D_MODEL)
+    struct = heads_struct(*weights)
+    stream_x = (torch.randn(8, 70, MAX_D_MODEL, generator=torch.Generator().manual_seed(5)) / 4).half().cuda()
+    expected = rows_with_workspace(lib, stream_x, weights, struct)
+    rows = torch.empty(8, 1969, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    call = lambda: lib.fry_heads_noalloc(ctypes.c_void_p(stream_x.data_ptr()), ctypes.byref(struct), 1e-5, ctypes.c_void_p(rows.data_ptr()),
+                                         8, MAX_D_MODEL, ctypes.c_void_p(side.cuda_stream))
+    with torch.cuda.stream(side):
+        call()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(2):
+        rows.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(rows, expected)
+
+
 def test_the_allocation_free_heads_refuse_more_than_their_array_holds():
     lib = library()
     weights = prepared_heads(MAX_D_MODEL)
