@@ -127,30 +127,40 @@ struct GemmShape {
 
 FRY_DEVICE void epilogue_sync() { asm volatile("bar.sync %0, %1;" ::"n"(kEpilogueBarrier), "n"(kEpilogueThreads + 32) : "memory"); }
 
-// The tile's column operands into shared memory (all epilogue threads together): columns[0, BN) the weight scales,
-// columns[SECOND, SECOND + BN) up's scales (gated) or the bias as floats, zero past N; the linears have no scales and
-// the mix and residual epilogues no second operand, so theirs share the one array (SECOND = 0).
-template <int EPI, int BN, int SECOND>
-FRY_DEVICE void stage_columns(const GemmArgs& p, float* columns, int n0, int N, int tid) {
-    for (int i = tid; i < BN; i += kEpilogueThreads) {
-        const int n = n0 + i;
-        const bool ok = n < N;
-        float scale = 0.0f, second = 0.0f;
-        if constexpr (scaled(EPI)) scale = ok ? p.w_scale[n] : 0.0f;
-        if constexpr (EPI == kEpiGated) second = ok ? p.w_scale[N + n] : 0.0f;
-        if constexpr (biased(EPI) || linear16(EPI) || EPI == kEpiGatedF16) second = (ok && p.bias) ? h2f_bits(p.bias[n]) : 0.0f;
-        if constexpr (EPI == kEpiLinearF32) second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
-        if constexpr (scaled(EPI)) columns[i] = scale;
-        if constexpr (EPI == kEpiLinearNorm) columns[i] = (ok && p.norm_gain) ? h2f_bits(p.norm_gain[n]) : 0.0f;
-        if constexpr (biased(EPI) || EPI == kEpiGated || linear16(EPI) || EPI == kEpiLinearF32 || EPI == kEpiGatedF16)
-            columns[SECOND + i] = second;
-        if constexpr (EPI == kEpiBiasQkNorm) {
-            float gain = 0.0f;
-            if (n < p.qk_queries) gain = h2f_bits(p.q_gain[n % p.qk_dq]);
-            else if (n < p.qk_keys) gain = h2f_bits(p.k_gain[(n - p.qk_queries) % p.qk_dq]);
-            columns[2 * BN + i] = gain;
-        }
+// A tile's column operands for one column n, as loaded: the weight scale (scaled epilogues), up's weight scale (gated)
+// or the fp32 bias, the fp16 bias, and the fp16 gain (the norm epilogue's, or the q/k norm's for a query or key column);
+// zero past N. They are loaded a tile ahead into registers and written to shared memory at the end of that tile (by
+// store_columns), so the loads' latency passes while the thread works on the tile before.
+struct ColumnLoad {
+    float scale = 0.0f, second = 0.0f;
+    uint16_t half = 0, gain = 0;  // fp16 bits; zero bits are +0.0
+};
+template <int EPI>
+FRY_DEVICE ColumnLoad load_columns(const GemmArgs& p, int n, int N) {
+    ColumnLoad c;
+    const bool ok = n < N;
+    if constexpr (scaled(EPI)) c.scale = ok ? p.w_scale[n] : 0.0f;
+    if constexpr (EPI == kEpiGated) c.second = ok ? p.w_scale[N + n] : 0.0f;
+    if constexpr (EPI == kEpiLinearF32) c.second = (ok && p.bias_f32) ? p.bias_f32[n] : 0.0f;
+    if constexpr (biased(EPI) || linear16(EPI) || EPI == kEpiGatedF16) c.half = (ok && p.bias) ? p.bias[n] : 0;
+    if constexpr (EPI == kEpiLinearNorm) c.gain = (ok && p.norm_gain) ? p.norm_gain[n] : 0;
+    if constexpr (EPI == kEpiBiasQkNorm) {
+        if (n < p.qk_queries) c.gain = p.q_gain[n % p.qk_dq];
+        else if (n < p.qk_keys) c.gain = p.k_gain[(n - p.qk_queries) % p.qk_dq];
     }
+    return c;
+}
+// Column i's operands into the tile's column buffer: columns[0, BN) the weight scales (the norm gains for the norm
+// epilogue), columns[SECOND, SECOND + BN) up's scales (gated) or the bias as floats, columns[2 BN, 3 BN) the q/k norm's
+// gains; the linears have no scales and the mix and residual epilogues no second operand, so theirs share the one array
+// (SECOND = 0).
+template <int EPI, int BN, int SECOND>
+FRY_DEVICE void store_columns(float* columns, const ColumnLoad& c, int i) {
+    if constexpr (scaled(EPI)) columns[i] = c.scale;
+    if constexpr (EPI == kEpiLinearNorm) columns[i] = h2f_bits(c.gain);
+    if constexpr (EPI == kEpiGated || EPI == kEpiLinearF32) columns[SECOND + i] = c.second;
+    if constexpr (biased(EPI) || linear16(EPI) || EPI == kEpiGatedF16) columns[SECOND + i] = h2f_bits(c.half);
+    if constexpr (EPI == kEpiBiasQkNorm) columns[2 * BN + i] = h2f_bits(c.gain);
 }
 
 // Issues the TMA loads of one sub-tile's row operands (the boxes of its columns below N, none past it) into a slot,
@@ -707,18 +717,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             m0 = row0(tile);
             n0 = column0(tile);
         };
-        // a tile's column operands and this thread's row scale are fetched during the tile before (the first tile's here),
-        // into the other of two column buffers, so one barrier a tile publishes both the staged outputs and them
+        // a tile's column operands (thread i < BN: column n0 + i) and this thread's row scale are loaded into registers
+        // at the start of the tile before (the first tile's here) and the column operands written at its end into the
+        // other of two column buffers, so one barrier a tile publishes both the staged outputs and them
+        static_assert(BN <= kEpilogueThreads, "an epilogue thread stages at most one column");
         bool alive = true;
         float xs_next = 0.0f;
-        auto fetch_operands = [&](int tile, int buffer) {
+        ColumnLoad column_next;
+        auto load_operands = [&](int tile) {
             int m0, n0;
             tile_origin(tile, m0, n0);
             const int m = m0 + row_in_tile;
             if constexpr (scaled(EPI) && NKS == 0) xs_next = (alive && m < M) ? args.x_scale[m] : 0.0f;
-            if constexpr (EPI != kEpiInt32) stage_columns<EPI, BN, S::kSecond>(args, column_buffers + buffer * S::kColumnArrays * BN, n0, N, threadIdx.x);
+            if constexpr (EPI != kEpiInt32)
+                if (threadIdx.x < BN) column_next = load_columns<EPI>(args, n0 + static_cast<int>(threadIdx.x), N);
         };
-        fetch_operands(first_tile, 0);
+        auto store_operands = [&](int buffer) {
+            if constexpr (EPI != kEpiInt32)
+                if (threadIdx.x < BN) store_columns<EPI, BN, S::kSecond>(column_buffers + buffer * S::kColumnArrays * BN, column_next, threadIdx.x);
+        };
+        load_operands(first_tile);
+        store_operands(0);
         epilogue_sync();
         // a warp whose wait timed out keeps walking the tiles (and the named barrier) without touching them, so the other
         // epilogue warps never wait at the barrier for it
@@ -742,6 +761,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             const float xs = NKS > 0 ? xs_unit : xs_next;
+            if (next < tiles) load_operands(next);  // in flight while this tile is worked on
             if (alive && !mbar_wait(&tmem_full[buffer], (local >> 1) & 1, 13)) alive = false;
             const float* columns = column_buffers + buffer * S::kColumnArrays * BN;
             const uint32_t lane_base = tmem + buffer * S::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -796,7 +816,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         if constexpr (PAIR) mbar_arrive_remote(peer_smem(&tmem_empty[buffer], 0));  // the even CTA's MMA warp waits on it
                         else mbar_arrive(&tmem_empty[buffer]);
                     }
-                    if (next < tiles) fetch_operands(next, buffer ^ 1);
+                    if (next < tiles) store_operands(buffer ^ 1);
                 }
                 // this thread's staged writes, visible to the async proxy before the stores read them
                 if constexpr (S::kStaged) fence_proxy_async_shared();
