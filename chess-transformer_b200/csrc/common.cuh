@@ -10,6 +10,7 @@
 
 #include <mutex>
 #include <map>
+#include <tuple>
 #include <utility>
 
 #define FRY_DEVICE __device__ __forceinline__
@@ -361,9 +362,25 @@ inline cudaError_t launch_dependent_cluster(void (*kernel)(Params...), dim3 grid
     return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
 }
 
-// How many clusters of `cluster` CTAs of the kernel (with this block and shared memory) the device holds at once.
+// How many clusters of `cluster` CTAs of the kernel (with this block and shared memory) the device holds at once. The
+// answer is kept per (kernel, device, shared memory, cluster): the occupancy query costs host time on every launch
+// otherwise, which eager (ungraphed) forwards pay per GEMM.
 template <typename... Params>
 inline cudaError_t max_active_clusters(void (*kernel)(Params...), dim3 block, size_t smem, int cluster, int* count) {
+    static std::mutex mutex;
+    static std::map<std::tuple<const void*, int, size_t, int, unsigned>, int> known;
+    int device = 0;
+    const cudaError_t found_device = cudaGetDevice(&device);
+    if (found_device != cudaSuccess) return found_device;
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), device, smem, cluster, block.x * block.y * block.z);
+    {
+        std::lock_guard<std::mutex> lock(mutex);
+        const auto found = known.find(key);
+        if (found != known.end()) {
+            *count = found->second;
+            return cudaSuccess;
+        }
+    }
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(cluster);
     config.blockDim = block;
@@ -375,7 +392,12 @@ inline cudaError_t max_active_clusters(void (*kernel)(Params...), dim3 block, si
     attribute[0].val.clusterDim.z = 1;
     config.attrs = attribute;
     config.numAttrs = 1;
-    return cudaOccupancyMaxActiveClusters(count, reinterpret_cast<const void*>(kernel), &config);
+    const cudaError_t status = cudaOccupancyMaxActiveClusters(count, reinterpret_cast<const void*>(kernel), &config);
+    if (status == cudaSuccess) {
+        std::lock_guard<std::mutex> lock(mutex);
+        known[key] = *count;
+    }
+    return status;
 }
 
 // ---- small numeric helpers -----------------------------------------------------------------------------
