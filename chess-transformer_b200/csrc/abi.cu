@@ -91,7 +91,9 @@ int run_forward(const FryNetwork* n, const int64_t* boards, const uint8_t* lean_
         const bool mixes_next = i + 1 < n->layers && n->blocks[i + 1].precision == b.precision;
         const int rows_p = projection_rows(n, b.dq);
         // an int8 block whose query/key heads are 8 or 16 wide has its projection's epilogue apply the attention's q and
-        // k RMSNorm (the same bits as the attention's own), so the attention copies them
+        // k RMSNorm (the same bits as the attention's own), so the attention copies them. At 24 wide the attention
+        // normalises them itself: the epilogue that does it for 24-wide heads (fry_int8_linear_qk_norm) measured a
+        // slower forward, 4.68 -> 4.74 ms at 256 boards.
         const bool qk_normed = !fp16 && (b.dq == 8 || b.dq == 16) && (n->heads * b.dq) % 16 == 0 && ((n->heads + n->kv_heads) * b.dq) % 16 == 0;
         fry::GemmArgs projection;
         projection.bias = b.projection_bias;
@@ -341,10 +343,11 @@ int fry_template_attention(const uint16_t* projected, const uint16_t* paired_tem
 int fry_int8_linear_qk_norm(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
                             const uint16_t* q_gain, const uint16_t* k_gain, float eps, uint16_t* out, int M, int N, int K, int heads,
                             int kv_heads, int dq, void* stream) {
-    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0 || (dq != 8 && dq != 16) || heads <= 0 || kv_heads <= 0 ||
-        (heads * dq) % 16 != 0 || ((heads + kv_heads) * dq) % 16 != 0 || (heads + kv_heads) * dq > N)
-        return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm takes query/key heads 8 or 16 wide whose blocks start on 16-column boundaries "
-                                     "within N (a multiple of 8), K a multiple of 16");
+    const int boundary = dq == 24 ? 48 : 16;
+    if (M < 0 || N <= 0 || K <= 0 || N % 8 != 0 || K % 16 != 0 || (dq != 8 && dq != 16 && dq != 24) || heads <= 0 || kv_heads <= 0 ||
+        (heads * dq) % boundary != 0 || ((heads + kv_heads) * dq) % boundary != 0 || (heads + kv_heads) * dq > N)
+        return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm takes query/key heads 8 or 16 wide whose blocks start on 16-column boundaries, "
+                                     "or 24 wide on 48-column boundaries, within N (a multiple of 8), K a multiple of 16");
     if (!aligned16(x) || !aligned16(weight) || !aligned16(out)) return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm needs 16-byte aligned x, weight and out");
     if (!x_scale || !weight_scale || !q_gain || !k_gain) return fail(FRY_ERROR_SHAPE, "fry_int8_linear_qk_norm needs both scales and both gains");
     if (M == 0) return check(cudaSuccess, "");
@@ -366,7 +369,7 @@ int fry_int8_linear_qk_norm(const int8_t* x, const float* x_scale, const int8_t*
 int fry_template_attention_normed(const uint16_t* projected, const uint16_t* paired_templates, uint16_t* out, int B, int heads, int kv_heads,
                                   int dq, int dv, int templates_count, void* stream) {
     if (B < 0) return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed takes B >= 0");
-    if (dq != 8 && dq != 16) return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed takes dq 8 or 16");
+    if (dq != 8 && dq != 16 && dq != 24) return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed takes dq 8, 16 or 24");
     if (!aligned16(projected) || !aligned16(out) || !aligned16(paired_templates))
         return fail(FRY_ERROR_SHAPE, "fry_template_attention_normed needs 16-byte aligned projections, templates and outputs");
     std::string detail;

@@ -157,34 +157,34 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
         if constexpr (NORMED) {  // zero past dq and past the 70th key, as loaded
 #pragma unroll
             for (int part = 0; part < kKeyParts; ++part) *reinterpret_cast<uint4*>(keys + (kv * kAttnKeys + key) * KROW + part * 8) = raw[part];
-            return;
-        }
-        float k[DQP];
+        } else {
+            float k[DQP];
 #pragma unroll
-        for (int part = 0; part < kKeyParts; ++part) {
-            const uint32_t words[4] = {raw[part].x, raw[part].y, raw[part].z, raw[part].w};
+            for (int part = 0; part < kKeyParts; ++part) {
+                const uint32_t words[4] = {raw[part].x, raw[part].y, raw[part].z, raw[part].w};
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                k[part * 8 + 2 * w] = low_half(words[w]);
-                k[part * 8 + 2 * w + 1] = high_half(words[w]);
+                for (int w = 0; w < 4; ++w) {
+                    k[part * 8 + 2 * w] = low_half(words[w]);
+                    k[part * 8 + 2 * w + 1] = high_half(words[w]);
+                }
             }
-        }
-        float squares = 0.0f;
+            float squares = 0.0f;
 #pragma unroll
-        for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
-        const float inverse = rsqrtf(__fadd_rn(mean_of(squares), eps));
-        uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
+            for (int i = 0; i < DQP; ++i) squares = __fmaf_rn(k[i], k[i], squares);
+            const float inverse = rsqrtf(__fadd_rn(mean_of(squares), eps));
+            uint16_t* row = keys + (kv * kAttnKeys + key) * KROW;
 #pragma unroll
-        for (int part = 0; part < kKeyParts; ++part) {
-            uint32_t words[4];
+            for (int part = 0; part < kKeyParts; ++part) {
+                uint32_t words[4];
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const int i = part * 8 + 2 * w;
-                const float g0 = i < dq ? h2f_exact(k_gain[i]) : 0.0f, g1 = i + 1 < dq ? h2f_exact(k_gain[i + 1]) : 0.0f;
-                words[w] = key < kAttnTokens ? pack_half2(__fmul_rn(__fmul_rn(k[i], inverse), g0), __fmul_rn(__fmul_rn(k[i + 1], inverse), g1))
-                                             : 0u;
+                for (int w = 0; w < 4; ++w) {
+                    const int i = part * 8 + 2 * w;
+                    const float g0 = i < dq ? h2f_exact(k_gain[i]) : 0.0f, g1 = i + 1 < dq ? h2f_exact(k_gain[i + 1]) : 0.0f;
+                    words[w] = key < kAttnTokens ? pack_half2(__fmul_rn(__fmul_rn(k[i], inverse), g0), __fmul_rn(__fmul_rn(k[i + 1], inverse), g1))
+                                                 : 0u;
+                }
+                *reinterpret_cast<uint4*>(row + part * 8) = make_uint4(words[0], words[1], words[2], words[3]);
             }
-            *reinterpret_cast<uint4*>(row + part * 8) = make_uint4(words[0], words[1], words[2], words[3]);
         }
     };
     const int key_items = kv_here * kAttnKeys;
@@ -208,16 +208,18 @@ __global__ void __launch_bounds__(kMaxHeadsPerCta * 32, 2)
     const int head = first_head + warp;
     const uint16_t* kv_keys = keys + (warp / group) * kAttnKeys * KROW;
     const uint16_t* kv_values = values + (warp / group) * kAttnKeys * kValueRow;
-    float qg[KS][2][2];
+    float qg[KS][2][2] = {};  // the query gains (NORMED takes none: q_gain may be null)
+    if constexpr (!NORMED) {
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks)
+        for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
-        for (int half = 0; half < 2; ++half)
+            for (int half = 0; half < 2; ++half)
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int col = ks * 16 + half * 8 + 2 * t + e;
-                qg[ks][half][e] = col < dq ? h2f_exact(q_gain[col]) : 0.0f;
-            }
+                for (int e = 0; e < 2; ++e) {
+                    const int col = ks * 16 + half * 8 + 2 * t + e;
+                    qg[ks][half][e] = col < dq ? h2f_exact(q_gain[col]) : 0.0f;
+                }
+    }
     uint32_t raw_q[KS][2][2];
     load_queries<KS>(raw_q, board, phase_begin * kSlab, width, head, dq, g, t);
     cp_async_wait<0>();  // this thread's value copies have landed; the barrier makes everyone's visible
@@ -406,8 +408,8 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
     const int dqp = dq <= 16 ? 16 : 32;
     const size_t bytes = (static_cast<size_t>(kv_per_cta) * kAttnKeys * (dqp + 8) + static_cast<size_t>(kv_per_cta) * kAttnKeys * kValueRow +
                           static_cast<size_t>(per_cta) * kBiasHead) * sizeof(uint16_t);
-    if (qk_normed && dqp != 16) {
-        if (error) *error = "template attention takes normalised queries and keys for dq up to 16 only";
+    if (qk_normed && dq != 8 && dq != 16 && dq != 24) {
+        if (error) *error = "template attention takes normalised queries and keys for dq 8, 16 or 24 only";
         return cudaErrorInvalidValue;
     }
     auto run = [&](auto kernel) {
@@ -416,7 +418,7 @@ cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired
         return launch_dependent(kernel, grid, dim3(per_cta * 32), bytes, stream, projected, paired, q_gain, k_gain, out, heads, kv_heads, dq, eps,
                                 scale);
     };
-    if (qk_normed) return run(attention_kernel<16, true>);
+    if (qk_normed) return dqp == 16 ? run(attention_kernel<16, true>) : run(attention_kernel<32, true>);
     return dqp == 16 ? run(attention_kernel<16, false>) : run(attention_kernel<32, false>);
 }
 

@@ -233,22 +233,106 @@ FRY_DEVICE void normalize_qk_heads(const GemmArgs& p, bool key, const float* gai
     for (int i = 0; i < 8; ++i) result[i] = pack_half2_rn(y[2 * i], y[2 * i + 1]);
 }
 
-// gains: the chunk's 16 column gains in shared memory (staged with the tile's column operands)
-FRY_DEVICE void normalize_qk(const GemmArgs& p, int column, const float* gains, uint32_t (&result)[8]) {
+// 1 / sqrt(mean(h^2) + eps) of one 24-wide head's fp16 values h, in the attention kernel's order: a key's squares in
+// column order; a query's as four partial sums (a quad lane's columns 2t, 2t + 1, 8 + 2t, 9 + 2t, 16 + 2t, 17 + 2t)
+// added as (s0 + s1) + (s2 + s3); the mean by division, as the attention takes it for a dq that is not a power of two.
+FRY_DEVICE float qk24_inverse(const float (&h)[24], bool key, float eps) {
+    float squares = 0.0f;
+    if (key) {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) squares = __fmaf_rn(h[i], h[i], squares);
+    } else {
+        float s[4];
+#pragma unroll
+        for (int lane = 0; lane < 4; ++lane) {
+            s[lane] = 0.0f;
+#pragma unroll
+            for (int base = 0; base < 24; base += 8)
+                s[lane] = __fmaf_rn(h[base + 2 * lane + 1], h[base + 2 * lane + 1], __fmaf_rn(h[base + 2 * lane], h[base + 2 * lane], s[lane]));
+        }
+        squares = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
+    }
+    return rsqrtf(__fadd_rn(__fdiv_rn(squares, 24.0f), eps));
+}
+
+// kEpiBiasQkNorm at dq 24: a head's 24 columns span this chunk and the one before or after it. The query and key
+// blocks start on 48-column boundaries, as do the 192-column tiles, so `phase` (the chunk's column mod 48) places the
+// heads: 0, one head of this chunk's 16 and the next chunk's first 8; 16, the end of one (the chunk before's 16, this
+// chunk's first 8) and the start of the next (this chunk's last 8, the next chunk's 16); 32, the end of one (the chunk
+// before's last 8, this chunk's 16). near[0] and near[1] hold the chunks before and after as fp16 pairs, computed from
+// the accumulator as this chunk's are, so every head is normalised from the values the attention would read.
+FRY_DEVICE void normalize_qk24(const GemmArgs& p, bool key, int phase, const float* gains, const uint32_t (&near)[2][8], uint32_t (&result)[8]) {
+    float x[16], before[16], after[16], h[24], inverse[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        x[2 * i] = h2f_exact(static_cast<uint16_t>(result[i] & 0xffff)), x[2 * i + 1] = h2f_exact(static_cast<uint16_t>(result[i] >> 16));
+        before[2 * i] = h2f_exact(static_cast<uint16_t>(near[0][i] & 0xffff)), before[2 * i + 1] = h2f_exact(static_cast<uint16_t>(near[0][i] >> 16));
+        after[2 * i] = h2f_exact(static_cast<uint16_t>(near[1][i] & 0xffff)), after[2 * i + 1] = h2f_exact(static_cast<uint16_t>(near[1][i] >> 16));
+    }
+    if (phase == 0) {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) h[i] = i < 16 ? x[i] : after[i - 16];
+        const float one = qk24_inverse(h, key, p.norm_eps);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) inverse[i] = one;
+    } else if (phase == 16) {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) h[i] = i < 16 ? before[i] : x[i - 16];
+        const float first = qk24_inverse(h, key, p.norm_eps);
+#pragma unroll
+        for (int i = 0; i < 24; ++i) h[i] = i < 8 ? x[8 + i] : after[i - 8];
+        const float second = qk24_inverse(h, key, p.norm_eps);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) inverse[i] = i < 8 ? first : second;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) h[i] = i < 8 ? before[8 + i] : x[i - 8];
+        const float one = qk24_inverse(h, key, p.norm_eps);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) inverse[i] = one;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        result[i] = pack_half2_rn(__fmul_rn(__fmul_rn(x[2 * i], inverse[2 * i]), gains[2 * i]),
+                                  __fmul_rn(__fmul_rn(x[2 * i + 1], inverse[2 * i + 1]), gains[2 * i + 1]));
+}
+
+// The bias epilogue's fp16 outputs of one row's 16 columns as pairs, by epilogue16's arithmetic for them: the q/k norm
+// at dq 24 reads a head's columns in the chunks beside its own.
+FRY_DEVICE void biased_pairs(float xs, const uint32_t (&acc)[16], const float* scale, const float* second, uint32_t (&pairs)[8]) {
+    const uint64_t xs2 = pair2(xs, xs);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 a = reinterpret_cast<const float4*>(scale)[q];
+        const float4 b = reinterpret_cast<const float4*>(second)[q];
+        const float2 low = lanes(fma2(mul2(pair2(static_cast<float>(static_cast<int32_t>(acc[4 * q])), static_cast<float>(static_cast<int32_t>(acc[4 * q + 1]))), xs2),
+                                      pair2(a.x, a.y), pair2(b.x, b.y)));
+        const float2 high = lanes(fma2(mul2(pair2(static_cast<float>(static_cast<int32_t>(acc[4 * q + 2])), static_cast<float>(static_cast<int32_t>(acc[4 * q + 3]))), xs2),
+                                       pair2(a.z, a.w), pair2(b.z, b.w)));
+        pairs[2 * q] = pack_half2_rn(low.x, low.y);
+        pairs[2 * q + 1] = pack_half2_rn(high.x, high.y);
+    }
+}
+
+// gains: the chunk's 16 column gains in shared memory (staged with the tile's column operands); near: at dq 24, the
+// chunks before and after (normalize_qk24)
+FRY_DEVICE void normalize_qk(const GemmArgs& p, int column, const float* gains, const uint32_t (&near)[2][8], uint32_t (&result)[8]) {
     if (column >= p.qk_keys) return;
     const bool key = column >= p.qk_queries;
     if (p.qk_dq == 8) normalize_qk_heads<8>(p, key, gains, result);
-    else normalize_qk_heads<16>(p, key, gains, result);
+    else if (p.qk_dq == 16) normalize_qk_heads<16>(p, key, gains, result);
+    else normalize_qk24(p, key, column % 48, gains, near, result);
 }
 
 // Applies the epilogue to one row's 16 consecutive columns. acc (and up, gated) hold the raw TMEM words, xs the row's
 // activation scale, rs and is the next block's input-mix scales, scale and second the chunk's column operands in shared
 // memory. Staged epilogues read the row's residual (and original) from its staged chunk and write the fp16 results over
 // it (and into result, as fp16 pairs); int32 and fp32 epilogues store [n, n + valid) of row index `row` directly.
+// gains and near: the q/k norm's column gains and, at dq 24, the fp16 outputs of the chunks beside this one.
 template <int EPI>
 FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, const uint32_t (&acc)[16], const uint32_t (&up)[16],
                            const float* scale, const float* second, const StagedChunk& staged, const StagedChunk& original, size_t row,
-                           int valid, int column, const float* gains, uint32_t (&result)[8]) {
+                           int valid, int column, const float* gains, const uint32_t (&near)[2][8], uint32_t (&result)[8]) {
     if constexpr (EPI == kEpiInt32) {
         int32_t* out = static_cast<int32_t*>(p.out) + row;
 #pragma unroll
@@ -342,7 +426,7 @@ FRY_DEVICE void epilogue16(const GemmArgs& p, float xs, float rs, float is, cons
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             result[i] = EPI == kEpiScaleBf16 ? pack_bf162_rn(values[2 * i], values[2 * i + 1]) : pack_half2_rn(values[2 * i], values[2 * i + 1]);
-        if constexpr (EPI == kEpiBiasQkNorm) normalize_qk(p, column, gains, result);
+        if constexpr (EPI == kEpiBiasQkNorm) normalize_qk(p, column, gains, near, result);
         *staged.at(0) = make_uint4(result[0], result[1], result[2], result[3]);
         *staged.at(1) = make_uint4(result[4], result[5], result[6], result[7]);
     }
@@ -785,6 +869,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int k = 0; k < S::kChunksPerSub; ++k) {
                         const int c = sub * SUB + part * kChunkCols + k * kChunkCols * kChunkParts;
                         if (c >= (sub + 1) * SUB || n0 + c >= N) break;  // uniform
+                        // the q/k norm at dq 24: the chunks before and after this one, where its heads reach into them (within
+                        // the tile: its columns and the heads' blocks start on 48-column boundaries)
+                        uint32_t near[2][8] = {};
+                        if constexpr (EPI == kEpiBiasQkNorm && BN % 48 == 0) {
+                            if (args.qk_dq == 24 && n0 + c < args.qk_keys) {  // uniform
+                                const int phase = (n0 + c) % 48;
+                                uint32_t side[16];
+                                if (phase != 0) {
+                                    tmem_load16(lane_base + c - kChunkCols, side);
+                                    tmem_load_wait();
+                                    biased_pairs(xs, side, columns + c - kChunkCols, columns + S::kSecond + c - kChunkCols, near[0]);
+                                }
+                                if (phase != 32) {
+                                    tmem_load16(lane_base + c + kChunkCols, side);
+                                    tmem_load_wait();
+                                    biased_pairs(xs, side, columns + c + kChunkCols, columns + S::kSecond + c + kChunkCols, near[1]);
+                                }
+                            }
+                        }
                         uint32_t acc[16], up[16];
                         tmem_load16(lane_base + c, acc);
                         if constexpr (GATED) tmem_load16(lane_base + BN + c, up);
@@ -797,7 +900,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         uint32_t result[8];
                         if (S::kStaged || m < M)
                             epilogue16<EPI>(args, xs, rs, is, acc, up, columns + c, columns + S::kSecond + c, staged, original,
-                                            static_cast<size_t>(m) * N + n0 + c, valid, n0 + c, columns + 2 * BN + c, result);
+                                            static_cast<size_t>(m) * N + n0 + c, valid, n0 + c, columns + 2 * BN + c, near, result);
                         if constexpr (EPI == kEpiLinearNorm) {
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
@@ -1016,17 +1119,24 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 256) return launch<0, 256, false, kEpiBias, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBias, 64>(a, b, args, M, N, K, stream, error);
-            case kEpiBiasQkNorm:
-                if ((args.qk_dq != 8 && args.qk_dq != 16) || args.qk_queries % 16 || args.qk_keys % 16 || args.qk_keys > N || !args.q_gain ||
-                    !args.k_gain) {
-                    if (error) *error = "the q/k norm epilogue takes heads 8 or 16 wide in blocks starting on 16-column boundaries, and both gains";
+            case kEpiBiasQkNorm: {
+                const bool dq24 = args.qk_dq == 24;
+                const int boundary = dq24 ? 48 : 16;
+                if ((args.qk_dq != 8 && args.qk_dq != 16 && !dq24) || args.qk_queries % boundary || args.qk_keys % boundary ||
+                    args.qk_keys > N || !args.q_gain || !args.k_gain) {
+                    if (error)
+                        *error = "the q/k norm epilogue takes heads 8 or 16 wide in blocks starting on 16-column boundaries, or 24 wide "
+                                 "on 48-column boundaries, and both gains";
                     return cudaErrorInvalidValue;
                 }
+                // dq 24: 192-column tiles (8 heads each), so no head leaves its tile, as CTA pairs at every batch
+                if (dq24) return launch<0, 192, false, kEpiBiasQkNorm, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 256 && (N + 191) / 192 * 192 < (N + 255) / 256 * 256)
                     return launch<0, 192, false, kEpiBiasQkNorm, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 256) return launch<0, 256, false, kEpiBiasQkNorm, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiBiasQkNorm, 64>(a, b, args, M, N, K, stream, error);
+            }
             case kEpiGated:
                 // as pairs, 128-column sub-tiles (two chunks a warp between barriers): 23.8 -> 22.5 us a launch at 256 boards
                 if (width == 256) return launch<0, 128, true, kEpiGated, 128, 0, true>(a, b, args, M, N, K, stream, error);

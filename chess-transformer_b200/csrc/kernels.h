@@ -48,7 +48,7 @@ struct GemmArgs {
     // kEpiLinearNorm: the int8 rows [M, N] and their scales [M] of norm_quant(out) with norm_gain and norm_eps
     int8_t* norm_q = nullptr;
     float* norm_scale = nullptr;
-    // kEpiBiasQkNorm: columns [0, qk_queries) are query heads and [qk_queries, qk_keys) key heads, qk_dq (8 or 16) wide,
+    // kEpiBiasQkNorm: columns [0, qk_queries) are query heads and [qk_queries, qk_keys) key heads, qk_dq (8, 16 or 24) wide,
     // each RMS-normalised (eps norm_eps) and scaled by q_gain / k_gain [qk_dq] after the fp16 rounding
     const uint16_t* q_gain = nullptr;
     const uint16_t* k_gain = nullptr;
@@ -82,7 +82,8 @@ cudaError_t square_feature_rows(const int64_t* boards, int32_t* rows, int B, cud
 // Template attention (attention.cu).
 // paired [64][64][8] fp16: templates[t][i][j] at paired[i][j][t]
 cudaError_t pair_templates(const uint16_t* templates, uint16_t* paired, cudaStream_t stream);
-// qk_normed: the projected rows' query and key columns are already normalised with their gains (kEpiBiasQkNorm; dq <= 16)
+// qk_normed: the projected rows' query and key columns are already normalised with their gains (kEpiBiasQkNorm; dq 8,
+// 16 or 24)
 cudaError_t template_attention(const uint16_t* projected, const uint16_t* paired, const uint16_t* q_gain, const uint16_t* k_gain,
                                uint16_t* out, int B, int heads, int kv_heads, int dq, int dv, int templates_count, float eps,
                                cudaStream_t stream, std::string* error, bool qk_normed = false);

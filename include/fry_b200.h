@@ -124,13 +124,14 @@ int fry_template_attention(const uint16_t* projected, const uint16_t* paired_tem
  * out[M, N] fp16 is fry_int8_linear's output with columns [0, heads*dq) (queries) and [heads*dq, (heads+kv_heads)*dq)
  * (keys) replaced, head by head, by fp16((x * inverse) * gain), inverse = rsqrt(mean(x^2) + eps), summed in the order
  * fry_template_attention sums them, so fry_template_attention_normed on it equals fry_template_attention on the plain
- * projection bit for bit. dq 8 or 16, the query and key blocks on 16-column boundaries. */
+ * projection bit for bit. dq 8 or 16 with the query and key blocks on 16-column boundaries, or dq 24 with them on
+ * 48-column boundaries (heads * 24 and (heads + kv_heads) * 24 multiples of 48). */
 int fry_int8_linear_qk_norm(const int8_t* x, const float* x_scale, const int8_t* weight, const float* weight_scale, const uint16_t* bias,
                             const uint16_t* q_gain, const uint16_t* k_gain, float eps, uint16_t* out, int M, int N, int K, int heads,
                             int kv_heads, int dq, void* stream);
 
 /* fry_template_attention on a projection whose query and key columns fry_int8_linear_qk_norm has normalised: the
- * queries and keys are used as they are. dq 8 or 16; otherwise as fry_template_attention. */
+ * queries and keys are used as they are. dq 8, 16 or 24; otherwise as fry_template_attention. */
 int fry_template_attention_normed(const uint16_t* projected, const uint16_t* paired_templates, uint16_t* out, int B, int heads, int kv_heads,
                                   int dq, int dv, int templates_count, void* stream);
 

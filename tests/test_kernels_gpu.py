@@ -350,10 +350,10 @@ def test_heads_are_the_oracles(boards):
     assert torch.allclose(found[:, -1], expected[:, -1], rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("dq", [8, 16])
+@pytest.mark.parametrize("dq", [8, 16, 24])
 @pytest.mark.parametrize("boards", [1, 5, 64, 256])
 def test_the_q_k_norm_in_the_projection_epilogue_gives_the_attentions_own_bits(dq, boards):
-    # the forward's fused pair for dq 8 and 16 (fry_int8_linear_qk_norm, then fry_template_attention_normed) against the
+    # the forward's fused pair (fry_int8_linear_qk_norm, then fry_template_attention_normed) against the
     # plain pair (fry_int8_linear, then fry_template_attention, which normalises queries and keys itself), at Fry's
     # geometry: the value and template-mix columns and the attention's output are the same bits
     import ctypes
@@ -378,6 +378,11 @@ def test_the_q_k_norm_in_the_projection_epilogue_gives_the_attentions_own_bits(d
     qk = (heads + kv_heads) * dq
     assert torch.equal(fused[:, qk:], plain[:, qk:])
     assert not torch.equal(fused[:, :qk], plain[:, :qk])
+    # each query and key head RMS-normalised with its gain, against fp32 to within fp16 rounding
+    for first, count, gain in ((0, heads, q_gain), (heads * dq, kv_heads, k_gain)):
+        rows = plain[:, first:first + count * dq].float().reshape(M, count, dq)
+        normed = rows * torch.rsqrt(rows.square().mean(-1, keepdim=True) + 1e-5) * gain.float()
+        assert torch.allclose(fused[:, first:first + count * dq].float().reshape(M, count, dq), normed, rtol=2e-3, atol=1e-3)
     expected = torch.empty(boards, 70, heads * dv, dtype=torch.float16, device="cuda")
     found = torch.empty_like(expected)
     lib.fry_template_attention(pointer(plain), pointer(paired), pointer(q_gain), pointer(k_gain), pointer(expected), boards, heads, kv_heads,

@@ -55,12 +55,13 @@ def test_shapes_are_refused_on_the_host_before_any_launch(lib):
     with pytest.raises(FryError, match="template attention"):
         lib.fry_template_attention(None, None, None, None, None, 1, 24, 12, 8, 64, 8, 1e-5, None)
     assert "template attention" in lib.fry_last_error().decode()
-    # the fused projection and attention take query/key heads 8 or 16 wide, their blocks on 16-column boundaries
-    for dq, heads in ((24, 24), (8, 3), (32, 24)):
+    # the fused projection and attention take query/key heads 8 or 16 wide, their blocks on 16-column boundaries, or 24
+    # wide on 48-column boundaries
+    for dq, heads in ((24, 23), (8, 3), (32, 24), (12, 24)):
         with pytest.raises(FryError, match="8 or 16 wide"):
             lib.fry_int8_linear_qk_norm(None, None, None, None, None, None, None, 1e-5, None, 70, 1440, 768, heads, 12, dq, None)
-    with pytest.raises(FryError, match="dq 8 or 16"):
-        lib.fry_template_attention_normed(None, None, None, 1, 24, 12, 24, 32, 8, None)
+    with pytest.raises(FryError, match="dq 8, 16 or 24"):
+        lib.fry_template_attention_normed(None, None, None, 1, 24, 12, 32, 32, 8, None)
     for limit in (0, 999, 60_000_000_001):
         with pytest.raises(FryError, match="1 us to 60 s"):
             lib.fry_set_wait_limit_ns(limit)
