@@ -1166,7 +1166,9 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 if (width == 256) return launch<1, 256, false, kEpiLinearF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<1, 128, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
-            case kEpiLinearF32: return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
+            case kEpiLinearF32:
+                if (width == 256) return launch<1, 256, false, kEpiLinearF32, 256, 0, true>(a, b, args, M, N, K, stream, error);
+                return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             case kEpiGatedF16:
                 if (width == 256) return launch<1, 128, true, kEpiGatedF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
                 if (width >= 128 || tiles(128) >= multiprocessors) return launch<1, 128, true, kEpiGatedF16, 64>(a, b, args, M, N, K, stream, error);
