@@ -1144,6 +1144,8 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 return launch<0, 64, true, kEpiGated>(a, b, args, M, N, K, stream, error);
             case kEpiResidual:
                 if (width == 256) return launch<0, 256, false, kEpiResidual, 64, 0, true>(a, b, args, M, N, K, stream, error);
+                // one round of 192-column tiles rather than two of 128, as the mixing down
+                if (width == 128 && tiles(192) <= multiprocessors) return launch<0, 192, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
                 if (width == 128) return launch<0, 128, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
                 return launch<0, 64, false, kEpiResidual, 64>(a, b, args, M, N, K, stream, error);
             case kEpiMix:
@@ -1171,6 +1173,8 @@ cudaError_t gemm(int kind, int epilogue, const void* a, const void* b, const Gem
                 return launch<1, 64, false, kEpiLinearF16, 64>(a, b, args, M, N, K, stream, error);
             case kEpiLinearF32:
                 if (width == 256) return launch<1, 256, false, kEpiLinearF32, 256, 0, true>(a, b, args, M, N, K, stream, error);
+                // one round of 192-column tiles rather than two of 128 (64 boards: 19.9 -> 17.2 us a launch)
+                if (width == 128 && tiles(192) <= multiprocessors) return launch<1, 192, false, kEpiLinearF32, 192>(a, b, args, M, N, K, stream, error);
                 return launch<1, 128, false, kEpiLinearF32>(a, b, args, M, N, K, stream, error);
             case kEpiGatedF16:
                 if (width == 256) return launch<1, 128, true, kEpiGatedF16, 64, 0, true>(a, b, args, M, N, K, stream, error);
